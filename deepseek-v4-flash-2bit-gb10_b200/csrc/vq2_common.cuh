@@ -1,0 +1,116 @@
+// Shared device helpers for the vq2 sm_100a kernels: bounded mbarrier waits, 1-D bulk async
+// copies (TMA engine), PDL control, warp reductions, the 64-point Walsh-Hadamard transform and
+// the in-CTA (token, slot) -> expert grouping used by the decode kernels.
+#pragma once
+#include <cuda_runtime.h>
+#include <cuda_fp16.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+#include "../../include/vq2_b200.h"
+
+#define VQ2_WAIT_LIMIT (1u << 22)   // try_wait polls before a wait gives up (well under a second)
+
+namespace vq2 {
+
+// Error word set by a wait that gave up; read by vq2_device_status(). The library is built as
+// one translation unit (vq2_lib.cu), so this is its only definition.
+__device__ int g_status = 0;
+
+__device__ __forceinline__ void set_status(int code) { atomicCAS(&g_status, 0, code); }
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.shared::cta.b64 st, [%0];\n}" ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("{\n .reg .b64 st;\n mbarrier.arrive.expect_tx.shared::cta.b64 st, [%0], %1;\n}"
+               ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait: returns false (and records VQ2_ERR_TIMEOUT) if the phase never completes.
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < VQ2_WAIT_LIMIT; ++i)
+    if (mbar_try_wait(bar, parity)) return true;
+  set_status(VQ2_ERR_TIMEOUT);
+  return false;
+}
+
+// ---------------------------------------------------------------- bulk async copy (1-D TMA)
+// global -> shared, completion counted on `bar` in bytes. src, dst 16-B aligned, bytes % 16 == 0.
+__device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+               ::"r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+// ---------------------------------------------------------------- programmatic dependent launch
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ---------------------------------------------------------------- warp helpers
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+// In-register 64-point Walsh-Hadamard transform in natural (Sylvester) order, unnormalised:
+// y_j = sum_i x_i (-1)^popcount(i&j), i.e. x @ (8 H64) with H64 the reference's normalised
+// Sylvester matrix (vq2_vllm/kernels/vq2_kernel.py:18-22).
+__device__ __forceinline__ void fwht64(float* v) {
+#pragma unroll
+  for (int len = 1; len < 64; len <<= 1) {
+#pragma unroll
+    for (int i = 0; i < 64; ++i) {
+      if ((i & len) == 0) {
+        float a = v[i], b = v[i + len];
+        v[i] = a + b;
+        v[i + len] = a - b;
+      }
+    }
+  }
+}
+
+// Power-of-two scale that maps a max magnitude `amax` to at most 2^14, so fp16 storage of
+// activations cannot overflow (returned as (scale, inverse)). amax == 0 -> 1.
+__device__ __forceinline__ float2 f16_range_scale(float amax) {
+  if (!(amax > 0.f)) return make_float2(1.f, 1.f);
+  int ex;
+  frexpf(amax, &ex);                 // amax in [2^(ex-1), 2^ex)
+  int s = 14 - ex;                   // amax * 2^s < 2^14
+  s = max(-60, min(60, s));
+  return make_float2(ldexpf(1.f, s), ldexpf(1.f, -s));
+}
+
+__device__ __forceinline__ int load_id(const void* ids, int ids_dtype, int m) {
+  return ids_dtype == VQ2_ID_I64 ? (int)((const long long*)ids)[m] : ((const int*)ids)[m];
+}
+
+__device__ __forceinline__ float load_act(const void* x, int dt, size_t i) {
+  if (dt == VQ2_DT_BF16) return __bfloat162float(((const __nv_bfloat16*)x)[i]);
+  if (dt == VQ2_DT_F16) return __half2float(((const __half*)x)[i]);
+  return ((const float*)x)[i];
+}
+
+}  // namespace vq2

@@ -1,0 +1,116 @@
+"""ctypes binding of libvq2_b200.so (the C ABI declared in include/vq2_b200.h).
+
+The library is loaded from the package tree (built in-tree by ``build_lib.py``). There is no
+fallback: if the library is missing every kernel entry raises, naming the build command.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(os.path.dirname(_HERE), "libvq2_b200.so")
+
+DT = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
+ID = {torch.int32: 0, torch.int64: 1}
+PREC = {"fp8": 0, "bf16": 1}
+DECODE_MAX_PAIRS = 512
+
+
+class Vq2MoeArgs(ctypes.Structure):
+    _fields_ = [("N", ctypes.c_int), ("H", ctypes.c_int), ("I", ctypes.c_int), ("E", ctypes.c_int),
+                ("topk", ctypes.c_int), ("x_dtype", ctypes.c_int), ("ids_dtype", ctypes.c_int),
+                ("expert_base", ctypes.c_int),
+                ("x", ctypes.c_void_p), ("topk_ids", ctypes.c_void_p), ("topk_w", ctypes.c_void_p),
+                ("w13_cb", ctypes.c_void_p), ("w13_lo", ctypes.c_void_p), ("w13_hi", ctypes.c_void_p),
+                ("w13_sc", ctypes.c_void_p),
+                ("w2_cb", ctypes.c_void_p), ("w2_lo", ctypes.c_void_p), ("w2_hi", ctypes.c_void_p),
+                ("w2_sc", ctypes.c_void_p), ("out", ctypes.c_void_p)]
+
+
+_SIGS = {
+    "vq2_decode_workspace_size": (ctypes.c_size_t, [ctypes.c_int] * 4),
+    "vq2_decode": (ctypes.c_int, [ctypes.POINTER(Vq2MoeArgs), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "vq2_prefill_workspace_size": (ctypes.c_size_t, [ctypes.c_int] * 6),
+    "vq2_prefill": (ctypes.c_int, [ctypes.POINTER(Vq2MoeArgs), ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,
+                                   ctypes.c_void_p]),
+    "vq2_align_workspace_size": (ctypes.c_size_t, [ctypes.c_int] * 3),
+    "vq2_align": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                 ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                 ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "vq2_quant_fp8_rows": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p,
+                                          ctypes.c_void_p, ctypes.c_void_p]),
+    "vq2_hadamard_rows": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                         ctypes.c_long, ctypes.c_int, ctypes.c_void_p]),
+    "vq2_device_status": (ctypes.c_int, [ctypes.c_int]),
+    "vq2_strerror": (ctypes.c_char_p, [ctypes.c_int]),
+    "vq2_version": (ctypes.c_int, []),
+}
+
+_LIB = None
+
+
+def lib():
+    """Load (once) and return the C-ABI library; raises if it is not built."""
+    global _LIB
+    if _LIB is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(f"vq2: {LIB_PATH} is not built; run python build_lib.py "
+                               "(or __graft_entry__.build()) — there is no fallback path")
+        L = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in _SIGS.items():
+            f = getattr(L, name, None)
+            if f is None:
+                continue
+            f.restype, f.argtypes = res, args
+        _LIB = L
+    return _LIB
+
+
+def check(code: int, what: str = "vq2"):
+    if code != 0:
+        msg = lib().vq2_strerror(code).decode()
+        raise RuntimeError(f"{what}: {msg} (code {code})")
+
+
+def stream_ptr(device=None) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t):
+    return None if t is None else t.data_ptr()
+
+
+def require_cuda(*ts):
+    for t in ts:
+        if not t.is_cuda:
+            raise RuntimeError("vq2: all tensors must be CUDA tensors (no CPU path)")
+
+
+_WS = {}
+
+
+def workspace(nbytes: int, device) -> torch.Tensor:
+    """Cached per-(device, stream) byte workspace, grown on demand (graph-safe once sized)."""
+    key = (str(device), torch.cuda.current_stream(device).cuda_stream)
+    buf = _WS.get(key)
+    if buf is None or buf.numel() < nbytes:
+        buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
+        _WS[key] = buf
+    return buf
+
+
+def moe_args(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, out, expert_base=0, E=None):
+    N, H = x.shape
+    a = Vq2MoeArgs()
+    a.N, a.H, a.I = N, H, lgu.shape[1] // 2
+    a.E = lgu.shape[0] if E is None else E
+    a.topk = topk_ids.shape[1]
+    a.x_dtype, a.ids_dtype, a.expert_base = DT[x.dtype], ID[topk_ids.dtype], expert_base
+    a.x, a.topk_ids, a.topk_w = ptr(x), ptr(topk_ids), ptr(topk_w)
+    a.w13_cb, a.w13_lo, a.w13_hi, a.w13_sc = ptr(Cgu), ptr(lgu), ptr(hgu), ptr(sgu)
+    a.w2_cb, a.w2_lo, a.w2_hi, a.w2_sc = ptr(Cd), ptr(ld), ptr(hd), ptr(sdn)
+    a.out = ptr(out)
+    return a

@@ -1,0 +1,86 @@
+"""vq2 decode entry points on the B200 C-ABI extension.
+
+Mirrors the reference module ``vq2_vllm/kernels/vq2_kernel.py`` for the routed-expert path: same
+function names, argument order and meaning, same return types. The arithmetic runs in
+libvq2_b200.so (sm_100a); there is no Triton and no CPU path.
+"""
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+
+DEV = "cuda"
+
+
+def _hadamard(n):
+    """Sylvester Hadamard / sqrt(n) (reference vq2_kernel.py:18-22). Host helper for tests and
+    weight tooling; the kernels apply the transform in-register."""
+    h = torch.ones(1, 1)
+    while h.shape[0] < n:
+        h = torch.cat([torch.cat([h, h], 1), torch.cat([h, -h], 1)], 0)
+    return h / (n ** 0.5)
+
+
+def _pack10(idx):
+    """10-bit index -> (lo u8, hi u8 with four 2-bit fields per byte) (reference vq2_kernel.py:491-498)."""
+    from ..synth import pack10
+    return pack10(idx)
+
+
+def had_act_batch(X, group=64):
+    """Hadamard per 64-group over the last dim: X[..., in] -> [..., in_pad], same dtype
+    (reference vq2_kernel.py:188-195). Runs the extension's shuffle-FWHT kernel."""
+    if group != 64:
+        raise ValueError("vq2: only group=64 is supported")
+    _lib.require_cuda(X)
+    *b, n = X.shape
+    pad = (-n) % group
+    if pad:
+        X = torch.cat([X, torch.zeros(*b, pad, device=X.device, dtype=X.dtype)], -1)
+    X = X.contiguous()
+    Y = torch.empty_like(X)
+    rows = X.numel() // X.shape[-1]
+    _lib.check(_lib.lib().vq2_hadamard_rows(X.data_ptr(), _lib.DT[X.dtype], Y.data_ptr(), _lib.DT[Y.dtype],
+                                            rows, X.shape[-1], _lib.stream_ptr(X.device)), "had_act_batch")
+    return Y
+
+
+def had_act(x, group=64):
+    """x [in] -> x' [in_pad] (reference vq2_kernel.py:75-82)."""
+    return had_act_batch(x[None], group)[0]
+
+
+def _prep(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn):
+    _lib.require_cuda(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn)
+    if x.dtype not in _lib.DT:
+        x = x.to(torch.bfloat16)
+    if topk_ids.dtype not in _lib.ID:
+        topk_ids = topk_ids.to(torch.int32)
+    t = [x.contiguous(), topk_ids.contiguous(), topk_w.float().contiguous()]
+    t += [Cgu.half().contiguous(), lgu.contiguous(), hgu.contiguous(), sgu.half().contiguous(),
+          Cd.half().contiguous(), ld.contiguous(), hd.contiguous(), sdn.half().contiguous()]
+    return t
+
+
+def vq2_moe_fused_10b(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, group=64, expert_base=0):
+    """Decode MoE over 10-bit byte-plane VQ experts -> fp32 [N, H]
+    (reference vq2_kernel.py:569-594). ``expert_base`` (extension, default 0): ids are global and
+    only experts [expert_base, expert_base + E) held in these tensors are applied (expert
+    parallelism). Batches above the decode kernel's pair limit go to the grouped GEMM path."""
+    if group != 64:
+        raise ValueError("vq2: only group=64 is supported")
+    N = x.shape[0]
+    k = topk_ids.shape[1]
+    if N * k > _lib.DECODE_MAX_PAIRS:
+        from .ds4_vq2_cuda import vq2_moe_grouped_wmma
+        return vq2_moe_grouped_wmma(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, group=group,
+                                    expert_base=expert_base)
+    t = _prep(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn)
+    out = torch.empty(N, x.shape[1], device=x.device, dtype=torch.float32)
+    L = _lib.lib()
+    a = _lib.moe_args(*t, out, expert_base=expert_base)
+    nb = L.vq2_decode_workspace_size(a.N, a.topk, a.H, a.I)
+    ws = _lib.workspace(nb, x.device)
+    _lib.check(L.vq2_decode(a, ws.data_ptr(), ws.numel(), _lib.stream_ptr(x.device)), "vq2_moe_fused_10b")
+    return out

@@ -1,0 +1,104 @@
+/* vq2_b200 — C ABI of the B200 (sm_100a) vq2 routed-expert MoE path.
+ *
+ * A drop-in for the kernel layer of the vq2 vLLM plugin (iggerask/deepseek-v4-flash-2bit-gb10).
+ * Plain pointers and sizes only; every pointer is DEVICE memory unless stated; the caller owns
+ * all buffers (the library never allocates); every launch goes on the `stream` argument
+ * (a cudaStream_t passed as void*; NULL = legacy default stream). Functions return 0 on success
+ * or a VQ2_ERR_* code (see vq2_strerror); no exceptions cross the ABI and no kernel traps.
+ *
+ * Weight format (reference vq2_vllm/__init__.py:164-173), 10-bit index planes, 4-wide codebook,
+ * group-64 scales and group-64 Hadamard incoherence folded into the activation:
+ *   w13_lo [E,2I,H/4] u8   w13_hi [E,2I,H/16] u8   w13_sc [E,2I,H/64] f16   (rows 0..I-1 gate,
+ *   w2_lo  [E,H,I/4]  u8   w2_hi  [E,H,I/16]  u8   w2_sc  [E,H,I/64]  f16    rows I..2I-1 up)
+ *   w13_cb, w2_cb [1024,4] f16
+ * Index of sub-vector s of a row: lo[s] | ((hi[s>>2] >> 2*(s&3)) & 3) << 8
+ * (reference vq2_vllm/kernels/vq2_kernel.py:491-498, :534-535).
+ */
+#ifndef VQ2_B200_H
+#define VQ2_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum {
+  VQ2_OK = 0,
+  VQ2_ERR_NULL = 1,          /* a required pointer is NULL */
+  VQ2_ERR_SHAPE = 2,         /* unsupported or inconsistent dimensions */
+  VQ2_ERR_ALIGN = 3,         /* a pointer is not 16-byte aligned */
+  VQ2_ERR_DTYPE = 4,         /* unknown dtype code */
+  VQ2_ERR_WORKSPACE = 5,     /* workspace NULL or smaller than the *_workspace_size answer */
+  VQ2_ERR_TOO_MANY_PAIRS = 6,/* decode path: N*topk above VQ2_DECODE_MAX_PAIRS */
+  VQ2_ERR_CUDA = 7,          /* a CUDA runtime call failed (launch / attribute) */
+  VQ2_ERR_TIMEOUT = 8,       /* a bounded device wait gave up (reported by vq2_device_status) */
+  VQ2_ERR_NO_DEVICE = 9      /* no sm_100 device is current */
+};
+
+enum { VQ2_DT_BF16 = 0, VQ2_DT_F16 = 1, VQ2_DT_F32 = 2 };   /* activation dtypes */
+enum { VQ2_ID_I32 = 0, VQ2_ID_I64 = 1 };                      /* topk_ids dtypes  */
+enum { VQ2_PREC_FP8 = 0, VQ2_PREC_BF16 = 1 };                 /* prefill operand precision */
+
+#define VQ2_DECODE_MAX_PAIRS 512
+
+typedef struct vq2_moe_args {
+  int N;            /* tokens */
+  int H;            /* hidden size (multiple of 64, <= 4096) */
+  int I;            /* expert intermediate size (multiple of 64, <= 4096) */
+  int E;            /* routed experts held by this call (local experts under expert parallelism) */
+  int topk;         /* experts per token */
+  int x_dtype;      /* VQ2_DT_* */
+  int ids_dtype;    /* VQ2_ID_* */
+  int expert_base;  /* ids are global: local expert = id - expert_base; pairs whose local id falls
+                       outside [0,E) are skipped (expert parallelism). 0 for a single device. */
+  const void* x;         /* [N,H] */
+  const void* topk_ids;  /* [N,topk] */
+  const float* topk_w;   /* [N,topk] fp32 */
+  const uint16_t* w13_cb; const uint8_t* w13_lo; const uint8_t* w13_hi; const uint16_t* w13_sc;
+  const uint16_t* w2_cb;  const uint8_t* w2_lo;  const uint8_t* w2_hi;  const uint16_t* w2_sc;
+  float* out;            /* [N,H] fp32, fully overwritten */
+} vq2_moe_args;
+
+/* Decode MoE (small token batches). Replaces vq2_kernel.vq2_moe_fused_10b
+ * (reference vq2_vllm/kernels/vq2_kernel.py:569-594): out = sum_j w_nj * down_e(H·(silu(gate_e(Hx)) * up_e(Hx))).
+ * Two kernels chained with programmatic dependent launch; no host sync, no allocation, safe to
+ * capture in a CUDA graph. Requires N*topk <= VQ2_DECODE_MAX_PAIRS. */
+size_t vq2_decode_workspace_size(int N, int topk, int H, int I);
+int vq2_decode(const vq2_moe_args* a, void* workspace, size_t ws_bytes, void* stream);
+
+/* Prefill MoE (grouped GEMM on tcgen05 tensor cores). Replaces ds4_vq2_cuda.vq2_moe_grouped_wmma
+ * (reference vq2_vllm/kernels/ds4_vq2_cuda.py:72-111). precision = VQ2_PREC_FP8 follows the
+ * reference's fp8 e4m3 algorithm; VQ2_PREC_BF16 runs bf16 operands (fp32 accumulation). */
+size_t vq2_prefill_workspace_size(int N, int topk, int E, int H, int I, int precision);
+int vq2_prefill(const vq2_moe_args* a, int precision, void* workspace, size_t ws_bytes, void* stream);
+
+/* moe_align: stable sort of (token, slot) pairs by expert, padded to BM per expert. Replaces
+ * moe_align.moe_align / _moe_align_torch (reference vq2_vllm/kernels/moe_align.py:50-86),
+ * bit-exact with the latter. Pmax = M + min(M,E)*BM, nblk = Pmax/BM (M = N*k). Outputs:
+ * sorted_tok i32[Pmax], sorted_slot i32[Pmax], valid u8[Pmax], block_e i32[nblk]. Ids outside
+ * [0,E) are clamped, as the reference's prefill wrapper does (ds4_vq2_cuda.py:82-85). */
+size_t vq2_align_workspace_size(int N, int k, int E);
+int vq2_align(const void* topk_ids, int ids_dtype, int N, int k, int E, int BM,
+              int32_t* sorted_tok, int32_t* sorted_slot, uint8_t* valid, int32_t* block_e,
+              void* workspace, size_t ws_bytes, void* stream);
+
+/* Per-row absmax fp8 e4m3 quantisation: s = 448/max(amax,1e-6); out = e4m3(x*s); inv = 1/s.
+ * Replaces ds4_vq2_cuda.quant_fp8_rows (reference vq2_vllm/kernels/ds4_vq2_cuda.py:8-32). */
+int vq2_quant_fp8_rows(const float* x, int rows, int cols, uint8_t* out, float* inv, void* stream);
+
+/* Group-64 Hadamard of each row, X @ H per group (H Sylvester, 1/8 normalised). in/out dtype
+ * VQ2_DT_*; cols a multiple of 64. Replaces vq2_kernel.had_act_batch
+ * (reference vq2_vllm/kernels/vq2_kernel.py:188-195). */
+int vq2_hadamard_rows(const void* x, int in_dtype, void* y, int out_dtype, long rows, int cols, void* stream);
+
+/* Error word written by bounded device waits (0 = none). Synchronises the device. */
+int vq2_device_status(int reset);
+const char* vq2_strerror(int code);
+int vq2_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* VQ2_B200_H */

@@ -1,0 +1,61 @@
+"""fp32 torch restatement of the oracle's dense MoE (TEST INFRASTRUCTURE ONLY).
+
+Same maths as ``oracle.vq2_oracle.moe_ref`` (reference vq2_vllm/kernels/vq2_kernel.py:63-64
+dequant, :720-727 MoE), written with torch so the full-size (config 1) parity tests can run it on
+the GPU box. It is cross-checked against the numpy oracle on the CPU (tests/test_oracle.py).
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs may use it.
+"""
+from __future__ import annotations
+
+import torch
+
+
+def _had(n, device):
+    h = torch.ones(1, 1, dtype=torch.float64)
+    while h.shape[0] < n:
+        h = torch.cat([torch.cat([h, h], 1), torch.cat([h, -h], 1)], 0)
+    return (h / n ** 0.5).float().to(device)
+
+
+def had_rows(x):
+    *b, n = x.shape
+    return (x.float().reshape(*b, n // 64, 64) @ _had(64, x.device)).reshape(*b, n)
+
+
+def dequant_rot(cb, lo, hi, sc):
+    """recon_rot = C[id] * scale per 64-group (reference vq2_kernel.py:63); lo [R,nsub]."""
+    lo32 = lo.int()
+    s = torch.arange(lo.shape[-1], device=lo.device)
+    hb = hi.int()[..., s >> 2]
+    ids = lo32 | (((hb >> ((s & 3) * 2)) & 3) << 8)
+    w = cb.float()[ids.long()]                                   # [R, nsub, 4]
+    R, nsub = ids.shape
+    return (w.reshape(R, nsub // 16, 64) * sc.float()[..., None]).reshape(R, nsub * 4)
+
+
+def moe_ref(x, topk_ids, topk_w, layer, expert_base=0, E=None):
+    """fp32 dense MoE over the experts [expert_base, expert_base+E) held in ``layer``."""
+    x = x.float()
+    N, H = x.shape
+    E = layer["w13_lo"].shape[0] if E is None else E
+    I = layer["w13_lo"].shape[1] // 2
+    ids = topk_ids.long() - expert_base
+    out = torch.zeros(N, H, device=x.device)
+    xh = had_rows(x)
+    for e in torch.unique(ids).tolist():
+        if e < 0 or e >= E:
+            continue
+        n_idx, j_idx = torch.nonzero(ids == e, as_tuple=True)
+        wgu = dequant_rot(layer["w13_cb"], layer["w13_lo"][e], layer["w13_hi"][e], layer["w13_sc"][e])
+        wdn = dequant_rot(layer["w2_cb"], layer["w2_lo"][e], layer["w2_hi"][e], layer["w2_sc"][e])
+        g = xh[n_idx] @ wgu.T
+        a = torch.nn.functional.silu(g[:, :I]) * g[:, I:]
+        d = had_rows(a) @ wdn.T
+        out.index_add_(0, n_idx, d * topk_w.float()[n_idx, j_idx, None])
+    return out
+
+
+def rel_l2(a, b):
+    a = a.double()
+    b = b.double()
+    return ((a - b).norm() / b.norm().clamp_min(1e-30)).item()

@@ -74,3 +74,11 @@ def test_fp8_prefill_emulation_sane():
     f8 = O.moe_prefill_fp8_ref(x, z["topk_ids"], z["topk_w"], _w(layer, "w13"), _w(layer, "w2"))
     # the reference's fp8 algorithm is a few percent away from fp32 on these weights
     assert 1e-3 < O.rel_l2(f8, ref) < 0.15
+
+
+def test_torch_ref_matches_numpy_oracle():
+    from oracle import torch_ref
+    z, layer, x = load_config0()
+    tl = {k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in layer.items()}
+    out = torch_ref.moe_ref(torch.from_numpy(x), torch.from_numpy(z["topk_ids"]), torch.from_numpy(z["topk_w"]), tl)
+    assert O.rel_l2(out.numpy(), z["ref_dense"]) < 1e-5
