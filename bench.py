@@ -1,0 +1,273 @@
+"""Benchmark of the vq2 routed-expert MoE path (BASELINE.json metric:
+"vq2 MoE layer: decode us/token (% HBM roofline); prefill tok/s (% fp8 TC peak)").
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One step = one call of the MoE layer on one decode batch (config 1: H=4096, I=2048, 256 routed
+experts, top-8, batch 1; batch 3 is reported beside it). Weights are seeded synthetic tensors
+in the reference layout. Four independent layers (8.8 GB) are cycled step by step, so every
+step streams its experts from HBM (the working set of the cycle is far above the 126 MB L2).
+
+N > 1 (torchrun, one rank per GPU): expert-parallel decode (config 3 shapes) — experts
+partitioned over the ranks, NCCL all-to-all dispatch and combine — timed as the max over ranks.
+
+--impl reference: the reference's CPU path (fp32 dequant + matmul, restated in
+oracle/torch_ref.py) on the host cores, on the same metric; rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(HERE, "deepseek-v4-flash-2bit-gb10_b200"))
+sys.path.insert(0, HERE)
+
+import torch  # noqa: E402
+
+METRIC = "vq2 MoE layer: decode us/token (% HBM roofline); prefill tok/s (% fp8 TC peak)"
+H, I, E, K = 4096, 2048, 256, 8
+IDX_BYTES_PER_EXPERT = 3 * H * I // 4 + 3 * H * I // 16          # lo + hi planes (gate, up, down)
+SC_BYTES_PER_EXPERT = 3 * H * I // 64 * 2                          # fp16 group scales
+FALLBACK_HBM_GBS = 6650.0
+
+
+def peaks():
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p.get("bf16_tflops", 1590.0)), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, 1590.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampler running during the timed region (clocks + throttle reasons)."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.p = None
+
+    def __enter__(self):
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                                       "--format=csv,noheader,nounits", "-lms", "100"],
+                                      stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.p = None
+        return self
+
+    def __exit__(self, *a):
+        self.rows = []
+        if self.p is None:
+            return
+        self.p.terminate()
+        out, _ = self.p.communicate(timeout=10)
+        for line in out.strip().splitlines():
+            f = [v.strip() for v in line.split(",")]
+            if len(f) >= 9:
+                self.rows.append(f)
+
+    def summary(self):
+        rows = getattr(self, "rows", [])
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def make_routing(x, seed):
+    from vq2_vllm import synth
+    return synth.route_softmax_topk(x, E, K, w_std=0.02, seed=seed)
+
+
+_CPU_LAYER = []
+
+
+def _cpu_layer():
+    if not _CPU_LAYER:
+        from vq2_vllm import synth
+        _CPU_LAYER.append(synth.make_layer(8, H, I, seed=0))
+    return _CPU_LAYER[0]
+
+
+def cpu_reference_us_per_token(threads, tokens=1, reps=1):
+    """The reference's CPU dequant+matmul path (oracle/torch_ref.py) on a bounded sample:
+    `tokens` decode tokens routed over 8 resident experts of the config-1 shape."""
+    from oracle import torch_ref
+    from vq2_vllm import synth
+    torch.set_num_threads(threads)
+    layer = _cpu_layer()
+    x = synth.make_tokens(tokens, H, seed=1)
+    ids = torch.stack([torch.randperm(8, generator=torch.Generator().manual_seed(t))[:K] for t in range(tokens)]).int()
+    w = torch.full((tokens, K), 1.0 / K)
+    torch_ref.moe_ref(x, ids, w, layer)                      # warm-up
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        torch_ref.moe_ref(x, ids, w, layer)
+        ts.append(time.perf_counter() - t0)
+    return statistics.median(ts) * 1e6 / tokens, f"{tokens} token(s), top-8 over 8 resident experts, H=4096 I=2048"
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    steps = []
+    for _ in range(max(args.warmup, 0)):
+        cpu_reference_us_per_token(threads)
+    for _ in range(args.steps):
+        v, sample = cpu_reference_us_per_token(threads)
+        steps.append(v)
+    v = statistics.median(steps)
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "us/token", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": v / 1e3, "higher_is_better": False,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": "config1 decode batch 1 (CPU sample)", "H": H, "I": I, "E": E, "topk": K},
+            "cpu_baseline": {"value": v, "unit": "us/token", "cores": threads, "kind": "port", "sample": sample},
+            "e2e": {"value": v, "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def time_decode(layers, xs, routes, steps, warmup, stream, soak_s=0.6):
+    """CUDA-event time per step (ms), cycling layers; inputs resident in HBM."""
+    from vq2_vllm.kernels.vq2_kernel import vq2_moe_fused_10b
+    from vq2_vllm import synth
+    nL = len(layers)
+
+    def step(i):
+        L = layers[i % nL]
+        ids, tw = routes[i % len(routes)]
+        return vq2_moe_fused_10b(xs[i % len(xs)], ids, tw, *synth.layer_args(L))
+
+    for i in range(warmup):
+        step(i)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()                # untimed soak: clocks settle and get sampled
+    i = 0
+    while time.perf_counter() - t0 < soak_s:
+        step(i)
+        i += 1
+        if i % 64 == 0:
+            torch.cuda.synchronize()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+    torch.cuda._sleep(5_000_000)          # queue ahead so host launch cost is hidden
+    s.record(stream)
+    for i in range(steps):
+        step(i)
+    e.record(stream)
+    e.synchronize()
+    return s.elapsed_time(e) / steps
+
+
+def run_ours(args, rank, world):
+    from vq2_vllm import synth
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
+    torch.cuda.set_device(dev)
+    if world > 1:
+        from vq2_vllm import ep
+        return ep.bench_ep(args, rank, world, METRIC)
+    hbm, _, src = peaks()
+    stream = torch.cuda.current_stream()
+    nlayers = 4
+    layers = [synth.make_layer(E, H, I, seed=10 + l, device=dev) for l in range(nlayers)]
+    res = {}
+    for B in (1, 3):
+        xs = [synth.make_tokens(B, H, seed=100 + j, device=dev) for j in range(8)]
+        routes = [make_routing(xs[j], seed=200 + j) for j in range(8)]
+        distinct = sum(torch.unique(routes[j % 8][0]).numel() for j in range(args.steps)) / args.steps
+        with Clocks(dev.index) as ck:
+            ms = time_decode(layers, xs, routes, args.steps, max(args.warmup, 3), stream)
+        res[B] = (ms, distinct, ck.summary())
+    ms1, u1, clocks = res[1]
+    us_tok = ms1 * 1e3 / 1
+    idx_bytes = u1 * IDX_BYTES_PER_EXPERT + 1 * H * 2 + 1 * H * 4
+    all_bytes = idx_bytes + u1 * SC_BYTES_PER_EXPERT + 2 * 8192
+    achieved = idx_bytes / (ms1 * 1e-3) / 1e9
+
+    # e2e: the public API with host buffers; H2D of x / ids / weights and D2H of the output
+    from vq2_vllm.kernels.vq2_kernel import vq2_moe_fused_10b
+    xh = [x.cpu().pin_memory() for x in [synth.make_tokens(1, H, seed=100 + j) for j in range(8)]]
+    rh = [(r[0].cpu().pin_memory(), r[1].cpu().pin_memory()) for r in
+          [make_routing(synth.make_tokens(1, H, seed=100 + j, device=dev), 200 + j) for j in range(8)]]
+    outh = torch.empty(1, H, dtype=torch.float32).pin_memory()
+
+    def e2e_step(i):
+        L = layers[i % nlayers]
+        x = xh[i % 8].to(dev, non_blocking=True)
+        ids = rh[i % 8][0].to(dev, non_blocking=True)
+        tw = rh[i % 8][1].to(dev, non_blocking=True)
+        out = vq2_moe_fused_10b(x, ids, tw, *synth.layer_args(L))
+        outh.copy_(out, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+    s.record()
+    for i in range(args.steps):
+        e2e_step(i)
+    e.record()
+    e.synchronize()
+    e2e_ms = s.elapsed_time(e) / args.steps
+    h2d = H * 2 + K * 4 + K * 4
+    d2h = H * 4
+
+    cpu_v, cpu_sample = (None, None)
+    if not args.no_cpu:
+        cpu_v, cpu_sample = cpu_reference_us_per_token(os.cpu_count() or 1)
+    ms3, u3, _ = res[3]
+    line = {"metric": METRIC, "value": us_tok, "unit": "us/token", "n_gpus": 1, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": ms1, "higher_is_better": False, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16x2+f32 (10-bit VQ indices, fp16 codebook/scales)",
+            "data": "synthetic (seeded weights in the reference layout, softmax top-8 routing)",
+            "config": {"workload": "config1 decode batch 1 (batch 3 in decode_b3)", "H": H, "I": I, "E": E,
+                       "topk": K, "batch": 1, "l2": f"{nlayers} layers cycled per step (8.8 GB > L2)",
+                       "distinct_experts_per_step": u1},
+            "decode_b3": {"us_per_token": ms3 * 1e3 / 3, "us_per_layer_call": ms3 * 1e3, "distinct_experts": u3,
+                          "idx_act_GBps": (u3 * IDX_BYTES_PER_EXPERT + 3 * H * 6) / (ms3 * 1e-3) / 1e9},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": None,
+                         "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src,
+                         "bytes": "index planes of distinct experts + x + out per layer call",
+                         "achieved_incl_scales": all_bytes / (ms1 * 1e-3) / 1e9},
+            "cpu_baseline": {"value": cpu_v, "unit": "us/token", "cores": os.cpu_count(), "kind": "port",
+                             "sample": cpu_sample},
+            "e2e": {"value": e2e_ms * 1e3, "unit": "us/token", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": 2 * args.steps,
+            "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    args = ap.parse_args()
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+    return run_ours(args, rank, world)
+
+
+if __name__ == "__main__":
+    main()

@@ -2,37 +2,56 @@
 // reference vq2_vllm/kernels/vq2_kernel.py:569-594).
 //
 // Two persistent kernels, one CTA per SM, chained with programmatic dependent launch:
-//   gateup: inter[m, i] = silu(<W_gate,e[i], Hx_n>) * <W_up,e[i], Hx_n>       (fp32 scratch)
-//   down:   out[n, h]  += w_m * <W_down,e[h], H·inter[m]>                       (fp32 red.add)
+//   gateup: part[m, s] = (<W_gate,e[i], Hx_n>, <W_up,e[i], Hx_n>) over K-slice s (fp32 scratch)
+//   down:   out[n, h] += w_m * <W_down,e[h], H·(silu(sum_s gate) * sum_s up)>  (fp32 red.add)
 // for every (token n, slot j) pair m routed to expert e. Pairs are grouped by expert so each
-// expert's index planes stream from HBM once per group of up to TT tokens.
+// expert's index planes stream from HBM once per group of up to DEC_TT tokens.
 //
 // Per CTA: a producer warp streams contiguous row chunks (lo / hi / scale planes) into a ring
 // of shared-memory stages with 1-D bulk async copies (TMA engine) and mbarriers; consumer warps
-// decode them. Lane l of a warp owns the 64-wide groups l, l+32 of a row: one 16-byte lo load,
-// one 4-byte hi load and one fp16 scale per group. The 1024x4 fp16 codebook is replicated 16x
-// in shared memory so that lane l reads only from bank pair (l mod 16): a half-warp's 8-byte
-// gathers are conflict-free. The Hadamard rotation of the activation is done per lane with an
-// in-register 64-point FWHT; activations are held as fp16 (scaled by a power of two so they
-// cannot overflow) and multiplied with fp16 codebook values by mixed-precision
-// fma.rn.f32.f16 into fp32 accumulators.
+// decode them. Lane l of a warp owns one 64-wide group of a row (a warp covers a 32-group
+// K-slice; rows wider than 2048 are split over KH warps): one 16-byte lo load, one 4-byte hi load
+// and one fp16 scale per group. A warp decodes several rows at once (independent chains) and
+// reduces their partial sums together with a halving shuffle reduction. The 1024x4 fp16 codebook
+// is replicated 16x in shared memory so that lane l reads only from bank pair (l mod 16): a
+// half-warp's 8-byte gathers are conflict-free. The Hadamard rotation of the activation is an
+// in-register 64-point FWHT per lane. Activations are held as fp16, scaled by a power of two
+// chosen from the slice max and the codebook max so that no half2 partial can overflow; a
+// group's 16 codebook-vector x activation products accumulate in packed half2 FMAs, and groups
+// combine in fp32 with their scale.
+#include <cstddef>
 #include "vq2_common.cuh"
 
 namespace vq2 {
 
-constexpr int DEC_NW = 8;                 // consumer warps
+#ifndef VQ2_DEC_NW
+#define VQ2_DEC_NW 8
+#endif
+constexpr int DEC_NW = VQ2_DEC_NW;        // consumer warps
 constexpr int DEC_THREADS = (DEC_NW + 1) * 32;
-constexpr int DEC_TT = 2;                 // tokens per unit held in registers
-constexpr int DEC_STAGES = 4;
+constexpr int DEC_TT = 1;                 // tokens per unit (a unit = one (expert, token) pair)
+constexpr int DEC_STAGES = 3;
 constexpr int DEC_GRAN = 8;               // row granule of the work split (keeps copies 16-B sized)
+constexpr int DEC_SA = 8;                 // gate/up row pairs per stage
+constexpr int DEC_SB = 32;                // down rows per stage
+constexpr int DEC_MAXG = 64;              // max 64-groups per input row (4096 / 64)
 constexpr int CB_COPIES = 16;
 constexpr int CB_BYTES = 1024 * 8 * CB_COPIES;   // 128 KB
 
 struct DecodeShared {
   uint64_t full[DEC_STAGES];
   uint64_t empty[DEC_STAGES];
+  uint64_t cbbar;
   int nunits;
   int abort;
+  float cmax;
+  float red[32];
+  unsigned slice_max[2];
+  float slice_inv[2];
+  alignas(16) uint32_t xs[DEC_MAXG][32];    // rotated, scaled activation of the current unit (half2 per group)
+  // prologue: the codebook as loaded (bulk-copy destination, 8 KB); main loop (down kernel): the
+  // combined silu(gate) * up row of the current unit, fp32, before rotation
+  alignas(16) float scratch[DEC_MAXG * 64];
   short unit_e[VQ2_DECODE_MAX_PAIRS];
   short unit_m[VQ2_DECODE_MAX_PAIRS][DEC_TT];
   int ekey[VQ2_DECODE_MAX_PAIRS];
@@ -46,10 +65,8 @@ __device__ void build_plan(const void* ids, int ids_dtype, int M, int E, int exp
                            DecodeShared* sh) {
   const int tid = threadIdx.x, nt = blockDim.x;
   for (int e = tid; e < E; e += nt) sh->cnt[e] = 0;
-  for (int u = tid; u < M; u += nt) {
-    sh->unit_m[u][0] = -1;
-    sh->unit_m[u][1] = -1;
-  }
+  for (int u = tid; u < M; u += nt)
+    for (int t = 0; t < DEC_TT; ++t) sh->unit_m[u][t] = -1;
   for (int m = tid; m < M; m += nt) {
     int e = load_id(ids, ids_dtype, m) - expert_base;
     sh->ekey[m] = (e >= 0 && e < E) ? e : -1;
@@ -112,114 +129,311 @@ struct ChunkIter {
   }
 };
 
-__device__ __forceinline__ void fill_codebook(const uint16_t* cb, uint8_t* cbs) {
-  const uint2* src = (const uint2*)cb;
-  for (int idx = threadIdx.x; idx < 1024 * CB_COPIES; idx += blockDim.x) {
-    int e = idx / CB_COPIES, c = idx % CB_COPIES;
-    *(uint2*)(cbs + e * (8 * CB_COPIES) + c * 8) = src[e];
-  }
+#ifdef VQ2_DEC_PROBE
+// Development probe (off in the product build): per-CTA global-timer stamps of the phases.
+__device__ unsigned long long g_probe[2][1024][8];
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+#define PROBE(k, i) do { g_probe[k][blockIdx.x][i] = gtime(); } while (0)
+#else
+#define PROBE(k, i) do {} while (0)
+#endif
+
+// consumer-only barrier (named barrier 1; the producer warp never joins it)
+__device__ __forceinline__ void consumer_sync() {
+  asm volatile("bar.sync 1, %0;" ::"r"(DEC_NW * 32) : "memory");
 }
 
-// acc += <codebook[id_s], x_s> over the 16 sub-vectors of one 64-group, for NT tokens.
-// lo: the group's 16 index low bytes; hw: its 4 hi bytes; xa[t]: 32 half2 regs of the group.
-template <int NT>
-__device__ __forceinline__ void group_dot(uint4 lo, uint32_t hw, uint32_t cb_lane,
-                                          const uint32_t (*xa)[32], float* acc) {
-  const uint32_t lw[4] = {lo.x, lo.y, lo.z, lo.w};
+// Consumers replicate the codebook (landed in sh->cbstage by one bulk copy) 16x — entry e of
+// copy c at byte e*128 + c*8 — and record max |C| into sh->cmax. Ends with a consumer barrier.
+__device__ __forceinline__ void fill_codebook(uint8_t* cbs, DecodeShared* sh) {
+  const int tid = threadIdx.x;
+  mbar_wait(&sh->cbbar, 0);
+  const uint2* src = (const uint2*)sh->scratch;
+  float m = 0.f;
+  // consecutive threads write consecutive 16-byte chunks (conflict-free stores)
+  for (int idx = tid; idx < 1024 * (CB_COPIES / 2); idx += DEC_NW * 32) {
+    const int e = idx / (CB_COPIES / 2), k = idx % (CB_COPIES / 2);
+    const uint2 v = src[e];
+    *(uint4*)(cbs + e * (8 * CB_COPIES) + k * 16) = make_uint4(v.x, v.y, v.x, v.y);
+    if (k == 0) {
+      const float2 a = __half22float2(*(const __half2*)&v.x), b = __half22float2(*(const __half2*)&v.y);
+      m = fmaxf(m, fmaxf(fmaxf(fabsf(a.x), fabsf(a.y)), fmaxf(fabsf(b.x), fabsf(b.y))));
+    }
+  }
+  m = warp_max(m);
+  if ((tid & 31) == 0) sh->red[tid >> 5] = m;
+  consumer_sync();
+  if (tid == 0) {
+    float r = 0.f;
+    for (int w = 0; w < DEC_NW; ++w) r = fmaxf(r, sh->red[w]);
+    sh->cmax = fmaxf(r, 1e-30f);
+  }
+  consumer_sync();
+}
+
+// R independent 64-group dot products for NT tokens: for each row r, sum over the group's 16
+// sub-vectors of <codebook[id_s], x_s>, accumulated in two half2 chains, returned in fp32.
+// lo[r]: the 16 index low bytes; hw[r]: the 4 hi bytes; x[t]: 32 half2 regs of the rotated group.
+template <int R, int NT>
+__device__ __forceinline__ void multi_dot(const uint4* lo, const uint32_t* hw, const uint8_t* cbl,
+                                          const uint32_t (*x)[32], float (*out)[NT]) {
+  __half2 a0[R][NT], a1[R][NT];
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int t = 0; t < NT; ++t) { a0[r][t] = __float2half2_rn(0.f); a1[r][t] = a0[r][t]; }
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    const uint32_t L = lw[q];
-    const uint32_t hb = hw >> (8 * q);
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int s = 4 * q + j;
-      uint32_t off = (((L >> (8 * j)) & 0xFFu) << 7) | (((hb >> (2 * j)) & 3u) << 15);
-      uint32_t c0, c1;
-      asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(c0), "=r"(c1) : "r"(cb_lane + off));
 #pragma unroll
-      for (int t = 0; t < NT; ++t) {
-        asm("{\n .reg .f16 a0, a1, a2, a3, b0, b1, b2, b3;\n"
-            " mov.b32 {a0, a1}, %1;\n mov.b32 {a2, a3}, %2;\n"
-            " mov.b32 {b0, b1}, %3;\n mov.b32 {b2, b3}, %4;\n"
-            " fma.rn.f32.f16 %0, a0, b0, %0;\n fma.rn.f32.f16 %0, a1, b1, %0;\n"
-            " fma.rn.f32.f16 %0, a2, b2, %0;\n fma.rn.f32.f16 %0, a3, b3, %0;\n}"
-            : "+f"(acc[t]) : "r"(c0), "r"(c1), "r"(xa[t][2 * s]), "r"(xa[t][2 * s + 1]));
+      for (int r = 0; r < R; ++r) {
+        const uint32_t L = q == 0 ? lo[r].x : q == 1 ? lo[r].y : q == 2 ? lo[r].z : lo[r].w;
+        const uint32_t off = (((L >> (8 * j)) & 0xFFu) << 7) | (((hw[r] >> (8 * q + 2 * j)) & 3u) << 15);
+        const uint2 c = *(const uint2*)(cbl + off);
+        const __half2 c01 = *(const __half2*)&c.x, c23 = *(const __half2*)&c.y;
+#pragma unroll
+        for (int t = 0; t < NT; ++t) {
+          __half2& acc = (s & 1) ? a1[r][t] : a0[r][t];
+          acc = __hfma2(c01, *(const __half2*)&x[t][2 * s], acc);
+          acc = __hfma2(c23, *(const __half2*)&x[t][2 * s + 1], acc);
+        }
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < R; ++r)
+#pragma unroll
+    for (int t = 0; t < NT; ++t) {
+      const float2 f = __half22float2(__hadd2(a0[r][t], a1[r][t]));
+      out[r][t] = f.x + f.y;
+    }
+}
+
+// Sum V (= 2, 4 or 8) per-lane values over the warp with V + 1 shuffles instead of 5V: each
+// halving step keeps half of the values per lane. Afterwards every lane holds the total of value
+// reduce_index<V>(lane).
+template <int V>
+__device__ __forceinline__ int reduce_index(int lane) {
+  return V == 8 ? (lane >> 2) & 7 : V == 4 ? (lane >> 3) & 3 : (lane >> 4) & 1;
+}
+template <int V>
+__device__ __forceinline__ float warp_reduce_multi(float* v) {
+  const int lane = threadIdx.x & 31;
+  int n = V;
+#pragma unroll
+  for (int o = 16; o >= 4; o >>= 1) {
+    if (n > 1) {
+      const bool hi = (lane & o) != 0;
+#pragma unroll
+      for (int i = 0; i < V / 2; ++i) {
+        if (i < n / 2) {
+          const float send = hi ? v[i] : v[i + n / 2];
+          const float keep = hi ? v[i + n / 2] : v[i];
+          v[i] = keep + __shfl_xor_sync(0xffffffffu, send, o);
+        }
+      }
+      n >>= 1;
+    } else {
+      v[0] += __shfl_xor_sync(0xffffffffu, v[0], o);
+    }
+  }
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 2);
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+  return v[0];
+}
+
+// CTA-wide staging of one unit's activation: consumer thread g (< ng) holds the fp32 values of
+// 64-group g in v; it is rotated (FWHT), the max over its 32-group K-slice is formed in shared
+// memory, and the group is scaled by a power of two so that max|x| * max|C| * 32 <= 2^15 over the
+// slice (no half2 partial can overflow) and stored as half2 in sh->xs[g]. sh->slice_inv[s] gets
+// the factor undoing the scale and the Hadamard's 1/8. Called by all consumer threads.
+__device__ __forceinline__ void stage_activation(float* v, bool valid, int g, DecodeShared* sh) {
+  const int tid = threadIdx.x;
+  if (tid < 2) sh->slice_max[tid] = 0u;
+  consumer_sync();                         // previous unit's xs no longer read; maxima reset
+  float amax = 0.f;
+  if (valid) {
+    fwht64(v);
+#pragma unroll
+    for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(v[i]));
+    atomicMax(&sh->slice_max[g >> 5], __float_as_uint(amax));   // non-negative floats order as ints
+  }
+  consumer_sync();
+  if (valid) {
+    const float smax = __uint_as_float(sh->slice_max[g >> 5]);
+    float sc = 1.f, inv = 1.f;
+    if (smax > 0.f) {
+      int ex;
+      frexpf((1024.f / sh->cmax) / smax, &ex);      // ratio in [2^(ex-1), 2^ex)
+      const int s = max(-100, min(100, ex - 1));
+      sc = ldexpf(1.f, s);
+      inv = ldexpf(1.f, -s);
+    }
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      __half2 h = __floats2half2_rn(v[2 * i] * sc, v[2 * i + 1] * sc);
+      sh->xs[g][i] = *(uint32_t*)&h;
+    }
+    if ((g & 31) == 0) sh->slice_inv[g >> 5] = inv * 0.125f;
+  }
+  consumer_sync();
+}
+
+// A consumer lane's copy of its group's staged activation (zeros past the row's groups).
+__device__ __forceinline__ void load_xs(const DecodeShared* sh, int g, bool gv, uint32_t* xr) {
+#pragma unroll
+  for (int i = 0; i < 32; i += 4) {
+    const uint4 q = gv ? *(const uint4*)&sh->xs[g][i] : make_uint4(0, 0, 0, 0);
+    xr[i] = q.x; xr[i + 1] = q.y; xr[i + 2] = q.z; xr[i + 3] = q.w;
+  }
+}
+
+// 64 consecutive activations of one token (bf16 / f16 / f32) -> fp32 registers.
+__device__ __forceinline__ void load_x64(const void* x, int dt, size_t base, float* v) {
+  if (dt == VQ2_DT_F32) {
+    const float4* p = (const float4*)((const float*)x + base);
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const float4 f = p[i];
+      v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
+    }
+  } else {
+    const uint4* p = (const uint4*)((const uint16_t*)x + base);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint4 u = p[i];
+      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        float2 f;
+        if (dt == VQ2_DT_BF16) f = __bfloat1622float2(*(const __nv_bfloat162*)&w[k]);
+        else f = __half22float2(*(const __half2*)&w[k]);
+        v[8 * i + 2 * k] = f.x; v[8 * i + 2 * k + 1] = f.y;
       }
     }
   }
 }
 
-// Load one activation row (64*GPL per lane: groups lane + 32 q) as fp32, rotate each group with
-// the FWHT, scale into fp16 range and pack. Returns the factor that undoes scale and the 1/8.
-template <int GPL, typename LoadF>
-__device__ __forceinline__ float load_rotated(LoadF ld, int ngroups, uint32_t (*xa)[32]) {
-  const int lane = threadIdx.x & 31;
-  float amax = 0.f;
-  float v[64];
-#pragma unroll
-  for (int q = 0; q < GPL; ++q) {
-    const int g = lane + 32 * q;
-    if (g < ngroups) {
-#pragma unroll
-      for (int i = 0; i < 64; ++i) v[i] = ld(g * 64 + i);
-      fwht64(v);
-#pragma unroll
-      for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    }
+// Shared-memory carve-up.
+struct DecSmem {
+  uint8_t* cbs;
+  DecodeShared* sh;
+  uint8_t* stages;
+};
+__device__ __forceinline__ DecSmem dec_smem(uint8_t* smem) {
+  DecSmem d;
+  d.cbs = smem;
+  d.sh = (DecodeShared*)(smem + CB_BYTES);
+  d.stages = smem + CB_BYTES + ((sizeof(DecodeShared) + 127) / 128) * 128;
+  return d;
+}
+
+// Barrier init, codebook bulk copy, expert plan (all threads; ends with __syncthreads).
+__device__ __forceinline__ void dec_prologue(const vq2_moe_args& a, const uint16_t* cb, DecSmem d) {
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < DEC_STAGES; ++s) { mbar_init(&d.sh->full[s], 1); mbar_init(&d.sh->empty[s], DEC_NW); }
+    mbar_init(&d.sh->cbbar, 1);
+    d.sh->abort = 0;
+    fence_mbar_init();
+    mbar_arrive_expect_tx(&d.sh->cbbar, 1024 * 4 * 2);
+    bulk_g2s(d.sh->scratch, cb, 1024 * 4 * 2, &d.sh->cbbar);
   }
-  amax = warp_max(amax);
-  const float2 sc = f16_range_scale(amax);
+  build_plan(a.topk_ids, a.ids_dtype, a.N * a.topk, a.E, a.expert_base, d.sh);
+}
+
+// One pass of a consumer warp over RB gate/up row pairs of a stage (rows rr0 + k*rstep):
+// 2*RB group dot products, one batched reduction, 2*RB writer lanes.
+template <int RB>
+__device__ __forceinline__ void gateup_rows(const uint8_t* st, int rr0, int rstep, int n, int g, bool gv, int nsub,
+                                            int ng, uint32_t lo_b, uint32_t hi_b, uint32_t sc_b, const uint8_t* cbl,
+                                            const uint32_t (*xr)[32], float inv, int m, int KH, int h, int I,
+                                            int i0, float* part) {
+  constexpr int R = 2 * RB;
+  uint4 lo[R];
+  uint32_t hw[R];
+  float sc[R];
 #pragma unroll
-  for (int q = 0; q < GPL; ++q) {
-    const int g = lane + 32 * q;
-    if (g < ngroups) {
-      // recompute (cheaper in registers than keeping GPL*64 floats live)
+  for (int k = 0; k < RB; ++k) {
+    const int rr = rr0 + k * rstep;
+    if (gv && rr < n) {
 #pragma unroll
-      for (int i = 0; i < 64; ++i) v[i] = ld(g * 64 + i);
-      fwht64(v);
-#pragma unroll
-      for (int i = 0; i < 32; ++i) {
-        __half2 h = __floats2half2_rn(v[2 * i] * sc.x, v[2 * i + 1] * sc.x);
-        xa[q][i] = *(uint32_t*)&h;
+      for (int u = 0; u < 2; ++u) {   // u = 0 gate row, 1 up row
+        lo[2 * k + u] = *(const uint4*)(st + u * lo_b + rr * nsub + g * 16);
+        hw[2 * k + u] = *(const uint32_t*)(st + 2 * lo_b + u * hi_b + rr * (nsub / 4) + g * 4);
+        sc[2 * k + u] = __half2float(*(const __half*)(st + 2 * (lo_b + hi_b) + u * sc_b + (rr * ng + g) * 2));
       }
     } else {
 #pragma unroll
-      for (int i = 0; i < 32; ++i) xa[q][i] = 0u;
+      for (int u = 0; u < 2; ++u) { lo[2 * k + u] = make_uint4(0, 0, 0, 0); hw[2 * k + u] = 0; sc[2 * k + u] = 0.f; }
     }
   }
-  return sc.y * 0.125f;
+  float d[R][1];
+  multi_dot<R, 1>(lo, hw, cbl, xr, d);
+  float v[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) v[r] = d[r][0] * sc[r] * inv;
+  const float tot = warp_reduce_multi<R>(v);
+  const int lane = threadIdx.x & 31;
+  const int r = reduce_index<R>(lane);
+  const int rr = rr0 + (r >> 1) * rstep;
+  if ((lane & (32 / R - 1)) == 0 && rr < n) part[(((size_t)m * KH + h) * 2 + (r & 1)) * I + i0 + rr] = tot;
 }
 
-// ------------------------------------------------------------------ kernel A: gate/up + SiLU
-template <int GPL>
-__global__ void __launch_bounds__(DEC_THREADS, 1)
-decode_gateup_kernel(vq2_moe_args a, float* __restrict__ inter) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* cbs = smem;
-  DecodeShared* sh = (DecodeShared*)(smem + CB_BYTES);
-  uint8_t* stages = smem + CB_BYTES + ((sizeof(DecodeShared) + 127) / 128) * 128;
+// One pass of a consumer warp over R down rows of a stage (rows rr0 + r*rstep).
+template <int R>
+__device__ __forceinline__ void down_rows(const uint8_t* st, int rr0, int rstep, int n, int g, bool gv, int nsub,
+                                          int ng, uint32_t lo_b, uint32_t hi_b, const uint8_t* cbl,
+                                          const uint32_t (*xr)[32], float wsc, int tok, int H, int h0, float* out) {
+  uint4 lo[R];
+  uint32_t hw[R];
+  float sc[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) {
+    const int rr = rr0 + r * rstep;
+    if (gv && rr < n) {
+      lo[r] = *(const uint4*)(st + rr * nsub + g * 16);
+      hw[r] = *(const uint32_t*)(st + lo_b + rr * (nsub / 4) + g * 4);
+      sc[r] = __half2float(*(const __half*)(st + lo_b + hi_b + (rr * ng + g) * 2));
+    } else {
+      lo[r] = make_uint4(0, 0, 0, 0); hw[r] = 0; sc[r] = 0.f;
+    }
+  }
+  float d[R][1];
+  multi_dot<R, 1>(lo, hw, cbl, xr, d);
+  float v[R];
+#pragma unroll
+  for (int r = 0; r < R; ++r) v[r] = d[r][0] * sc[r] * wsc;
+  const float tot = warp_reduce_multi<R>(v);
+  const int lane = threadIdx.x & 31;
+  const int r = reduce_index<R>(lane);
+  const int rr = rr0 + r * rstep;
+  if ((lane & (32 / R - 1)) == 0 && rr < n) atomicAdd(&out[(size_t)tok * H + h0 + rr], tot);
+}
 
+// ------------------------------------------------------------------ kernel A: gate/up partials
+// KH = K-slices of the H-wide input (H/64 groups, 32 per warp).
+template <int KH>
+__global__ void __launch_bounds__(DEC_THREADS, 1)
+decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const DecSmem d = dec_smem(smem);
+  DecodeShared* sh = d.sh;
+  if (threadIdx.x == 0) PROBE(0, 0);
   pdl_launch_dependents();
-  const int H = a.H, I = a.I, M = a.N * a.topk;
+  const int H = a.H, I = a.I;
   const int nsub = H / 4, ng = H / 64;
-  const int S = 8;
+  constexpr int S = DEC_SA;
   const uint32_t lo_b = S * nsub, hi_b = S * (nsub / 4), sc_b = S * ng * 2;
   const uint32_t stage_b = 2 * (lo_b + hi_b + sc_b);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  // zero the output (down kernel accumulates into it after its grid-dependency wait)
-  {
-    const long tot = (long)a.N * a.H;
-    for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < tot; i += (long)gridDim.x * blockDim.x)
-      a.out[i] = 0.f;
-  }
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < DEC_STAGES; ++s) { mbar_init(&sh->full[s], 1); mbar_init(&sh->empty[s], DEC_NW); }
-    sh->abort = 0;
-    fence_mbar_init();
-  }
-  fill_codebook(a.w13_cb, cbs);
-  build_plan(a.topk_ids, a.ids_dtype, M, a.E, a.expert_base, sh);   // ends with __syncthreads
+  dec_prologue(a, a.w13_cb, d);
   const long total = (long)sh->nunits * I;
 
   if (warp == DEC_NW) {   // ---------------- producer
@@ -231,7 +445,7 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ inter) {
         if (c >= DEC_STAGES && !mbar_wait(&sh->empty[slot], ((c / DEC_STAGES) - 1) & 1)) { sh->abort = 1; break; }
         const long e = sh->unit_e[u];
         const long rg = e * 2 * I + i0, ru = rg + I;
-        uint8_t* st = stages + slot * stage_b;
+        uint8_t* st = d.stages + slot * stage_b;
         mbar_arrive_expect_tx(&sh->full[slot], 2u * n * (nsub + nsub / 4 + ng * 2));
         bulk_g2s(st, a.w13_lo + rg * nsub, n * nsub, &sh->full[slot]);
         bulk_g2s(st + lo_b, a.w13_lo + ru * nsub, n * nsub, &sh->full[slot]);
@@ -242,106 +456,76 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ inter) {
         ++c;
       }
       // drain: every issued copy must land before the CTA exits
-      for (int d = max(0, c - DEC_STAGES); d < c; ++d) mbar_wait(&sh->full[d % DEC_STAGES], (d / DEC_STAGES) & 1);
+      for (int q = max(0, c - DEC_STAGES); q < c; ++q) mbar_wait(&sh->full[q % DEC_STAGES], (q / DEC_STAGES) & 1);
     }
     return;
   }
 
   // ---------------- consumers
-  const uint32_t cb_lane = smem_u32(cbs) + (lane & (CB_COPIES - 1)) * 8;
-  uint32_t xa[DEC_TT][GPL][32];
-  float inv[DEC_TT];
-  int mcur[DEC_TT];
-  int ucur = -1;
+  {  // zero the output (the down kernel accumulates into it after its grid-dependency wait)
+    const long tot = (long)a.N * a.H;
+    for (long i = (long)blockIdx.x * DEC_NW * 32 + threadIdx.x; i < tot; i += (long)gridDim.x * DEC_NW * 32)
+      a.out[i] = 0.f;
+  }
+  if (threadIdx.x == 0) PROBE(0, 1);
+  fill_codebook(d.cbs, sh);
+  if (threadIdx.x == 0) PROBE(0, 2);
+  const int h = warp % KH, rsub = warp / KH, rstep = DEC_NW / KH;
+  const int g = h * 32 + lane;
+  const bool gv = g < ng;
+  const uint8_t* cbl = d.cbs + (lane & (CB_COPIES - 1)) * 8;
+  uint32_t xr[1][32];
+  float inv = 0.f;
+  int mcur = -1, ucur = -1;
   ChunkIter it(total, I, S);
   int u, i0, n, c = 0;
   while (it.next(u, i0, n)) {
     const int slot = c % DEC_STAGES;
-    if (u != ucur) {
+    if (u != ucur) {   // uniform across consumer warps: all walk the same chunk list
       ucur = u;
-#pragma unroll
-      for (int t = 0; t < DEC_TT; ++t) {
-        const int m = sh->unit_m[u][t];
-        mcur[t] = m;
-        if (m >= 0) {
-          const int tok = m / a.topk;
-          const void* xp = a.x;
-          const int dt = a.x_dtype;
-          inv[t] = load_rotated<GPL>([&](int k) { return load_act(xp, dt, (size_t)tok * H + k); }, ng, xa[t]);
-        } else {
-          inv[t] = 0.f;
-#pragma unroll
-          for (int q = 0; q < GPL; ++q)
-#pragma unroll
-            for (int i = 0; i < 32; ++i) xa[t][q][i] = 0u;
-        }
-      }
+      mcur = sh->unit_m[u][0];
+      const int tg = threadIdx.x;
+      float v[64];
+      const bool ok = tg < ng;
+      if (ok) load_x64(a.x, a.x_dtype, (size_t)(mcur / a.topk) * H + tg * 64, v);
+      stage_activation(v, ok, tg, sh);
+      load_xs(sh, g, gv, xr[0]);
+      inv = sh->slice_inv[h];
+      if (threadIdx.x == 0 && c == 0) PROBE(0, 5);
     }
     if (!mbar_wait(&sh->full[slot], (c / DEC_STAGES) & 1)) break;
-    const uint8_t* st = stages + slot * stage_b;
-    for (int rr = warp; rr < n; rr += DEC_NW) {
-      float g[DEC_TT] = {}, up[DEC_TT] = {};
-#pragma unroll
-      for (int q = 0; q < GPL; ++q) {
-        const int gi = lane + 32 * q;
-        if (gi < ng) {
-          float ag[DEC_TT] = {}, au[DEC_TT] = {};
-          const uint4 lg = *(const uint4*)(st + rr * nsub + gi * 16);
-          const uint4 lu = *(const uint4*)(st + lo_b + rr * nsub + gi * 16);
-          const uint32_t hg = *(const uint32_t*)(st + 2 * lo_b + rr * (nsub / 4) + gi * 4);
-          const uint32_t hu = *(const uint32_t*)(st + 2 * lo_b + hi_b + rr * (nsub / 4) + gi * 4);
-          const float sg = __half2float(*(const __half*)(st + 2 * (lo_b + hi_b) + (rr * ng + gi) * 2));
-          const float su = __half2float(*(const __half*)(st + 2 * (lo_b + hi_b) + sc_b + (rr * ng + gi) * 2));
-          uint32_t (*xq)[32] = nullptr;
-          (void)xq;
-          uint32_t xt[DEC_TT][32];
-#pragma unroll
-          for (int t = 0; t < DEC_TT; ++t)
-#pragma unroll
-            for (int i = 0; i < 32; ++i) xt[t][i] = xa[t][q][i];
-          group_dot<DEC_TT>(lg, hg, cb_lane, xt, ag);
-          group_dot<DEC_TT>(lu, hu, cb_lane, xt, au);
-#pragma unroll
-          for (int t = 0; t < DEC_TT; ++t) { g[t] += ag[t] * sg; up[t] += au[t] * su; }
-        }
-      }
-#pragma unroll
-      for (int t = 0; t < DEC_TT; ++t) {
-        const float gs = warp_sum(g[t]) * inv[t];
-        const float us = warp_sum(up[t]) * inv[t];
-        if (lane == 0 && mcur[t] >= 0)
-          inter[(size_t)mcur[t] * I + i0 + rr] = gs / (1.f + __expf(-gs)) * us;
-      }
+    if (threadIdx.x == 0 && c == 0) PROBE(0, 3);
+    const uint8_t* st = d.stages + slot * stage_b;
+    if (S / rstep >= 2) {
+      for (int rr0 = rsub; rr0 < n; rr0 += 2 * rstep)
+        gateup_rows<2>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, sc_b, cbl, xr, inv, mcur, KH, h, I, i0, part);
+    } else {
+      for (int rr0 = rsub; rr0 < n; rr0 += rstep)
+        gateup_rows<1>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, sc_b, cbl, xr, inv, mcur, KH, h, I, i0, part);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&sh->empty[slot]);
     ++c;
   }
+  if (threadIdx.x == 0) PROBE(0, 4);
 }
 
 // ------------------------------------------------------------------ kernel B: down + combine
-template <int GPL>
+// KH = K-slices of the I-wide input; khA = K-slices the gate/up kernel used (partials to sum).
+template <int KH>
 __global__ void __launch_bounds__(DEC_THREADS, 1)
-decode_down_kernel(vq2_moe_args a, const float* __restrict__ inter) {
+decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
   extern __shared__ __align__(128) uint8_t smem[];
-  uint8_t* cbs = smem;
-  DecodeShared* sh = (DecodeShared*)(smem + CB_BYTES);
-  uint8_t* stages = smem + CB_BYTES + ((sizeof(DecodeShared) + 127) / 128) * 128;
-
-  const int H = a.H, I = a.I, M = a.N * a.topk;
+  const DecSmem d = dec_smem(smem);
+  DecodeShared* sh = d.sh;
+  const int H = a.H, I = a.I;
   const int nsub = I / 4, ng = I / 64;
-  const int S = 32;
+  constexpr int S = DEC_SB;
   const uint32_t lo_b = S * nsub, hi_b = S * (nsub / 4), sc_b = S * ng * 2;
   const uint32_t stage_b = lo_b + hi_b + sc_b;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < DEC_STAGES; ++s) { mbar_init(&sh->full[s], 1); mbar_init(&sh->empty[s], DEC_NW); }
-    sh->abort = 0;
-    fence_mbar_init();
-  }
-  fill_codebook(a.w2_cb, cbs);
-  build_plan(a.topk_ids, a.ids_dtype, M, a.E, a.expert_base, sh);
+  dec_prologue(a, a.w2_cb, d);
   const long total = (long)sh->nunits * H;
 
   if (warp == DEC_NW) {   // ---------------- producer: weights do not depend on the gate/up grid
@@ -352,93 +536,115 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ inter) {
         const int slot = c % DEC_STAGES;
         if (c >= DEC_STAGES && !mbar_wait(&sh->empty[slot], ((c / DEC_STAGES) - 1) & 1)) { sh->abort = 1; break; }
         const long r = (long)sh->unit_e[u] * H + h0;
-        uint8_t* st = stages + slot * stage_b;
+        if (c == 0) PROBE(1, 6);
+        uint8_t* st = d.stages + slot * stage_b;
         mbar_arrive_expect_tx(&sh->full[slot], (uint32_t)n * (nsub + nsub / 4 + ng * 2));
         bulk_g2s(st, a.w2_lo + r * nsub, n * nsub, &sh->full[slot]);
         bulk_g2s(st + lo_b, a.w2_hi + r * (nsub / 4), n * (nsub / 4), &sh->full[slot]);
         bulk_g2s(st + lo_b + hi_b, a.w2_sc + r * ng, n * ng * 2, &sh->full[slot]);
         ++c;
       }
-      for (int d = max(0, c - DEC_STAGES); d < c; ++d) mbar_wait(&sh->full[d % DEC_STAGES], (d / DEC_STAGES) & 1);
+      for (int q = max(0, c - DEC_STAGES); q < c; ++q) mbar_wait(&sh->full[q % DEC_STAGES], (q / DEC_STAGES) & 1);
     }
     return;
   }
 
-  pdl_wait();   // inter and the zeroed output come from the gate/up grid
-  const uint32_t cb_lane = smem_u32(cbs) + (lane & (CB_COPIES - 1)) * 8;
-  uint32_t xa[DEC_TT][GPL][32];
-  float wsc[DEC_TT];
-  int tokc[DEC_TT];
-  int ucur = -1;
+  if (threadIdx.x == 0) PROBE(1, 0);
+  fill_codebook(d.cbs, sh);
+  if (threadIdx.x == 0) PROBE(1, 1);
+  pdl_wait();   // the gate/up partials and the zeroed output come from the previous grid
+  if (threadIdx.x == 0) PROBE(1, 2);
+  const int h = warp % KH, rsub = warp / KH, rstep = DEC_NW / KH;
+  const int g = h * 32 + lane;
+  const bool gv = g < ng;
+  const uint8_t* cbl = d.cbs + (lane & (CB_COPIES - 1)) * 8;
+  uint32_t xr[1][32];
+  float wsc = 0.f;
+  int tok = -1, ucur = -1;
   ChunkIter it(total, H, S);
   int u, h0, n, c = 0;
   while (it.next(u, h0, n)) {
     const int slot = c % DEC_STAGES;
     if (u != ucur) {
       ucur = u;
+      const int m = sh->unit_m[u][0];
+      tok = m / a.topk;
+      const int tg = threadIdx.x;
+      // combine the K-slice partials and apply silu(gate) * up: all consumer threads, 4 columns
+      // per step, loads independent so they overlap
+      for (int i4 = tg; i4 < I / 4; i4 += DEC_NW * 32) {
+        const float* p = part + (size_t)m * khA * 2 * I + 4 * i4;
+        float4 G = *(const float4*)p, U = *(const float4*)(p + I);
+        if (khA > 1) {
+          const float4 g2 = *(const float4*)(p + 2 * I), u2 = *(const float4*)(p + 3 * I);
+          G.x += g2.x; G.y += g2.y; G.z += g2.z; G.w += g2.w;
+          U.x += u2.x; U.y += u2.y; U.z += u2.z; U.w += u2.w;
+        }
+        float4 r;
+        r.x = G.x / (1.f + __expf(-G.x)) * U.x;
+        r.y = G.y / (1.f + __expf(-G.y)) * U.y;
+        r.z = G.z / (1.f + __expf(-G.z)) * U.z;
+        r.w = G.w / (1.f + __expf(-G.w)) * U.w;
+        *(float4*)&sh->scratch[4 * i4] = r;
+      }
+      consumer_sync();
+      float v[64];
+      const bool ok = tg < ng;
+      if (ok) {
 #pragma unroll
-      for (int t = 0; t < DEC_TT; ++t) {
-        const int m = sh->unit_m[u][t];
-        tokc[t] = m >= 0 ? m / a.topk : -1;
-        if (m >= 0) {
-          const float* ip = inter + (size_t)m * I;
-          wsc[t] = a.topk_w[m] * load_rotated<GPL>([&](int k) { return ip[k]; }, ng, xa[t]);
-        } else {
-          wsc[t] = 0.f;
-#pragma unroll
-          for (int q = 0; q < GPL; ++q)
-#pragma unroll
-            for (int i = 0; i < 32; ++i) xa[t][q][i] = 0u;
+        for (int k4 = 0; k4 < 16; ++k4) {
+          const float4 f = *(const float4*)&sh->scratch[tg * 64 + 4 * k4];
+          v[4 * k4] = f.x; v[4 * k4 + 1] = f.y; v[4 * k4 + 2] = f.z; v[4 * k4 + 3] = f.w;
         }
       }
+      stage_activation(v, ok, tg, sh);
+      load_xs(sh, g, gv, xr[0]);
+      wsc = a.topk_w[m] * sh->slice_inv[h];
+      if (threadIdx.x == 0 && c == 0) PROBE(1, 5);
     }
     if (!mbar_wait(&sh->full[slot], (c / DEC_STAGES) & 1)) break;
-    const uint8_t* st = stages + slot * stage_b;
-    for (int rr = warp; rr < n; rr += DEC_NW) {
-      float d[DEC_TT] = {};
-#pragma unroll
-      for (int q = 0; q < GPL; ++q) {
-        const int gi = lane + 32 * q;
-        if (gi < ng) {
-          float ad[DEC_TT] = {};
-          const uint4 lo = *(const uint4*)(st + rr * nsub + gi * 16);
-          const uint32_t hw = *(const uint32_t*)(st + lo_b + rr * (nsub / 4) + gi * 4);
-          const float sc = __half2float(*(const __half*)(st + lo_b + hi_b + (rr * ng + gi) * 2));
-          uint32_t xt[DEC_TT][32];
-#pragma unroll
-          for (int t = 0; t < DEC_TT; ++t)
-#pragma unroll
-            for (int i = 0; i < 32; ++i) xt[t][i] = xa[t][q][i];
-          group_dot<DEC_TT>(lo, hw, cb_lane, xt, ad);
-#pragma unroll
-          for (int t = 0; t < DEC_TT; ++t) d[t] += ad[t] * sc;
-        }
-      }
-#pragma unroll
-      for (int t = 0; t < DEC_TT; ++t) {
-        const float ds = warp_sum(d[t]);
-        if (lane == 0 && tokc[t] >= 0) atomicAdd(&a.out[(size_t)tokc[t] * H + h0 + rr], ds * wsc[t]);
-      }
+    if (threadIdx.x == 0 && c == 0) PROBE(1, 3);
+    const uint8_t* st = d.stages + slot * stage_b;
+    if (S / rstep >= 8) {
+      for (int rr0 = rsub; rr0 < n; rr0 += 8 * rstep)
+        down_rows<8>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, tok, H, h0, a.out);
+    } else {
+      for (int rr0 = rsub; rr0 < n; rr0 += 4 * rstep)
+        down_rows<4>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, tok, H, h0, a.out);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&sh->empty[slot]);
     ++c;
   }
+  if (threadIdx.x == 0) PROBE(1, 4);
 }
 
-static size_t decode_smem_bytes(int S_rows_bytes) {
-  return CB_BYTES + ((sizeof(DecodeShared) + 127) / 128) * 128 + (size_t)DEC_STAGES * S_rows_bytes;
+static size_t decode_smem_bytes(size_t stage_bytes) {
+  return CB_BYTES + ((sizeof(DecodeShared) + 127) / 128) * 128 + (size_t)DEC_STAGES * stage_bytes;
 }
 
 static bool aligned16(const void* p) { return ((uintptr_t)p & 15) == 0; }
+
+struct DecodeLaunchCache {
+  int nsm = 0;
+  bool attr_set = false;
+};
+static DecodeLaunchCache g_dec_cache[64];
 
 }  // namespace vq2
 
 using namespace vq2;
 
+#ifdef VQ2_DEC_PROBE
+extern "C" int vq2_probe_read(void* host) {
+  return (int)cudaMemcpyFromSymbol(host, g_probe, sizeof(g_probe));
+}
+#endif
+
+static int khA_of(int H) { return (H / 64 + 31) / 32; }
+
 extern "C" size_t vq2_decode_workspace_size(int N, int topk, int H, int I) {
-  (void)H;
-  return (size_t)N * topk * I * sizeof(float) + 256;
+  return (size_t)N * topk * khA_of(H) * 2 * I * sizeof(float) + 256;
 }
 
 extern "C" int vq2_decode(const vq2_moe_args* a, void* ws, size_t ws_bytes, void* stream) {
@@ -450,38 +656,48 @@ extern "C" int vq2_decode(const vq2_moe_args* a, void* ws, size_t ws_bytes, void
     return VQ2_ERR_SHAPE;
   if ((long)a->N * a->topk > VQ2_DECODE_MAX_PAIRS) return VQ2_ERR_TOO_MANY_PAIRS;
   if (a->x_dtype < 0 || a->x_dtype > 2 || a->ids_dtype < 0 || a->ids_dtype > 1) return VQ2_ERR_DTYPE;
-  const void* ptrs[] = {a->w13_lo, a->w13_hi, a->w13_sc, a->w2_lo, a->w2_hi, a->w2_sc, a->w13_cb, a->w2_cb};
+  const void* ptrs[] = {a->x, a->w13_lo, a->w13_hi, a->w13_sc, a->w2_lo, a->w2_hi, a->w2_sc, a->w13_cb, a->w2_cb};
   for (const void* p : ptrs)
     if (!aligned16(p)) return VQ2_ERR_ALIGN;
   if (!ws || ws_bytes < vq2_decode_workspace_size(a->N, a->topk, a->H, a->I)) return VQ2_ERR_WORKSPACE;
-  float* inter = (float*)(((uintptr_t)ws + 255) & ~(uintptr_t)255);
+  float* part = (float*)(((uintptr_t)ws + 255) & ~(uintptr_t)255);
 
-  int dev = 0, nsm = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess) return VQ2_ERR_NO_DEVICE;
-  if (cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return VQ2_ERR_CUDA;
-  cudaStream_t st = (cudaStream_t)stream;
-
-  const int gplA = (a->H / 64 + 31) / 32, gplB = (a->I / 64 + 31) / 32;
-  const size_t smA = decode_smem_bytes(8 * 2 * (a->H / 4 + a->H / 16 + a->H / 32));
-  const size_t smB = decode_smem_bytes(32 * (a->I / 4 + a->I / 16 + a->I / 32));
-  void (*ka)(vq2_moe_args, float*) = gplA == 1 ? decode_gateup_kernel<1> : decode_gateup_kernel<2>;
-  void (*kb)(vq2_moe_args, const float*) = gplB == 1 ? decode_down_kernel<1> : decode_down_kernel<2>;
-  if (cudaFuncSetAttribute(ka, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smA) != cudaSuccess) return VQ2_ERR_CUDA;
-  if (cudaFuncSetAttribute(kb, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smB) != cudaSuccess) return VQ2_ERR_CUDA;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VQ2_ERR_NO_DEVICE;
+  DecodeLaunchCache& lc = g_dec_cache[dev];
+  // smem sized for the largest supported rows (H, I <= 4096)
+  const size_t smA = decode_smem_bytes((size_t)DEC_SA * 2 * (4096 / 4 + 4096 / 16 + 4096 / 32));
+  const size_t smB = decode_smem_bytes((size_t)DEC_SB * (4096 / 4 + 4096 / 16 + 4096 / 32) / 2);
+  if (!lc.attr_set) {
+    if (cudaDeviceGetAttribute(&lc.nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return VQ2_ERR_CUDA;
+    bool ok = true;
+    ok &= cudaFuncSetAttribute(decode_gateup_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smA) == cudaSuccess;
+    ok &= cudaFuncSetAttribute(decode_gateup_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smA) == cudaSuccess;
+    ok &= cudaFuncSetAttribute(decode_down_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smB) == cudaSuccess;
+    ok &= cudaFuncSetAttribute(decode_down_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smB) == cudaSuccess;
+    if (!ok) return VQ2_ERR_CUDA;
+    lc.attr_set = true;
+  }
+  const int khA = khA_of(a->H), khB = (a->I / 64 + 31) / 32;
+  void (*ka)(vq2_moe_args, float*) = khA == 1 ? decode_gateup_kernel<1> : decode_gateup_kernel<2>;
+  void (*kb)(vq2_moe_args, const float*, int) = khB == 1 ? decode_down_kernel<1> : decode_down_kernel<2>;
 
   vq2_moe_args args = *a;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(nsm);
+  cfg.gridDim = dim3(lc.nsm);
   cfg.blockDim = dim3(DEC_THREADS);
   cfg.dynamicSmemBytes = smA;
-  cfg.stream = st;
-  if (cudaLaunchKernelEx(&cfg, ka, args, inter) != cudaSuccess) return VQ2_ERR_CUDA;
+  cfg.stream = (cudaStream_t)stream;
+  if (cudaLaunchKernelEx(&cfg, ka, args, part) != cudaSuccess) return VQ2_ERR_CUDA;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.dynamicSmemBytes = smB;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kb, args, (const float*)inter) != cudaSuccess) return VQ2_ERR_CUDA;
+  if (cudaLaunchKernelEx(&cfg, kb, args, (const float*)part, khA) != cudaSuccess) return VQ2_ERR_CUDA;
   return VQ2_OK;
 }
+
+static_assert(offsetof(vq2::DecodeShared, xs) % 16 == 0, "xs must be 16-byte aligned");
+static_assert(offsetof(vq2::DecodeShared, scratch) % 16 == 0, "bulk-copy destination must be 16-byte aligned");

@@ -11,7 +11,7 @@ import os
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(os.path.dirname(_HERE), "libvq2_b200.so")
+LIB_PATH = os.environ.get("VQ2_LIB") or os.path.join(os.path.dirname(_HERE), "libvq2_b200.so")
 
 DT = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
 ID = {torch.int32: 0, torch.int64: 1}
