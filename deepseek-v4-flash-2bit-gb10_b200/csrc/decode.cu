@@ -701,3 +701,31 @@ extern "C" int vq2_decode(const vq2_moe_args* a, void* ws, size_t ws_bytes, void
 
 static_assert(offsetof(vq2::DecodeShared, xs) % 16 == 0, "xs must be 16-byte aligned");
 static_assert(offsetof(vq2::DecodeShared, scratch) % 16 == 0, "bulk-copy destination must be 16-byte aligned");
+
+// ------------------------------------------------------------------ allocation-free decode
+// For callers that cannot allocate device memory at call time — for example code running under a
+// memory pool that forbids new allocations, inside a driver callback, or in a host runtime that
+// has no CUDA allocator of its own — this variant takes its gate/up scratch from a fixed array
+// compiled into the library instead of a caller workspace. Every GPU that loads the library keeps
+// VQ2_NOALLOC_SCRATCH_BYTES reserved for it until the process exits.
+static __device__ __align__(256) unsigned char g_noalloc_scratch[VQ2_NOALLOC_SCRATCH_BYTES];
+static void* g_noalloc_ptr[64];   // device address of the array, looked up once per device
+
+extern "C" int vq2_decode_noalloc(const vq2_moe_args* a, void* stream) {
+  if (!a) return VQ2_ERR_NULL;
+  if (a->N <= 0 || a->topk <= 0 || a->H <= 0 || a->I <= 0) return VQ2_ERR_SHAPE;
+  // the scratch this call needs: fp32 gate/up partials per (pair, K-slice)
+  const size_t need = vq2_decode_workspace_size(a->N, a->topk, a->H, a->I) - 256;
+  if (need > (size_t)VQ2_NOALLOC_SCRATCH_BYTES) return VQ2_ERR_NOALLOC_LIMIT;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VQ2_ERR_NO_DEVICE;
+  if (!g_noalloc_ptr[dev]) {
+    // The array's host-side name is not a device address; ask the runtime for this device's.
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || !p) return VQ2_ERR_CUDA;
+    g_noalloc_ptr[dev] = p;
+  }
+  // The partials are fully rewritten before they are read, so nothing needs clearing; the
+  // 256-aligned array start means the workspace's alignment slack is not used.
+  return vq2_decode(a, g_noalloc_ptr[dev], vq2_decode_workspace_size(a->N, a->topk, a->H, a->I), stream);
+}

@@ -125,6 +125,7 @@ extern "C" const char* vq2_strerror(int code) {
     case VQ2_ERR_CUDA: return "vq2: CUDA runtime call failed";
     case VQ2_ERR_TIMEOUT: return "vq2: a bounded device wait timed out";
     case VQ2_ERR_NO_DEVICE: return "vq2: no CUDA device";
+    case VQ2_ERR_NOALLOC_LIMIT: return "vq2: vq2_decode_noalloc needs more scratch than VQ2_NOALLOC_SCRATCH_BYTES (2 MiB); use vq2_decode with a workspace";
     default: return "vq2: unknown error";
   }
 }

@@ -34,7 +34,8 @@ enum {
   VQ2_ERR_TOO_MANY_PAIRS = 6,/* decode path: N*topk above VQ2_DECODE_MAX_PAIRS */
   VQ2_ERR_CUDA = 7,          /* a CUDA runtime call failed (launch / attribute) */
   VQ2_ERR_TIMEOUT = 8,       /* a bounded device wait gave up (reported by vq2_device_status) */
-  VQ2_ERR_NO_DEVICE = 9      /* no sm_100 device is current */
+  VQ2_ERR_NO_DEVICE = 9,     /* no sm_100 device is current */
+  VQ2_ERR_NOALLOC_LIMIT = 10 /* vq2_decode_noalloc: the call needs more scratch than its fixed array */
 };
 
 enum { VQ2_DT_BF16 = 0, VQ2_DT_F16 = 1, VQ2_DT_F32 = 2 };   /* activation dtypes */
@@ -67,6 +68,19 @@ typedef struct vq2_moe_args {
  * capture in a CUDA graph. Requires N*topk <= VQ2_DECODE_MAX_PAIRS. */
 size_t vq2_decode_workspace_size(int N, int topk, int H, int I);
 int vq2_decode(const vq2_moe_args* a, void* workspace, size_t ws_bytes, void* stream);
+
+/* Allocation-free decode: no counterpart in the reference. For callers that cannot allocate
+ * device memory when they call (a memory pool that forbids new allocations, a driver callback, a
+ * host runtime without a CUDA allocator): same result as vq2_decode, but the gate/up scratch is a
+ * fixed array inside the library (VQ2_NOALLOC_SCRATCH_BYTES, reserved on every GPU that loads the
+ * library until the process exits) instead of a caller workspace. The call allocates nothing.
+ * Limit: N*topk*ceil(H/2048)*2*I*4 bytes <= VQ2_NOALLOC_SCRATCH_BYTES, else VQ2_ERR_NOALLOC_LIMIT
+ * (2 MiB: 64 token-expert pairs at H=4096, I=2048, i.e. 8 decode tokens at top-8).
+ * The first call on a device looks up the array's device address (cudaGetSymbolAddress) with that
+ * device current; make that first call before any stream capture. All calls share the array:
+ * calls that overlap on the GPU (other streams, other threads) race and corrupt each other. */
+#define VQ2_NOALLOC_SCRATCH_BYTES (2u << 20)
+int vq2_decode_noalloc(const vq2_moe_args* a, void* stream);
 
 /* Prefill MoE (grouped GEMM on tcgen05 tensor cores). Replaces ds4_vq2_cuda.vq2_moe_grouped_wmma
  * (reference vq2_vllm/kernels/ds4_vq2_cuda.py:72-111). precision = VQ2_PREC_FP8 follows the
