@@ -16,12 +16,24 @@ constexpr int ALIGN_MAX_E = 1024;
 
 __device__ __forceinline__ int clamp_e(int e, int E) { return e < 0 ? 0 : (e >= E ? E - 1 : e); }
 
+// Local expert of a pair: id - base, clamped into [0, E) (reference semantics) or, with drop,
+// -1 for ids outside [base, base + E) (expert parallelism: pairs owned by another device).
+__device__ __forceinline__ int map_e(int id, int E, int base, int drop) {
+  const int e = id - base;
+  if (drop) return (e >= 0 && e < E) ? e : -1;
+  return clamp_e(e, E);
+}
+
 // histogram of one chunk -> counts[chunk][E]
-__device__ void align_count_chunk(const void* ids, int dt, long M, int E, int chunk, int* counts, int* sh_cnt) {
+__device__ void align_count_chunk(const void* ids, int dt, long M, int E, int base, int drop, int chunk, int* counts,
+                                  int* sh_cnt) {
   for (int e = threadIdx.x; e < E; e += blockDim.x) sh_cnt[e] = 0;
   __syncthreads();
   const long b = (long)chunk * ALIGN_CHUNK, end = min(M, b + ALIGN_CHUNK);
-  for (long m = b + threadIdx.x; m < end; m += blockDim.x) atomicAdd(&sh_cnt[clamp_e(load_id(ids, dt, m), E)], 1);
+  for (long m = b + threadIdx.x; m < end; m += blockDim.x) {
+    const int e = map_e(load_id(ids, dt, m), E, base, drop);
+    if (e >= 0) atomicAdd(&sh_cnt[e], 1);
+  }
   __syncthreads();
   for (int e = threadIdx.x; e < E; e += blockDim.x) counts[(long)chunk * E + e] = sh_cnt[e];
   __syncthreads();
@@ -74,7 +86,8 @@ __device__ void align_scan(int nchunks, int E, int BM, long Pmax, int* counts, i
 }
 
 // stable placement of one chunk: rounds of blockDim pairs, in pair order
-__device__ void align_place_chunk(const void* ids, int dt, long M, int k, int E, int chunk, const int* base,
+__device__ void align_place_chunk(const void* ids, int dt, long M, int k, int E, int ebase, int drop, int chunk,
+                                  const int* base,
                                   int32_t* st, int32_t* ss, uint8_t* val, int* sh_run, int* sh_wc) {
   const int nw = blockDim.x / 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int e = threadIdx.x; e < E; e += blockDim.x) sh_run[e] = base[(long)chunk * E + e];
@@ -82,8 +95,9 @@ __device__ void align_place_chunk(const void* ids, int dt, long M, int k, int E,
   const long b = (long)chunk * ALIGN_CHUNK, end = min(M, b + ALIGN_CHUNK);
   for (long r0 = b; r0 < end; r0 += blockDim.x) {
     const long m = r0 + threadIdx.x;
-    const bool act = m < end;
-    const int e = act ? clamp_e(load_id(ids, dt, m), E) : -1 - lane;   // inactive lanes: unique keys
+    const int e0 = m < end ? map_e(load_id(ids, dt, m), E, ebase, drop) : -1;
+    const bool act = e0 >= 0;
+    const int e = act ? e0 : -1 - lane;   // inactive / dropped lanes: unique keys
     const unsigned peers = __match_any_sync(0xffffffffu, e);
     const int lrank = __popc(peers & ((1u << lane) - 1));
     const bool leader = lrank == 0;
@@ -114,7 +128,7 @@ __device__ void zero_outputs(long Pmax, int32_t* st, int32_t* ss, uint8_t* val) 
 }
 
 struct AlignArgs {
-  const void* ids; int dt; long M; int k; int E; int BM; long Pmax; int nchunks;
+  const void* ids; int dt; long M; int k; int E; int BM; int base; int drop; long Pmax; int nchunks;
   int32_t* st; int32_t* ss; uint8_t* val; int32_t* be; int* counts;
 };
 
@@ -123,15 +137,15 @@ __global__ void __launch_bounds__(ALIGN_THREADS) align_single_kernel(AlignArgs a
   extern __shared__ int sh_wc[];          // [nwarps][E]
   zero_outputs(a.Pmax, a.st, a.ss, a.val);
   for (int i = threadIdx.x; i < (blockDim.x / 32) * a.E; i += blockDim.x) sh_wc[i] = 0;
-  align_count_chunk(a.ids, a.dt, a.M, a.E, 0, a.counts, sh_a);
+  align_count_chunk(a.ids, a.dt, a.M, a.E, a.base, a.drop, 0, a.counts, sh_a);
   align_scan(1, a.E, a.BM, a.Pmax, a.counts, a.be, sh_a);
-  align_place_chunk(a.ids, a.dt, a.M, a.k, a.E, 0, a.counts, a.st, a.ss, a.val, sh_a, sh_wc);
+  align_place_chunk(a.ids, a.dt, a.M, a.k, a.E, a.base, a.drop, 0, a.counts, a.st, a.ss, a.val, sh_a, sh_wc);
 }
 
 __global__ void __launch_bounds__(ALIGN_THREADS) align_count_kernel(AlignArgs a) {
   __shared__ int sh_a[ALIGN_MAX_E];
   zero_outputs(a.Pmax, a.st, a.ss, a.val);
-  align_count_chunk(a.ids, a.dt, a.M, a.E, blockIdx.x, a.counts, sh_a);
+  align_count_chunk(a.ids, a.dt, a.M, a.E, a.base, a.drop, blockIdx.x, a.counts, sh_a);
 }
 
 __global__ void __launch_bounds__(ALIGN_THREADS) align_scan_kernel(AlignArgs a) {
@@ -144,14 +158,14 @@ __global__ void __launch_bounds__(ALIGN_THREADS) align_place_kernel(AlignArgs a)
   extern __shared__ int sh_wc[];
   for (int i = threadIdx.x; i < (blockDim.x / 32) * a.E; i += blockDim.x) sh_wc[i] = 0;
   __syncthreads();
-  align_place_chunk(a.ids, a.dt, a.M, a.k, a.E, blockIdx.x, a.counts, a.st, a.ss, a.val, sh_a, sh_wc);
+  align_place_chunk(a.ids, a.dt, a.M, a.k, a.E, a.base, a.drop, blockIdx.x, a.counts, a.st, a.ss, a.val, sh_a, sh_wc);
 }
 
 // Host-side launcher shared with the prefill path. `counts` needs nchunks*E ints.
-int launch_align(const void* ids, int dt, long N, int k, int E, int BM, int32_t* st, int32_t* ss,
-                 uint8_t* val, int32_t* be, int* counts, cudaStream_t stream) {
+int launch_align_ex(const void* ids, int dt, long N, int k, int E, int BM, int base, int drop, int32_t* st,
+                    int32_t* ss, uint8_t* val, int32_t* be, int* counts, cudaStream_t stream) {
   AlignArgs a;
-  a.ids = ids; a.dt = dt; a.M = N * k; a.k = k; a.E = E; a.BM = BM;
+  a.ids = ids; a.dt = dt; a.M = N * k; a.k = k; a.E = E; a.BM = BM; a.base = base; a.drop = drop;
   a.Pmax = a.M + (long)min(a.M, (long)E) * BM;
   a.nchunks = (int)((a.M + ALIGN_CHUNK - 1) / ALIGN_CHUNK);
   a.st = st; a.ss = ss; a.val = val; a.be = be; a.counts = counts;
@@ -170,6 +184,11 @@ int launch_align(const void* ids, int dt, long N, int k, int E, int BM, int32_t*
     align_place_kernel<<<a.nchunks, threads, wc, stream>>>(a);
   }
   return cudaGetLastError() == cudaSuccess ? VQ2_OK : VQ2_ERR_CUDA;
+}
+
+int launch_align(const void* ids, int dt, long N, int k, int E, int BM, int32_t* st, int32_t* ss,
+                 uint8_t* val, int32_t* be, int* counts, cudaStream_t stream) {
+  return launch_align_ex(ids, dt, N, k, E, BM, 0, 0, st, ss, val, be, counts, stream);
 }
 
 }  // namespace vq2

@@ -1,0 +1,530 @@
+// K2 — prefill MoE: grouped GEMMs on the 5th-generation tensor cores (tcgen05 + TMEM)
+// (replaces ds4_vq2_cuda.vq2_moe_grouped_wmma, reference vq2_vllm/kernels/ds4_vq2_cuda.py:72-111,
+// whose device kernels are vq2_vllm/kernels/vq2_grouped.cu:383-581).
+//
+// Pipeline of one call (all on the caller's stream, no host sync):
+//   align      pairs grouped by expert, each expert padded to 128 slots (csrc/align.cu)
+//   act_quant  x -> Hadamard -> per-token quantised activation (fp8 e4m3 with s = 448/amax, as the
+//              reference's quant_fp8_rows; or fp16 with a power-of-two range scale)
+//   gateup     per (128-slot block, 64 gate + 64 matching up rows): D = A . B^T in TMEM, epilogue
+//              inter = silu(g * inv_x) * (u * inv_x)   (reference vq2_grouped.cu:255-264 fused)
+//   vb_quant   inter -> Hadamard -> per-slot quantised activation (+ inv)
+//   down       per (block, 128 output rows): D = vb . Wd^T; epilogue out[tok] += D * w * inv_vb
+//
+// GEMM CTA (one per SM, 320 threads): warp 0 allocates TMEM and gathers the activation tile rows
+// with cp.async into the 128-byte-swizzled K-major layout; warp 1 lane 0 issues tcgen05.mma
+// (M=128, N=128, K=32 fp8 / K=16 f16 per instruction) into a 128-column fp32 TMEM accumulator;
+// warps 2..9 decode the VQ weight tile (10-bit index -> fp16 codebook vector x fp16 group scale
+// -> e4m3 / f16) straight into the swizzled B tile, then run the epilogue out of TMEM.
+// A 3-stage ring of (A, B) tiles is synchronised with mbarriers; tcgen05.commit frees a stage.
+#include <cuda_fp8.h>
+#include <algorithm>
+#include "vq2_common.cuh"
+
+namespace vq2 {
+
+int launch_align_ex(const void* ids, int dt, long N, int k, int E, int BM, int base, int drop, int32_t* st,
+                    int32_t* ss, uint8_t* val, int32_t* be, int* counts, cudaStream_t stream);
+
+constexpr int PF_BM = 128;            // slots per block (MMA M)
+constexpr int PF_BN = 128;            // weight rows per tile (MMA N)
+constexpr int PF_STAGES = 3;
+constexpr int PF_DEC_WARPS = 8;
+constexpr int PF_THREADS = (2 + PF_DEC_WARPS) * 32;
+constexpr int PF_TILE = 16384;        // one 128 x 128-byte operand tile
+constexpr int PF_CB_BYTES = 1024 * 8 * 16;
+constexpr int PF_TMEM_COLS = 128;
+
+struct PfShared {
+  uint64_t full_a[PF_STAGES];
+  uint64_t full_b[PF_STAGES];
+  uint64_t empty[PF_STAGES];
+  uint64_t done;
+  uint32_t tmem_base;
+  int slot_tok[PF_BM];
+};
+
+constexpr size_t PF_SMEM = (size_t)PF_CB_BYTES + 2 * PF_STAGES * PF_TILE + sizeof(PfShared) + 1024;
+
+struct PfGemmArgs {
+  const uint8_t* act;        // activation rows (token rows for gate/up, slot rows for down)
+  const float* inv_act;      // per activation row: inverse quantisation scale
+  const int32_t* st;         // sorted_tok [Pmax]
+  const int32_t* ss;         // sorted_slot [Pmax]
+  const uint8_t* val;        // valid [Pmax]
+  const int32_t* be;         // block -> local expert
+  const uint8_t* lo;
+  const uint8_t* hi;
+  const uint16_t* sc;
+  const uint16_t* cb;
+  const float* topk_w;
+  float* inter;              // gate/up output [Pmax, I]
+  float* out;                // down output [N, H]
+  int K;                     // input width (elements)
+  int R;                     // weight rows per expert (2I or H)
+  int I;
+  int H;
+  int topk;
+};
+
+// ------------------------------------------------------------------ tcgen05 helpers
+// Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 B apart (stride
+// byte offset), leading byte offset unused for this layout (1), descriptor version 1 (sm_100).
+__device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor: D fp32, A/B format 0 (e4m3 for kind::f8f6f4, f16 for kind::f16),
+// both K-major, N = 128, M = 128.
+constexpr uint32_t PF_IDESC = (1u << 4) | ((uint32_t)(PF_BN >> 3) << 17) | ((uint32_t)(PF_BM >> 4) << 24);
+
+template <int PREC>
+__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t acc) {
+  if (PREC == VQ2_PREC_FP8)
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                 " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}"
+                 ::"r"(tmem_d), "l"(da), "l"(db), "r"(PF_IDESC), "r"(acc));
+  else
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                 " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
+                 ::"r"(tmem_d), "l"(da), "l"(db), "r"(PF_IDESC), "r"(acc));
+}
+
+__device__ __forceinline__ void umma_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];"
+               ::"r"(smem_u32(bar)) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void fence_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  uint32_t r[32];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,"
+               "%16,%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                 "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]),
+                 "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]),
+                 "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]),
+                 "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
+}
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool ok) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+// byte offset of 16-byte chunk kc of row r in a 128 x 128-byte SW128 K-major tile
+__device__ __forceinline__ uint32_t sw128_off(int r, int kc) {
+  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((kc ^ (r & 7)) << 4));
+}
+
+// ------------------------------------------------------------------ weight tile decode
+// Decode 16-byte chunks [4h, 4h+4) of B row r of one stage:
+// fp8: 16 sub-vectors (one 64-group) -> 64 e4m3 values = e4m3(sat(C[id] * sc)) (reference
+//      vq2_grouped.cu:434-446); f16: 8 sub-vectors -> 32 f16 values C[id] * sc.
+template <int PREC>
+__device__ __forceinline__ void decode_b_row(const uint8_t* cbl, uint4 lo, uint32_t hw, float scf, uint8_t* tile,
+                                             int r, int h) {
+  if (PREC == VQ2_PREC_FP8) {
+    const uint32_t lw[4] = {lo.x, lo.y, lo.z, lo.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      uint32_t packed[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t off = (((lw[q] >> (8 * j)) & 0xFFu) << 7) | (((hw >> (8 * q + 2 * j)) & 3u) << 15);
+        const uint2 c = *(const uint2*)(cbl + off);
+        const float2 a = __half22float2(*(const __half2*)&c.x), b = __half22float2(*(const __half2*)&c.y);
+        const __nv_fp8x2_storage_t p0 = __nv_cvt_float2_to_fp8x2(make_float2(a.x * scf, a.y * scf), __NV_SATFINITE, __NV_E4M3);
+        const __nv_fp8x2_storage_t p1 = __nv_cvt_float2_to_fp8x2(make_float2(b.x * scf, b.y * scf), __NV_SATFINITE, __NV_E4M3);
+        packed[j] = (uint32_t)p0 | ((uint32_t)p1 << 16);
+      }
+      *(uint4*)(tile + sw128_off(r, 4 * h + q)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    }
+  } else {
+    const __half2 s2 = __float2half2_rn(scf);
+    const uint32_t lw[2] = {lo.x, lo.y};
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {         // chunk q: sub-vectors 2q, 2q+1 (8 f16)
+      uint32_t w[4];
+#pragma unroll
+      for (int j = 0; j < 2; ++j) {
+        const int s = 2 * q + j;
+        const uint32_t off = (((lw[s >> 2] >> (8 * (s & 3))) & 0xFFu) << 7) | (((hw >> (2 * s)) & 3u) << 15);
+        const uint2 c = *(const uint2*)(cbl + off);
+        const __half2 v0 = __hmul2(*(const __half2*)&c.x, s2), v1 = __hmul2(*(const __half2*)&c.y, s2);
+        w[2 * j] = *(const uint32_t*)&v0;
+        w[2 * j + 1] = *(const uint32_t*)&v1;
+      }
+      *(uint4*)(tile + sw128_off(r, 4 * h + q)) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+  }
+}
+
+// ------------------------------------------------------------------ grouped GEMM kernel
+// grid (tiles along N, blocks of 128 slots). GATEUP: tile n covers gate rows [64n, 64n+64) and
+// the matching up rows; the epilogue writes inter. Otherwise tile n covers output rows
+// [128n, 128n+128) and the epilogue accumulates into out.
+template <int PREC, bool GATEUP>
+__global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(PfGemmArgs a) {
+  extern __shared__ __align__(1024) uint8_t pf_smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)pf_smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* cbs = smem;
+  uint8_t* tiles = smem + PF_CB_BYTES;                 // A0 B0 A1 B1 A2 B2
+  PfShared* sh = (PfShared*)(tiles + 2 * PF_STAGES * PF_TILE);
+  const int blk = blockIdx.y, tile = blockIdx.x;
+  if (!a.val[(size_t)blk * PF_BM]) return;           // blocks past the last expert hold no pair
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int e = a.be[blk];
+  const int elem = PREC == VQ2_PREC_FP8 ? 1 : 2;
+  const int KE = 128 / elem;                          // K elements per stage (128 bytes per row)
+  const int nchunks = a.K / KE;
+  const int nsub = a.K / 4, ngk = a.K / 64;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < PF_STAGES; ++s) {
+      mbar_init(&sh->full_a[s], 32);
+      mbar_init(&sh->full_b[s], PF_DEC_WARPS);
+      mbar_init(&sh->empty[s], 1);
+    }
+    mbar_init(&sh->done, 1);
+    fence_mbar_init();
+  }
+  for (int i = threadIdx.x; i < PF_BM; i += blockDim.x) {
+    const size_t p = (size_t)blk * PF_BM + i;
+    sh->slot_tok[i] = a.val[p] ? a.st[p] : -1;
+  }
+  {  // codebook replicated 16x (entry e of copy c at e*128 + c*8), consecutive 16-byte stores
+    const uint2* src = (const uint2*)a.cb;
+    for (int idx = threadIdx.x; idx < 1024 * 8; idx += blockDim.x) {
+      const uint2 v = src[idx >> 3];
+      *(uint4*)(cbs + (idx >> 3) * 128 + (idx & 7) * 16) = make_uint4(v.x, v.y, v.x, v.y);
+    }
+  }
+  if (warp == 0) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+                 ::"r"(smem_u32(&sh->tmem_base)), "r"(PF_TMEM_COLS) : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sh->tmem_base;
+
+  if (warp == 0) {
+    // ---------------- activation tile loader: 128 rows x 128 bytes per stage, 32 chunks per lane
+    int issued = 0;
+    for (int c = 0; c < nchunks; ++c) {
+      const int slot = c % PF_STAGES;
+      if (c >= PF_STAGES && !mbar_wait(&sh->empty[slot], ((c / PF_STAGES) - 1) & 1)) break;
+      const uint32_t abase = smem_u32(tiles + 2 * slot * PF_TILE);
+#pragma unroll 8
+      for (int i = 0; i < 32; ++i) {
+        const int id = i * 32 + lane, r = id >> 3, kc = id & 7;
+        int row;
+        bool ok;
+        if (GATEUP) { row = sh->slot_tok[r]; ok = row >= 0; if (!ok) row = 0; }
+        else { row = blk * PF_BM + r; ok = true; }
+        const uint8_t* src = a.act + (size_t)row * a.K * elem + (size_t)c * 128 + kc * 16;
+        cp_async16(abase + sw128_off(r, kc), src, ok);
+      }
+      cp_async_commit();
+      ++issued;
+      if (c >= 1) {
+        cp_async_wait<1>();
+        fence_async_smem();
+        mbar_arrive(&sh->full_a[(c - 1) % PF_STAGES]);
+      }
+    }
+    cp_async_wait<0>();
+    fence_async_smem();
+    if (issued >= 1) mbar_arrive(&sh->full_a[(issued - 1) % PF_STAGES]);
+  } else if (warp == 1) {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      for (int c = 0; c < nchunks; ++c) {
+        const int slot = c % PF_STAGES;
+        const uint32_t par = (c / PF_STAGES) & 1;
+        if (!mbar_wait(&sh->full_a[slot], par) || !mbar_wait(&sh->full_b[slot], par)) break;
+        tc_fence_after();
+        const uint32_t abase = smem_u32(tiles + 2 * slot * PF_TILE), bbase = abase + PF_TILE;
+#pragma unroll
+        for (int ks = 0; ks < 4; ++ks)
+          umma<PREC>(tmem, umma_desc_sw128(abase + ks * 32), umma_desc_sw128(bbase + ks * 32), (c | ks) != 0);
+        umma_commit(&sh->empty[slot]);
+      }
+      umma_commit(&sh->done);   // arrives once every MMA issued above has completed
+    }
+  } else {
+    // ---------------- weight decoders (256 threads: row r, half h of the 128-byte row)
+    const int dt = threadIdx.x - 64, r = dt & 127, h = dt >> 7;
+    const uint8_t* cbl = cbs + (lane & 15) * 8;
+    long wrow;
+    if (GATEUP) wrow = (long)e * a.R + (r < 64 ? tile * 64 + r : a.I + tile * 64 + (r - 64));
+    else wrow = (long)e * a.R + tile * PF_BN + r;
+    const uint8_t* lo_row = a.lo + wrow * nsub;
+    const uint8_t* hi_row = a.hi + wrow * (nsub / 4);
+    const uint16_t* sc_row = a.sc + wrow * ngk;
+    for (int c = 0; c < nchunks; ++c) {
+      const int slot = c % PF_STAGES;
+      const int s0 = (c * KE + h * (KE / 2)) / 4;      // first sub-vector of this thread
+      uint4 lo;
+      uint32_t hw;
+      if (PREC == VQ2_PREC_FP8) {
+        lo = *(const uint4*)(lo_row + s0);
+        hw = *(const uint32_t*)(hi_row + s0 / 4);
+      } else {
+        const uint2 l2 = *(const uint2*)(lo_row + s0);
+        lo = make_uint4(l2.x, l2.y, 0, 0);
+        hw = *(const uint16_t*)(hi_row + s0 / 4);
+      }
+      const float scf = __half2float(__ushort_as_half(sc_row[(s0 * 4) / 64]));
+      if (c >= PF_STAGES && !mbar_wait(&sh->empty[slot], ((c / PF_STAGES) - 1) & 1)) break;
+      decode_b_row<PREC>(cbl, lo, hw, scf, tiles + (2 * slot + 1) * PF_TILE, r, h);
+      fence_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->full_b[slot]);
+    }
+    // ---------------- epilogue out of TMEM
+    const int q = warp & 3, ch = (warp - 2) >> 2;       // TMEM lane quarter, column half
+    const int slot_i = q * 32 + lane;
+    const int tok = sh->slot_tok[slot_i];
+    const size_t p = (size_t)blk * PF_BM + slot_i;
+    if (mbar_wait(&sh->done, 0)) {
+      tc_fence_after();
+      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
+      if (GATEUP) {
+        float g[32], u[32];
+        tmem_ld32(trow + ch * 32, g);
+        tmem_ld32(trow + 64 + ch * 32, u);
+        const float inv = tok >= 0 ? a.inv_act[tok] : 0.f;
+        float* dst = a.inter + p * a.I + tile * 64 + ch * 32;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          float rr[4];
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            const float gg = g[j + t] * inv, uu = u[j + t] * inv;
+            rr[t] = gg / (1.f + __expf(-gg)) * uu;
+          }
+          *(float4*)(dst + j) = make_float4(rr[0], rr[1], rr[2], rr[3]);
+        }
+      } else {
+        float v[64];
+        tmem_ld32(trow + ch * 64, v);
+        tmem_ld32(trow + ch * 64 + 32, v + 32);
+        if (tok >= 0) {
+          const float w = a.topk_w[(size_t)tok * a.topk + a.ss[p]] * a.inv_act[p];
+          float* dst = a.out + (size_t)tok * a.H + tile * PF_BN + ch * 64;
+#pragma unroll
+          for (int j = 0; j < 64; j += 4)
+            atomicAdd((float4*)(dst + j), make_float4(v[j] * w, v[j + 1] * w, v[j + 2] * w, v[j + 3] * w));
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PF_TMEM_COLS) : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ activation quantisation
+// One CTA (8 warps) per row: y = x @ H per 64-group (shuffle FWHT, lane holds elements lane and
+// lane + 32 of each group), then fp8: s = 448 / max(amax, 1e-6), q = e4m3(y * s), inv = 1 / s
+// (reference quant_fp8_rows, ds4_vq2_cuda.py:11-23, applied to had_act_batch output as at
+// ds4_vq2_cuda.py:94 and :106); f16: s = the power of two with amax * s <= 2^15, q = f16(y * s).
+// Rows with valid[row] == 0 are written as zeros with inv = 0. cols <= 4096.
+template <int PREC>
+__global__ void __launch_bounds__(256) had_quant_rows_kernel(const void* __restrict__ x, int in_dt,
+                                                             const uint8_t* __restrict__ valid, int cols,
+                                                             uint8_t* __restrict__ out, float* __restrict__ inv) {
+  __shared__ float red[33];
+  const long row = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ng = cols / 64;
+  const int elem = PREC == VQ2_PREC_FP8 ? 1 : 2;
+  uint8_t* orow = out + row * (size_t)cols * elem;
+  if (valid && !valid[row]) {
+    for (int c = threadIdx.x; c < cols * elem / 4; c += blockDim.x) ((uint32_t*)orow)[c] = 0u;
+    if (threadIdx.x == 0) inv[row] = 0.f;
+    return;
+  }
+  float va[8], vb[8];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int g = warp + 8 * i;
+    va[i] = vb[i] = 0.f;
+    if (g < ng) {
+      const size_t base = row * (size_t)cols + g * 64;
+      float a = load_act(x, in_dt, base + lane), b = load_act(x, in_dt, base + 32 + lane);
+      float t = a + b;
+      b = a - b;
+      a = t;
+#pragma unroll
+      for (int len = 16; len >= 1; len >>= 1) {
+        const float pa = __shfl_xor_sync(0xffffffffu, a, len), pb = __shfl_xor_sync(0xffffffffu, b, len);
+        a = (lane & len) ? (pa - a) : (a + pa);
+        b = (lane & len) ? (pb - b) : (b + pb);
+      }
+      va[i] = a * 0.125f;
+      vb[i] = b * 0.125f;
+      amax = fmaxf(amax, fmaxf(fabsf(va[i]), fabsf(vb[i])));
+    }
+  }
+  amax = block_max(amax, red);
+  float s;
+  if (PREC == VQ2_PREC_FP8) {
+    s = 448.0f / fmaxf(amax, 1e-6f);
+  } else {
+    s = 1.f;
+    if (amax > 0.f) {
+      int ex;
+      frexpf(32768.f / amax, &ex);
+      s = ldexpf(1.f, max(-100, min(100, ex - 1)));
+    }
+  }
+  if (threadIdx.x == 0) inv[row] = 1.0f / s;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int g = warp + 8 * i;
+    if (g < ng) {
+      if (PREC == VQ2_PREC_FP8) {
+        orow[g * 64 + lane] = (uint8_t)__nv_cvt_float_to_fp8(va[i] * s, __NV_SATFINITE, __NV_E4M3);
+        orow[g * 64 + 32 + lane] = (uint8_t)__nv_cvt_float_to_fp8(vb[i] * s, __NV_SATFINITE, __NV_E4M3);
+      } else {
+        ((__half*)orow)[g * 64 + lane] = __float2half_rn(va[i] * s);
+        ((__half*)orow)[g * 64 + 32 + lane] = __float2half_rn(vb[i] * s);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ host
+struct PfLayout {
+  long M, Pmax, nblk, nchunks;
+  size_t off_st, off_ss, off_val, off_be, off_counts, off_xq, off_invx, off_inter, off_vb, off_invvb, total;
+};
+
+static size_t up256(size_t v) { return (v + 255) & ~(size_t)255; }
+
+static PfLayout pf_layout(int N, int k, int E, int H, int I, int prec) {
+  PfLayout L;
+  const size_t elem = prec == VQ2_PREC_FP8 ? 1 : 2;
+  L.M = (long)N * k;
+  L.Pmax = L.M + (long)std::min<long>(L.M, E) * PF_BM;
+  L.nblk = L.Pmax / PF_BM;
+  L.nchunks = std::max<long>(1, (L.M + 8191) / 8192);
+  size_t o = 0;
+  L.off_st = o; o = up256(o + L.Pmax * 4);
+  L.off_ss = o; o = up256(o + L.Pmax * 4);
+  L.off_val = o; o = up256(o + L.Pmax);
+  L.off_be = o; o = up256(o + L.nblk * 4);
+  L.off_counts = o; o = up256(o + L.nchunks * E * 4);
+  L.off_xq = o; o = up256(o + (size_t)N * H * elem);
+  L.off_invx = o; o = up256(o + (size_t)N * 4);
+  L.off_inter = o; o = up256(o + (size_t)L.Pmax * I * 4);
+  L.off_vb = o; o = up256(o + (size_t)L.Pmax * I * elem);
+  L.off_invvb = o; o = up256(o + (size_t)L.Pmax * 4);
+  L.total = o + 256;
+  return L;
+}
+
+static bool g_pf_attr[64];
+
+}  // namespace vq2
+
+using namespace vq2;
+
+extern "C" size_t vq2_prefill_workspace_size(int N, int topk, int E, int H, int I, int precision) {
+  if (N <= 0 || topk <= 0 || E <= 0) return 0;
+  return pf_layout(N, topk, E, H, I, precision).total;
+}
+
+extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_bytes, void* stream) {
+  if (!a || !a->x || !a->topk_ids || !a->topk_w || !a->out || !a->w13_cb || !a->w13_lo || !a->w13_hi ||
+      !a->w13_sc || !a->w2_cb || !a->w2_lo || !a->w2_hi || !a->w2_sc)
+    return VQ2_ERR_NULL;
+  if (prec != VQ2_PREC_FP8 && prec != VQ2_PREC_F16) return VQ2_ERR_DTYPE;
+  if (a->N <= 0 || a->topk <= 0 || a->E <= 0 || a->E > 1024 || a->H % 128 || a->I % 128 || a->H > 4096 ||
+      a->I > 4096)
+    return VQ2_ERR_SHAPE;
+  if (a->x_dtype < 0 || a->x_dtype > 2 || a->ids_dtype < 0 || a->ids_dtype > 1) return VQ2_ERR_DTYPE;
+  const void* ptrs[] = {a->w13_lo, a->w13_hi, a->w13_sc, a->w2_lo, a->w2_hi, a->w2_sc, a->w13_cb, a->w2_cb};
+  for (const void* p : ptrs)
+    if (((uintptr_t)p & 15) != 0) return VQ2_ERR_ALIGN;
+  const PfLayout L = pf_layout(a->N, a->topk, a->E, a->H, a->I, prec);
+  if (L.nblk > 65535) return VQ2_ERR_SHAPE;
+  if (!ws || ws_bytes < L.total) return VQ2_ERR_WORKSPACE;
+  uint8_t* w = (uint8_t*)(((uintptr_t)ws + 255) & ~(uintptr_t)255);
+  int32_t* st = (int32_t*)(w + L.off_st);
+  int32_t* ss = (int32_t*)(w + L.off_ss);
+  uint8_t* val = w + L.off_val;
+  int32_t* be = (int32_t*)(w + L.off_be);
+  int* counts = (int*)(w + L.off_counts);
+  uint8_t* xq = w + L.off_xq;
+  float* invx = (float*)(w + L.off_invx);
+  float* inter = (float*)(w + L.off_inter);
+  uint8_t* vb = w + L.off_vb;
+  float* invvb = (float*)(w + L.off_invvb);
+  cudaStream_t st_ = (cudaStream_t)stream;
+
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VQ2_ERR_NO_DEVICE;
+  if (!g_pf_attr[dev]) {
+    bool ok = true;
+    ok &= cudaFuncSetAttribute(prefill_gemm_kernel<VQ2_PREC_FP8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM) == cudaSuccess;
+    ok &= cudaFuncSetAttribute(prefill_gemm_kernel<VQ2_PREC_FP8, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM) == cudaSuccess;
+    ok &= cudaFuncSetAttribute(prefill_gemm_kernel<VQ2_PREC_F16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM) == cudaSuccess;
+    ok &= cudaFuncSetAttribute(prefill_gemm_kernel<VQ2_PREC_F16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM) == cudaSuccess;
+    if (!ok) return VQ2_ERR_CUDA;
+    g_pf_attr[dev] = true;
+  }
+  int rc = launch_align_ex(a->topk_ids, a->ids_dtype, a->N, a->topk, a->E, PF_BM, a->expert_base, 1, st, ss, val,
+                           be, counts, st_);
+  if (rc) return rc;
+  if (cudaMemsetAsync(a->out, 0, (size_t)a->N * a->H * sizeof(float), st_) != cudaSuccess) return VQ2_ERR_CUDA;
+
+  PfGemmArgs g = {};
+  g.st = st; g.ss = ss; g.val = val; g.be = be; g.topk_w = a->topk_w; g.inter = inter; g.out = a->out;
+  g.I = a->I; g.H = a->H; g.topk = a->topk;
+  if (prec == VQ2_PREC_FP8) {
+    had_quant_rows_kernel<VQ2_PREC_FP8><<<a->N, 256, 0, st_>>>(a->x, a->x_dtype, nullptr, a->H, xq, invx);
+  } else {
+    had_quant_rows_kernel<VQ2_PREC_F16><<<a->N, 256, 0, st_>>>(a->x, a->x_dtype, nullptr, a->H, xq, invx);
+  }
+  // gate/up
+  g.act = xq; g.inv_act = invx; g.lo = a->w13_lo; g.hi = a->w13_hi; g.sc = a->w13_sc; g.cb = a->w13_cb;
+  g.K = a->H; g.R = 2 * a->I;
+  dim3 g1(a->I / 64, (unsigned)L.nblk);
+  if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, true><<<g1, PF_THREADS, PF_SMEM, st_>>>(g);
+  else prefill_gemm_kernel<VQ2_PREC_F16, true><<<g1, PF_THREADS, PF_SMEM, st_>>>(g);
+  // inter -> Hadamard -> quantised activation of the down projection
+  if (prec == VQ2_PREC_FP8)
+    had_quant_rows_kernel<VQ2_PREC_FP8><<<(unsigned)L.Pmax, 256, 0, st_>>>(inter, VQ2_DT_F32, val, a->I, vb, invvb);
+  else
+    had_quant_rows_kernel<VQ2_PREC_F16><<<(unsigned)L.Pmax, 256, 0, st_>>>(inter, VQ2_DT_F32, val, a->I, vb, invvb);
+  // down + combine
+  g.act = vb; g.inv_act = invvb; g.lo = a->w2_lo; g.hi = a->w2_hi; g.sc = a->w2_sc; g.cb = a->w2_cb;
+  g.K = a->I; g.R = a->H;
+  dim3 g2(a->H / PF_BN, (unsigned)L.nblk);
+  if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, false><<<g2, PF_THREADS, PF_SMEM, st_>>>(g);
+  else prefill_gemm_kernel<VQ2_PREC_F16, false><<<g2, PF_THREADS, PF_SMEM, st_>>>(g);
+  return cudaGetLastError() == cudaSuccess ? VQ2_OK : VQ2_ERR_CUDA;
+}

@@ -3,3 +3,4 @@
 #include "misc.cu"
 #include "align.cu"
 #include "decode.cu"
+#include "prefill.cu"

@@ -15,7 +15,7 @@ LIB_PATH = os.environ.get("VQ2_LIB") or os.path.join(os.path.dirname(_HERE), "li
 
 DT = {torch.bfloat16: 0, torch.float16: 1, torch.float32: 2}
 ID = {torch.int32: 0, torch.int64: 1}
-PREC = {"fp8": 0, "bf16": 1}
+PREC = {"fp8": 0, "f16": 1}
 DECODE_MAX_PAIRS = 512
 
 

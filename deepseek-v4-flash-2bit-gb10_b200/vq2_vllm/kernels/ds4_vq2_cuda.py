@@ -27,12 +27,12 @@ def vq2_moe_grouped_wmma(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sd
                          expert_base=0, precision=None):
     """Prefill (grouped GEMM) MoE -> fp32 [N, H] (reference ds4_vq2_cuda.py:72-111).
     NN/BKC/NW are the reference's mma.sync tiling hints, accepted and ignored. ``precision``:
-    "fp8" (the reference's fp8 e4m3 algorithm, default, like VQ2_FP8_PREFILL=1) or "bf16"
-    (bf16 operands; VQ2_FP8_PREFILL=0 selects it)."""
+    "fp8" (the reference's fp8 e4m3 algorithm, default, like VQ2_FP8_PREFILL=1) or "f16"
+    (fp16 operands with power-of-two activation scaling, fp32 accumulation; VQ2_FP8_PREFILL=0)."""
     if group != 64:
         raise ValueError("vq2: only group=64 is supported")
     if precision is None:
-        precision = "fp8" if os.environ.get("VQ2_FP8_PREFILL", "1") == "1" else "bf16"
+        precision = "fp8" if os.environ.get("VQ2_FP8_PREFILL", "1") == "1" else "f16"
     t = _prep(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn)
     N = x.shape[0]
     out = torch.empty(N, x.shape[1], device=x.device, dtype=torch.float32)

@@ -40,7 +40,7 @@ enum {
 
 enum { VQ2_DT_BF16 = 0, VQ2_DT_F16 = 1, VQ2_DT_F32 = 2 };   /* activation dtypes */
 enum { VQ2_ID_I32 = 0, VQ2_ID_I64 = 1 };                      /* topk_ids dtypes  */
-enum { VQ2_PREC_FP8 = 0, VQ2_PREC_BF16 = 1 };                 /* prefill operand precision */
+enum { VQ2_PREC_FP8 = 0, VQ2_PREC_F16 = 1 };                 /* prefill operand precision */
 
 #define VQ2_DECODE_MAX_PAIRS 512
 
@@ -84,7 +84,8 @@ int vq2_decode_noalloc(const vq2_moe_args* a, void* stream);
 
 /* Prefill MoE (grouped GEMM on tcgen05 tensor cores). Replaces ds4_vq2_cuda.vq2_moe_grouped_wmma
  * (reference vq2_vllm/kernels/ds4_vq2_cuda.py:72-111). precision = VQ2_PREC_FP8 follows the
- * reference's fp8 e4m3 algorithm; VQ2_PREC_BF16 runs bf16 operands (fp32 accumulation). */
+ * reference's fp8 e4m3 algorithm; VQ2_PREC_F16 runs fp16 operands (activations scaled by a power of two
+ * into fp16 range, fp32 accumulation) and meets 3e-2 against the fp32 dequant reference. */
 size_t vq2_prefill_workspace_size(int N, int topk, int E, int H, int I, int precision);
 int vq2_prefill(const vq2_moe_args* a, int precision, void* workspace, size_t ws_bytes, void* stream);
 
