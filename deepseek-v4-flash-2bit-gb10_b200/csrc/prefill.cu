@@ -243,15 +243,16 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(PfGemmArgs 
       }
       cp_async_commit();
       ++issued;
-      if (c >= 1) {
-        cp_async_wait<1>();
+      // keep up to PF_STAGES-1 chunk loads in flight; publish the oldest once it has landed
+      if (c >= PF_STAGES - 1) {
+        cp_async_wait<PF_STAGES - 1>();
         fence_async_smem();
-        mbar_arrive(&sh->full_a[(c - 1) % PF_STAGES]);
+        mbar_arrive(&sh->full_a[(c - (PF_STAGES - 1)) % PF_STAGES]);
       }
     }
     cp_async_wait<0>();
     fence_async_smem();
-    if (issued >= 1) mbar_arrive(&sh->full_a[(issued - 1) % PF_STAGES]);
+    for (int c = max(0, issued - (PF_STAGES - 1)); c < issued; ++c) mbar_arrive(&sh->full_a[c % PF_STAGES]);
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
@@ -278,11 +279,9 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(PfGemmArgs 
     const uint8_t* lo_row = a.lo + wrow * nsub;
     const uint8_t* hi_row = a.hi + wrow * (nsub / 4);
     const uint16_t* sc_row = a.sc + wrow * ngk;
-    for (int c = 0; c < nchunks; ++c) {
-      const int slot = c % PF_STAGES;
+    // index planes of chunk c are loaded one chunk ahead (registers), hiding their latency
+    auto load_idx = [&](int c, uint4& lo, uint32_t& hw, float& scf) {
       const int s0 = (c * KE + h * (KE / 2)) / 4;      // first sub-vector of this thread
-      uint4 lo;
-      uint32_t hw;
       if (PREC == VQ2_PREC_FP8) {
         lo = *(const uint4*)(lo_row + s0);
         hw = *(const uint32_t*)(hi_row + s0 / 4);
@@ -291,7 +290,18 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(PfGemmArgs 
         lo = make_uint4(l2.x, l2.y, 0, 0);
         hw = *(const uint16_t*)(hi_row + s0 / 4);
       }
-      const float scf = __half2float(__ushort_as_half(sc_row[(s0 * 4) / 64]));
+      scf = __half2float(__ushort_as_half(sc_row[(s0 * 4) / 64]));
+    };
+    uint4 lo_n;
+    uint32_t hw_n;
+    float sc_n;
+    if (nchunks > 0) load_idx(0, lo_n, hw_n, sc_n);
+    for (int c = 0; c < nchunks; ++c) {
+      const int slot = c % PF_STAGES;
+      const uint4 lo = lo_n;
+      const uint32_t hw = hw_n;
+      const float scf = sc_n;
+      if (c + 1 < nchunks) load_idx(c + 1, lo_n, hw_n, sc_n);
       if (c >= PF_STAGES && !mbar_wait(&sh->empty[slot], ((c / PF_STAGES) - 1) & 1)) break;
       decode_b_row<PREC>(cbl, lo, hw, scf, tiles + (2 * slot + 1) * PF_TILE, r, h);
       fence_async_smem();

@@ -75,7 +75,7 @@ def vq2_moe_fused_10b(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, 
     if N * k > _lib.DECODE_MAX_PAIRS:
         from .ds4_vq2_cuda import vq2_moe_grouped_wmma
         return vq2_moe_grouped_wmma(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, group=group,
-                                    expert_base=expert_base)
+                                    expert_base=expert_base, precision="f16")
     t = _prep(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn)
     out = torch.empty(N, x.shape[1], device=x.device, dtype=torch.float32)
     L = _lib.lib()

@@ -59,3 +59,39 @@ def rel_l2(a, b):
     a = a.double()
     b = b.double()
     return ((a - b).norm() / b.norm().clamp_min(1e-30)).item()
+
+
+def quant_fp8_rows(x):
+    """s = 448 / max(amax, 1e-6); q = e4m3(x * s); inv = 1 / s per row
+    (reference vq2_vllm/kernels/ds4_vq2_cuda.py:8-23). Returns (q as fp32 values, inv)."""
+    amax = x.abs().amax(-1)
+    s = 448.0 / amax.clamp_min(1e-6)
+    q = (x * s[:, None]).clamp(-448, 448).to(torch.float8_e4m3fn).float()
+    return q, 1.0 / s
+
+
+def moe_prefill_fp8_ref(x, topk_ids, topk_w, layer, expert_base=0, E=None):
+    """The reference's fp8 prefill algorithm (vq2_vllm/kernels/ds4_vq2_cuda.py:72-111): per-token
+    fp8 activations, weights decoded as e4m3(sat(C[id] * sc)) (vq2_grouped.cu:434-446),
+    silu(g*inv)*(u*inv) (vq2_grouped.cu:255-264), per-row fp8 of had(inter), down weighted by
+    w * inv_vb. fp32 sums. Same maths as oracle.vq2_oracle.moe_prefill_fp8_ref."""
+    x = x.float()
+    N, H = x.shape
+    E = layer["w13_lo"].shape[0] if E is None else E
+    I = layer["w13_lo"].shape[1] // 2
+    ids = topk_ids.long() - expert_base
+    xq, inv_x = quant_fp8_rows(had_rows(x))
+    out = torch.zeros(N, H, device=x.device)
+    q8 = lambda w: w.clamp(-448, 448).to(torch.float8_e4m3fn).float()
+    for e in torch.unique(ids).tolist():
+        if e < 0 or e >= E:
+            continue
+        n_idx, j_idx = torch.nonzero(ids == e, as_tuple=True)
+        bgu = q8(dequant_rot(layer["w13_cb"], layer["w13_lo"][e], layer["w13_hi"][e], layer["w13_sc"][e]))
+        bdn = q8(dequant_rot(layer["w2_cb"], layer["w2_lo"][e], layer["w2_hi"][e], layer["w2_sc"][e]))
+        gu = (xq[n_idx] @ bgu.T) * inv_x[n_idx, None]
+        a = torch.nn.functional.silu(gu[:, :I]) * gu[:, I:]
+        vq, inv_v = quant_fp8_rows(had_rows(a))
+        d = (vq @ bdn.T) * (topk_w.float()[n_idx, j_idx] * inv_v)[:, None]
+        out.index_add_(0, n_idx, d)
+    return out

@@ -82,3 +82,13 @@ def test_torch_ref_matches_numpy_oracle():
     tl = {k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in layer.items()}
     out = torch_ref.moe_ref(torch.from_numpy(x), torch.from_numpy(z["topk_ids"]), torch.from_numpy(z["topk_w"]), tl)
     assert O.rel_l2(out.numpy(), z["ref_dense"]) < 1e-5
+
+
+def test_torch_fp8_prefill_matches_numpy_oracle():
+    from oracle import torch_ref
+    z, layer, x = load_config0()
+    tl = {k: torch.from_numpy(np.ascontiguousarray(v)) for k, v in layer.items()}
+    a = torch_ref.moe_prefill_fp8_ref(torch.from_numpy(x), torch.from_numpy(z["topk_ids"]),
+                                      torch.from_numpy(z["topk_w"]), tl)
+    b = O.moe_prefill_fp8_ref(x, z["topk_ids"], z["topk_w"], _w(layer, "w13"), _w(layer, "w2"))
+    assert O.rel_l2(a.numpy(), b) < 2e-3
