@@ -16,7 +16,10 @@
 // (M=128, N=128, K=32 fp8 / K=16 f16 per instruction) into a 128-column fp32 TMEM accumulator;
 // warps 2..9 decode the VQ weight tile (10-bit index -> fp16 codebook vector x fp16 group scale
 // -> e4m3 / f16) straight into the swizzled B tile, then run the epilogue out of TMEM.
-// A 3-stage ring of (A, B) tiles is synchronised with mbarriers; tcgen05.commit frees a stage.
+// A 5-stage ring of (A tile, staged index planes), filled by warp 0 with cp.async, and a 2-stage
+// ring of B tiles, filled by the decoders from the staged planes, are synchronised with mbarriers;
+// tcgen05.commit frees stages of both rings. The codebook (8 copies, lane l reads copy l mod 8) arrives
+// by one bulk copy.
 #include <cuda_fp8.h>
 #include <algorithm>
 #include "vq2_common.cuh"
@@ -28,23 +31,30 @@ int launch_align_ex(const void* ids, int dt, long N, int k, int E, int BM, int b
 
 constexpr int PF_BM = 128;            // slots per block (MMA M)
 constexpr int PF_BN = 128;            // weight rows per tile (MMA N)
-constexpr int PF_STAGES = 3;
+constexpr int PF_STAGES = 5;          // ring of (A tile, index planes): memory latency
+constexpr int PF_BSTAGES = 2;         // ring of decoded B tiles: produced in the CTA
 constexpr int PF_DEC_WARPS = 8;
 constexpr int PF_THREADS = (2 + PF_DEC_WARPS) * 32;
 constexpr int PF_TILE = 16384;        // one 128 x 128-byte operand tile
-constexpr int PF_CB_BYTES = 1024 * 8 * 16;
+constexpr int PF_CB_COPIES = 8;
+constexpr int PF_CB_BYTES = 1024 * 8 * PF_CB_COPIES;
+constexpr int PF_IDX = 6144;   // staged index planes of one stage: lo 4096 B, hi 1024 B, sc 512 B (padded)
+static_assert(PF_IDX % 1024 == 0, "index stages keep the following tiles 1024-byte aligned");
 constexpr int PF_TMEM_COLS = 128;
 
 struct PfShared {
   uint64_t full_a[PF_STAGES];
-  uint64_t full_b[PF_STAGES];
   uint64_t empty[PF_STAGES];
+  uint64_t full_b[PF_BSTAGES];
+  uint64_t empty_b[PF_BSTAGES];
   uint64_t done;
+  uint64_t cbbar;
   uint32_t tmem_base;
   int slot_tok[PF_BM];
 };
 
-constexpr size_t PF_SMEM = (size_t)PF_CB_BYTES + 2 * PF_STAGES * PF_TILE + sizeof(PfShared) + 1024;
+constexpr size_t PF_SMEM = (size_t)PF_CB_BYTES + (size_t)PF_STAGES * (PF_TILE + PF_IDX) + (size_t)PF_BSTAGES * PF_TILE +
+                           sizeof(PfShared) + 1024;
 
 struct PfGemmArgs {
   const uint8_t* act;        // activation rows (token rows for gate/up, slot rows for down)
@@ -145,7 +155,7 @@ __device__ __forceinline__ void decode_b_row(const uint8_t* cbl, uint4 lo, uint3
       uint32_t packed[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint32_t off = (((lw[q] >> (8 * j)) & 0xFFu) << 7) | (((hw >> (8 * q + 2 * j)) & 3u) << 15);
+        const uint32_t off = (((lw[q] >> (8 * j)) & 0xFFu) << 6) | (((hw >> (8 * q + 2 * j)) & 3u) << 14);
         const uint2 c = *(const uint2*)(cbl + off);
         const float2 a = __half22float2(*(const __half2*)&c.x), b = __half22float2(*(const __half2*)&c.y);
         const __nv_fp8x2_storage_t p0 = __nv_cvt_float2_to_fp8x2(make_float2(a.x * scf, a.y * scf), __NV_SATFINITE, __NV_E4M3);
@@ -163,7 +173,7 @@ __device__ __forceinline__ void decode_b_row(const uint8_t* cbl, uint4 lo, uint3
 #pragma unroll
       for (int j = 0; j < 2; ++j) {
         const int s = 2 * q + j;
-        const uint32_t off = (((lw[s >> 2] >> (8 * (s & 3))) & 0xFFu) << 7) | (((hw >> (2 * s)) & 3u) << 15);
+        const uint32_t off = (((lw[s >> 2] >> (8 * (s & 3))) & 0xFFu) << 6) | (((hw >> (2 * s)) & 3u) << 14);
         const uint2 c = *(const uint2*)(cbl + off);
         const __half2 v0 = __hmul2(*(const __half2*)&c.x, s2), v1 = __hmul2(*(const __half2*)&c.y, s2);
         w[2 * j] = *(const uint32_t*)&v0;
@@ -178,59 +188,104 @@ __device__ __forceinline__ void decode_b_row(const uint8_t* cbl, uint4 lo, uint3
 // grid (tiles along N, blocks of 128 slots). GATEUP: tile n covers gate rows [64n, 64n+64) and
 // the matching up rows; the epilogue writes inter. Otherwise tile n covers output rows
 // [128n, 128n+128) and the epilogue accumulates into out.
+#ifdef VQ2_PF_PROBE
+// Development probe (off in the product build): global-timer stamps per stage of CTA (0, 0).
+__device__ unsigned long long g_pf_probe[4][64];
+__device__ __forceinline__ unsigned long long pf_time() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+#define PF_PROBE(k, i) do { if (blockIdx.x == 0 && blockIdx.y == 0 && (i) < 64) g_pf_probe[k][i] = pf_time(); } while (0)
+#else
+#define PF_PROBE(k, i) do {} while (0)
+#endif
+
+template <bool GATEUP>
+__device__ __forceinline__ long pf_weight_row(const PfGemmArgs& a, int e, int tile, int r) {
+  if (GATEUP) return (long)e * a.R + (r < 64 ? tile * 64 + r : a.I + tile * 64 + (r - 64));
+  return (long)e * a.R + tile * PF_BN + r;
+}
+
 template <int PREC, bool GATEUP>
 __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(PfGemmArgs a) {
   extern __shared__ __align__(1024) uint8_t pf_smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)pf_smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* cbs = smem;
-  uint8_t* tiles = smem + PF_CB_BYTES;                 // A0 B0 A1 B1 A2 B2
-  PfShared* sh = (PfShared*)(tiles + 2 * PF_STAGES * PF_TILE);
+  uint8_t* atiles = smem + PF_CB_BYTES;                // A ring
+  uint8_t* btiles = atiles + PF_STAGES * PF_TILE;      // B ring
+  uint8_t* itiles = btiles + PF_BSTAGES * PF_TILE;     // index-plane ring
+  PfShared* sh = (PfShared*)(itiles + PF_STAGES * PF_IDX);
   const int blk = blockIdx.y, tile = blockIdx.x;
+  if (threadIdx.x == 0) PF_PROBE(3, 0);
   if (!a.val[(size_t)blk * PF_BM]) return;           // blocks past the last expert hold no pair
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int e = a.be[blk];
-  const int elem = PREC == VQ2_PREC_FP8 ? 1 : 2;
-  const int KE = 128 / elem;                          // K elements per stage (128 bytes per row)
+  constexpr int elem = PREC == VQ2_PREC_FP8 ? 1 : 2;
+  constexpr int KE = 128 / elem;                      // K elements per stage (128 bytes per row)
   const int nchunks = a.K / KE;
   const int nsub = a.K / 4, ngk = a.K / 64;
+  auto A_t = [&](int slot) { return atiles + slot * PF_TILE; };
+  auto B_t = [&](int slot) { return btiles + slot * PF_TILE; };
+  auto I_t = [&](int slot) { return itiles + slot * PF_IDX; };   // lo | hi | sc
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < PF_STAGES; ++s) {
       mbar_init(&sh->full_a[s], 32);
-      mbar_init(&sh->full_b[s], PF_DEC_WARPS);
       mbar_init(&sh->empty[s], 1);
     }
+    for (int s = 0; s < PF_BSTAGES; ++s) {
+      mbar_init(&sh->full_b[s], PF_DEC_WARPS);
+      mbar_init(&sh->empty_b[s], 1);
+    }
     mbar_init(&sh->done, 1);
+    mbar_init(&sh->cbbar, 1);
     fence_mbar_init();
+    mbar_arrive_expect_tx(&sh->cbbar, 1024 * 8);
+    bulk_g2s(B_t(0), a.cb, 1024 * 8, &sh->cbbar);     // codebook lands in stage 0's B tile first
   }
   for (int i = threadIdx.x; i < PF_BM; i += blockDim.x) {
     const size_t p = (size_t)blk * PF_BM + i;
     sh->slot_tok[i] = a.val[p] ? a.st[p] : -1;
-  }
-  {  // codebook replicated 16x (entry e of copy c at e*128 + c*8), consecutive 16-byte stores
-    const uint2* src = (const uint2*)a.cb;
-    for (int idx = threadIdx.x; idx < 1024 * 8; idx += blockDim.x) {
-      const uint2 v = src[idx >> 3];
-      *(uint4*)(cbs + (idx >> 3) * 128 + (idx & 7) * 16) = make_uint4(v.x, v.y, v.x, v.y);
-    }
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
                  ::"r"(smem_u32(&sh->tmem_base)), "r"(PF_TMEM_COLS) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
+  __syncthreads();                                    // barrier inits visible
+  mbar_wait(&sh->cbbar, 0);
+  {  // replicate: entry e of copy c at e*64 + c*8; consecutive 16-byte stores
+    const uint2* src = (const uint2*)B_t(0);
+    for (int idx = threadIdx.x; idx < 1024 * (PF_CB_COPIES / 2); idx += blockDim.x) {
+      const uint2 v = src[idx / (PF_CB_COPIES / 2)];
+      *(uint4*)(cbs + idx * 16) = make_uint4(v.x, v.y, v.x, v.y);
+    }
+  }
   tc_fence_before();
-  __syncthreads();
+  __syncthreads();                                    // codebook ready, staging tile free again
   tc_fence_after();
+  if (threadIdx.x == 0) PF_PROBE(3, 1);
   const uint32_t tmem = sh->tmem_base;
 
   if (warp == 0) {
-    // ---------------- activation tile loader: 128 rows x 128 bytes per stage, 32 chunks per lane
+    // ---------------- loader: A tile (128 rows x 128 B) + the B tile's index planes, cp.async
+    const uint8_t* lo_r[4];
+    const uint8_t* hi_r[4];
+    const uint8_t* sc_r[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const long wr = pf_weight_row<GATEUP>(a, e, tile, lane + 32 * i);
+      lo_r[i] = a.lo + wr * nsub;
+      hi_r[i] = a.hi + wr * (nsub / 4);
+      sc_r[i] = (const uint8_t*)(a.sc + wr * ngk);
+    }
     int issued = 0;
+    (void)issued;
     for (int c = 0; c < nchunks; ++c) {
       const int slot = c % PF_STAGES;
       if (c >= PF_STAGES && !mbar_wait(&sh->empty[slot], ((c / PF_STAGES) - 1) & 1)) break;
-      const uint32_t abase = smem_u32(tiles + 2 * slot * PF_TILE);
+      const uint32_t abase = smem_u32(A_t(slot)), ibase = smem_u32(I_t(slot));
 #pragma unroll 8
       for (int i = 0; i < 32; ++i) {
         const int id = i * 32 + lane, r = id >> 3, kc = id & 7;
@@ -241,72 +296,74 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(PfGemmArgs 
         const uint8_t* src = a.act + (size_t)row * a.K * elem + (size_t)c * 128 + kc * 16;
         cp_async16(abase + sw128_off(r, kc), src, ok);
       }
-      cp_async_commit();
-      ++issued;
-      // keep up to PF_STAGES-1 chunk loads in flight; publish the oldest once it has landed
-      if (c >= PF_STAGES - 1) {
-        cp_async_wait<PF_STAGES - 1>();
-        fence_async_smem();
-        mbar_arrive(&sh->full_a[(c - (PF_STAGES - 1)) % PF_STAGES]);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = lane + 32 * i;
+        if (PREC == VQ2_PREC_FP8) {          // 32 sub-vectors per row per stage
+          cp_async16(ibase + r * 32, lo_r[i] + c * 32, true);
+          cp_async16(ibase + r * 32 + 16, lo_r[i] + c * 32 + 16, true);
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(ibase + 4096 + r * 8), "l"(hi_r[i] + c * 8) : "memory");
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + 5120 + r * 4), "l"(sc_r[i] + c * 4) : "memory");
+        } else {                             // 16 sub-vectors; the group scale pair holding this group
+          cp_async16(ibase + r * 32, lo_r[i] + c * 16, true);
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + 4096 + r * 8), "l"(hi_r[i] + c * 4) : "memory");
+          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + 5120 + r * 4), "l"(sc_r[i] + (c & ~1) * 2) : "memory");
+        }
       }
+      // the stage's full barrier (32 arrivals) is signalled by the hardware once this lane's
+      // copies above have landed
+      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&sh->full_a[slot])) : "memory");
+      if (lane == 0) PF_PROBE(0, c);
+      ++issued;
     }
-    cp_async_wait<0>();
-    fence_async_smem();
-    for (int c = max(0, issued - (PF_STAGES - 1)); c < issued; ++c) mbar_arrive(&sh->full_a[c % PF_STAGES]);
+    cp_async_wait<0>();                               // nothing in flight when the CTA retires
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
       for (int c = 0; c < nchunks; ++c) {
-        const int slot = c % PF_STAGES;
-        const uint32_t par = (c / PF_STAGES) & 1;
-        if (!mbar_wait(&sh->full_a[slot], par) || !mbar_wait(&sh->full_b[slot], par)) break;
+        const int slot = c % PF_STAGES, bslot = c % PF_BSTAGES;
+        if (!mbar_wait(&sh->full_a[slot], (c / PF_STAGES) & 1)) break;
+        PF_PROBE(1, c);
+        if (!mbar_wait(&sh->full_b[bslot], (c / PF_BSTAGES) & 1)) break;
+        PF_PROBE(2, c);
+        fence_async_smem();                               // cp.async-written A visible to the tensor core
         tc_fence_after();
-        const uint32_t abase = smem_u32(tiles + 2 * slot * PF_TILE), bbase = abase + PF_TILE;
+        const uint32_t abase = smem_u32(A_t(slot)), bbase = smem_u32(B_t(bslot));
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks)
           umma<PREC>(tmem, umma_desc_sw128(abase + ks * 32), umma_desc_sw128(bbase + ks * 32), (c | ks) != 0);
         umma_commit(&sh->empty[slot]);
+        umma_commit(&sh->empty_b[bslot]);
       }
       umma_commit(&sh->done);   // arrives once every MMA issued above has completed
     }
   } else {
     // ---------------- weight decoders (256 threads: row r, half h of the 128-byte row)
     const int dt = threadIdx.x - 64, r = dt & 127, h = dt >> 7;
-    const uint8_t* cbl = cbs + (lane & 15) * 8;
-    long wrow;
-    if (GATEUP) wrow = (long)e * a.R + (r < 64 ? tile * 64 + r : a.I + tile * 64 + (r - 64));
-    else wrow = (long)e * a.R + tile * PF_BN + r;
-    const uint8_t* lo_row = a.lo + wrow * nsub;
-    const uint8_t* hi_row = a.hi + wrow * (nsub / 4);
-    const uint16_t* sc_row = a.sc + wrow * ngk;
-    // index planes of chunk c are loaded one chunk ahead (registers), hiding their latency
-    auto load_idx = [&](int c, uint4& lo, uint32_t& hw, float& scf) {
-      const int s0 = (c * KE + h * (KE / 2)) / 4;      // first sub-vector of this thread
-      if (PREC == VQ2_PREC_FP8) {
-        lo = *(const uint4*)(lo_row + s0);
-        hw = *(const uint32_t*)(hi_row + s0 / 4);
-      } else {
-        const uint2 l2 = *(const uint2*)(lo_row + s0);
-        lo = make_uint4(l2.x, l2.y, 0, 0);
-        hw = *(const uint16_t*)(hi_row + s0 / 4);
-      }
-      scf = __half2float(__ushort_as_half(sc_row[(s0 * 4) / 64]));
-    };
-    uint4 lo_n;
-    uint32_t hw_n;
-    float sc_n;
-    if (nchunks > 0) load_idx(0, lo_n, hw_n, sc_n);
+    const uint8_t* cbl = cbs + (lane & (PF_CB_COPIES - 1)) * 8;
     for (int c = 0; c < nchunks; ++c) {
-      const int slot = c % PF_STAGES;
-      const uint4 lo = lo_n;
-      const uint32_t hw = hw_n;
-      const float scf = sc_n;
-      if (c + 1 < nchunks) load_idx(c + 1, lo_n, hw_n, sc_n);
-      if (c >= PF_STAGES && !mbar_wait(&sh->empty[slot], ((c / PF_STAGES) - 1) & 1)) break;
-      decode_b_row<PREC>(cbl, lo, hw, scf, tiles + (2 * slot + 1) * PF_TILE, r, h);
+      const int slot = c % PF_STAGES, bslot = c % PF_BSTAGES;
+      // the index planes of this stage come with the A tile
+      if (!mbar_wait(&sh->full_a[slot], (c / PF_STAGES) & 1)) break;
+      if (c >= PF_BSTAGES && !mbar_wait(&sh->empty_b[bslot], ((c / PF_BSTAGES) - 1) & 1)) break;
+      const uint8_t* ip = I_t(slot);
+      uint4 lo;
+      uint32_t hw;
+      float scf;
+      if (PREC == VQ2_PREC_FP8) {
+        lo = *(const uint4*)(ip + r * 32 + h * 16);
+        hw = *(const uint32_t*)(ip + 4096 + r * 8 + h * 4);
+        scf = __half2float(*(const __half*)(ip + 5120 + r * 4 + h * 2));
+      } else {
+        const uint2 l2 = *(const uint2*)(ip + r * 32 + h * 8);
+        lo = make_uint4(l2.x, l2.y, 0, 0);
+        hw = *(const uint16_t*)(ip + 4096 + r * 8 + h * 2);
+        scf = __half2float(*(const __half*)(ip + 5120 + r * 4 + (c & 1) * 2));
+      }
+      decode_b_row<PREC>(cbl, lo, hw, scf, B_t(bslot), r, h);
       fence_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sh->full_b[slot]);
+      if (lane == 0) mbar_arrive(&sh->full_b[bslot]);
     }
     // ---------------- epilogue out of TMEM
     const int q = warp & 3, ch = (warp - 2) >> 2;       // TMEM lane quarter, column half
@@ -314,6 +371,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(PfGemmArgs 
     const int tok = sh->slot_tok[slot_i];
     const size_t p = (size_t)blk * PF_BM + slot_i;
     if (mbar_wait(&sh->done, 0)) {
+      if (threadIdx.x == 64) PF_PROBE(3, 2);
       tc_fence_after();
       const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
       if (GATEUP) {
@@ -348,6 +406,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(PfGemmArgs 
   }
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) PF_PROBE(3, 3);
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PF_TMEM_COLS) : "memory");
@@ -461,6 +520,10 @@ static bool g_pf_attr[64];
 }  // namespace vq2
 
 using namespace vq2;
+
+#ifdef VQ2_PF_PROBE
+extern "C" int vq2_pf_probe_read(void* host) { return (int)cudaMemcpyFromSymbol(host, g_pf_probe, sizeof(g_pf_probe)); }
+#endif
 
 extern "C" size_t vq2_prefill_workspace_size(int N, int topk, int E, int H, int I, int precision) {
   if (N <= 0 || topk <= 0 || E <= 0) return 0;
