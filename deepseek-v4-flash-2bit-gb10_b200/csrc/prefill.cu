@@ -11,15 +11,18 @@
 //   vb_quant   inter -> Hadamard -> per-slot quantised activation (+ inv)
 //   down       per (block, 128 output rows): D = vb . Wd^T; epilogue out[tok] += D * w * inv_vb
 //
-// GEMM CTA (one per SM, 320 threads): warp 0 allocates TMEM and gathers the activation tile rows
-// with cp.async into the 128-byte-swizzled K-major layout; warp 1 lane 0 issues tcgen05.mma
+// GEMM CTA (one per SM, 320 threads): warp 0 allocates TMEM and loads the activation tile (rows in
+// slot order, 128-byte swizzled K-major) and the weight tile's lo index plane with 2-D TMA copies,
+// the small hi / scale planes with cp.async; warp 1 lane 0 issues tcgen05.mma
 // (M=128, N=128, K=32 fp8 / K=16 f16 per instruction) into a 128-column fp32 TMEM accumulator;
 // warps 2..9 decode the VQ weight tile (10-bit index -> fp16 codebook vector x fp16 group scale
 // -> e4m3 / f16) straight into the swizzled B tile, then run the epilogue out of TMEM.
-// A 5-stage ring of (A tile, staged index planes), filled by warp 0 with cp.async, and a 2-stage
+// A 5-stage ring of (A tile, staged index planes), filled by warp 0, and a 2-stage
 // ring of B tiles, filled by the decoders from the staged planes, are synchronised with mbarriers;
 // tcgen05.commit frees stages of both rings. The codebook (8 copies, lane l reads copy l mod 8) arrives
 // by one bulk copy.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_fp8.h>
 #include <algorithm>
 #include "vq2_common.cuh"
@@ -129,6 +132,11 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+  asm volatile("cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+               ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool ok) {
   asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(ok ? 16 : 0) : "memory");
 }
@@ -208,7 +216,8 @@ __device__ __forceinline__ long pf_weight_row(const PfGemmArgs& a, int e, int ti
 }
 
 template <int PREC, bool GATEUP>
-__global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(PfGemmArgs a) {
+__global__ void __launch_bounds__(PF_THREADS, 1)
+prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_lo) {
   extern __shared__ __align__(1024) uint8_t pf_smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)pf_smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* cbs = smem;
@@ -231,7 +240,7 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(PfGemmArgs 
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < PF_STAGES; ++s) {
-      mbar_init(&sh->full_a[s], 32);
+      mbar_init(&sh->full_a[s], 33);        // TMA bytes (1 arrival) + 32 lanes' cp.async
       mbar_init(&sh->empty[s], 1);
     }
     for (int s = 0; s < PF_BSTAGES; ++s) {
@@ -269,52 +278,41 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(PfGemmArgs 
   const uint32_t tmem = sh->tmem_base;
 
   if (warp == 0) {
-    // ---------------- loader: A tile (128 rows x 128 B) + the B tile's index planes, cp.async
-    const uint8_t* lo_r[4];
+    // ---------------- loader: A tile + lo plane by TMA, hi / scale planes by cp.async
+    constexpr int LOB = 128 / elem / 4;               // lo bytes per row per stage (32 fp8, 16 f16)
     const uint8_t* hi_r[4];
     const uint8_t* sc_r[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
       const long wr = pf_weight_row<GATEUP>(a, e, tile, lane + 32 * i);
-      lo_r[i] = a.lo + wr * nsub;
       hi_r[i] = a.hi + wr * (nsub / 4);
       sc_r[i] = (const uint8_t*)(a.sc + wr * ngk);
     }
-    int issued = 0;
-    (void)issued;
+    const int row0 = (int)pf_weight_row<GATEUP>(a, e, tile, 0), row1 = (int)pf_weight_row<GATEUP>(a, e, tile, 64);
     for (int c = 0; c < nchunks; ++c) {
       const int slot = c % PF_STAGES;
       if (c >= PF_STAGES && !mbar_wait(&sh->empty[slot], ((c / PF_STAGES) - 1) & 1)) break;
-      const uint32_t abase = smem_u32(A_t(slot)), ibase = smem_u32(I_t(slot));
-#pragma unroll 8
-      for (int i = 0; i < 32; ++i) {
-        const int id = i * 32 + lane, r = id >> 3, kc = id & 7;
-        int row;
-        bool ok;
-        if (GATEUP) { row = sh->slot_tok[r]; ok = row >= 0; if (!ok) row = 0; }
-        else { row = blk * PF_BM + r; ok = true; }
-        const uint8_t* src = a.act + (size_t)row * a.K * elem + (size_t)c * 128 + kc * 16;
-        cp_async16(abase + sw128_off(r, kc), src, ok);
+      const uint32_t ibase = smem_u32(I_t(slot));
+      if (lane == 0) {
+        mbar_arrive_expect_tx(&sh->full_a[slot], PF_TILE + 128 * LOB);
+        tma_load_2d(A_t(slot), &tm_act, c * 128, blk * PF_BM, &sh->full_a[slot]);
+        tma_load_2d(I_t(slot), &tm_lo, c * LOB, row0, &sh->full_a[slot]);
+        tma_load_2d(I_t(slot) + 64 * LOB, &tm_lo, c * LOB, row1, &sh->full_a[slot]);
       }
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
         const int r = lane + 32 * i;
-        if (PREC == VQ2_PREC_FP8) {          // 32 sub-vectors per row per stage
-          cp_async16(ibase + r * 32, lo_r[i] + c * 32, true);
-          cp_async16(ibase + r * 32 + 16, lo_r[i] + c * 32 + 16, true);
+        if (PREC == VQ2_PREC_FP8) {          // hi: 8 bytes (32 sub-vectors); scales of 2 groups
           asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(ibase + 4096 + r * 8), "l"(hi_r[i] + c * 8) : "memory");
           asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + 5120 + r * 4), "l"(sc_r[i] + c * 4) : "memory");
-        } else {                             // 16 sub-vectors; the group scale pair holding this group
-          cp_async16(ibase + r * 32, lo_r[i] + c * 16, true);
+        } else {                             // hi: 4 bytes (16 sub-vectors); the scale pair holding this group
           asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + 4096 + r * 8), "l"(hi_r[i] + c * 4) : "memory");
           asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + 5120 + r * 4), "l"(sc_r[i] + (c & ~1) * 2) : "memory");
         }
       }
-      // the stage's full barrier (32 arrivals) is signalled by the hardware once this lane's
-      // copies above have landed
+      // the stage's full barrier also gets one arrival per lane when its copies above have landed
       asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&sh->full_a[slot])) : "memory");
       if (lane == 0) PF_PROBE(0, c);
-      ++issued;
     }
     cp_async_wait<0>();                               // nothing in flight when the CTA retires
   } else if (warp == 1) {
@@ -351,11 +349,11 @@ __global__ void __launch_bounds__(PF_THREADS, 1) prefill_gemm_kernel(PfGemmArgs 
       uint32_t hw;
       float scf;
       if (PREC == VQ2_PREC_FP8) {
-        lo = *(const uint4*)(ip + r * 32 + h * 16);
+        lo = *(const uint4*)(ip + r * 32 + h * 16);           // lo rows 32 bytes apart
         hw = *(const uint32_t*)(ip + 4096 + r * 8 + h * 4);
         scf = __half2float(*(const __half*)(ip + 5120 + r * 4 + h * 2));
       } else {
-        const uint2 l2 = *(const uint2*)(ip + r * 32 + h * 8);
+        const uint2 l2 = *(const uint2*)(ip + r * 16 + h * 8);  // lo rows 16 bytes apart
         lo = make_uint4(l2.x, l2.y, 0, 0);
         hw = *(const uint16_t*)(ip + 4096 + r * 8 + h * 2);
         scf = __half2float(*(const __half*)(ip + 5120 + r * 4 + (c & 1) * 2));
@@ -485,10 +483,46 @@ __global__ void __launch_bounds__(256) had_quant_rows_kernel(const void* __restr
   }
 }
 
+// Quantised token rows into slot order (padding slots zero), so the gate/up A tile of a block is
+// one contiguous 2-D TMA box.
+__global__ void __launch_bounds__(256) gather_slot_rows_kernel(const uint8_t* __restrict__ src,
+                                                              const int32_t* __restrict__ st,
+                                                              const uint8_t* __restrict__ val, int row_bytes,
+                                                              uint8_t* __restrict__ dst) {
+  const long p = blockIdx.x;
+  uint4* d = (uint4*)(dst + p * (size_t)row_bytes);
+  const bool ok = val[p] != 0;
+  const uint4* s = (const uint4*)(src + (size_t)(ok ? st[p] : 0) * row_bytes);
+  for (int i = threadIdx.x; i < row_bytes / 16; i += blockDim.x) d[i] = ok ? s[i] : make_uint4(0, 0, 0, 0);
+}
+
 // ------------------------------------------------------------------ host
+static PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+static int encode_2d(CUtensorMap* m, const void* base, uint64_t inner_bytes, uint64_t rows, uint32_t box_x,
+                     uint32_t box_y, bool swizzle128) {
+  if (!g_encode) {
+    cudaDriverEntryPointQueryResult q;
+    void* fn = nullptr;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !fn)
+      return VQ2_ERR_CUDA;
+    g_encode = (PFN_cuTensorMapEncodeTiled_v12000)fn;
+  }
+  const cuuint64_t dims[2] = {inner_bytes, rows};
+  const cuuint64_t strides[1] = {inner_bytes};
+  const cuuint32_t box[2] = {box_x, box_y};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = g_encode(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE,
+                        swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_128B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? VQ2_OK : VQ2_ERR_CUDA;
+}
+
 struct PfLayout {
   long M, Pmax, nblk, nchunks;
-  size_t off_st, off_ss, off_val, off_be, off_counts, off_xq, off_invx, off_inter, off_vb, off_invvb, total;
+  size_t off_st, off_ss, off_val, off_be, off_counts, off_xq, off_invx, off_xs, off_inter, off_vb, off_invvb, total;
 };
 
 static size_t up256(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -508,6 +542,7 @@ static PfLayout pf_layout(int N, int k, int E, int H, int I, int prec) {
   L.off_counts = o; o = up256(o + L.nchunks * E * 4);
   L.off_xq = o; o = up256(o + (size_t)N * H * elem);
   L.off_invx = o; o = up256(o + (size_t)N * 4);
+  L.off_xs = o; o = up256(o + (size_t)L.Pmax * H * elem);
   L.off_inter = o; o = up256(o + (size_t)L.Pmax * I * 4);
   L.off_vb = o; o = up256(o + (size_t)L.Pmax * I * elem);
   L.off_invvb = o; o = up256(o + (size_t)L.Pmax * 4);
@@ -552,6 +587,7 @@ extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_
   int32_t* be = (int32_t*)(w + L.off_be);
   int* counts = (int*)(w + L.off_counts);
   uint8_t* xq = w + L.off_xq;
+  uint8_t* xs = w + L.off_xs;
   float* invx = (float*)(w + L.off_invx);
   float* inter = (float*)(w + L.off_inter);
   uint8_t* vb = w + L.off_vb;
@@ -575,6 +611,7 @@ extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_
   if (cudaMemsetAsync(a->out, 0, (size_t)a->N * a->H * sizeof(float), st_) != cudaSuccess) return VQ2_ERR_CUDA;
 
   PfGemmArgs g = {};
+  g.act = nullptr;
   g.st = st; g.ss = ss; g.val = val; g.be = be; g.topk_w = a->topk_w; g.inter = inter; g.out = a->out;
   g.I = a->I; g.H = a->H; g.topk = a->topk;
   if (prec == VQ2_PREC_FP8) {
@@ -582,22 +619,31 @@ extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_
   } else {
     had_quant_rows_kernel<VQ2_PREC_F16><<<a->N, 256, 0, st_>>>(a->x, a->x_dtype, nullptr, a->H, xq, invx);
   }
+  const int elem = prec == VQ2_PREC_FP8 ? 1 : 2;
+  const int lob = 128 / elem / 4;
+  gather_slot_rows_kernel<<<(unsigned)L.Pmax, 256, 0, st_>>>(xq, st, val, a->H * elem, xs);
+  CUtensorMap tm_x, tm_v, tm_l13, tm_l2;
+  if (encode_2d(&tm_x, xs, (uint64_t)a->H * elem, L.Pmax, 128, 128, true) ||
+      encode_2d(&tm_v, vb, (uint64_t)a->I * elem, L.Pmax, 128, 128, true) ||
+      encode_2d(&tm_l13, a->w13_lo, a->H / 4, (uint64_t)a->E * 2 * a->I, lob, 64, false) ||
+      encode_2d(&tm_l2, a->w2_lo, a->I / 4, (uint64_t)a->E * a->H, lob, 64, false))
+    return VQ2_ERR_CUDA;
   // gate/up
-  g.act = xq; g.inv_act = invx; g.lo = a->w13_lo; g.hi = a->w13_hi; g.sc = a->w13_sc; g.cb = a->w13_cb;
+  g.inv_act = invx; g.lo = a->w13_lo; g.hi = a->w13_hi; g.sc = a->w13_sc; g.cb = a->w13_cb;
   g.K = a->H; g.R = 2 * a->I;
   dim3 g1(a->I / 64, (unsigned)L.nblk);
-  if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, true><<<g1, PF_THREADS, PF_SMEM, st_>>>(g);
-  else prefill_gemm_kernel<VQ2_PREC_F16, true><<<g1, PF_THREADS, PF_SMEM, st_>>>(g);
+  if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, true><<<g1, PF_THREADS, PF_SMEM, st_>>>(g, tm_x, tm_l13);
+  else prefill_gemm_kernel<VQ2_PREC_F16, true><<<g1, PF_THREADS, PF_SMEM, st_>>>(g, tm_x, tm_l13);
   // inter -> Hadamard -> quantised activation of the down projection
   if (prec == VQ2_PREC_FP8)
     had_quant_rows_kernel<VQ2_PREC_FP8><<<(unsigned)L.Pmax, 256, 0, st_>>>(inter, VQ2_DT_F32, val, a->I, vb, invvb);
   else
     had_quant_rows_kernel<VQ2_PREC_F16><<<(unsigned)L.Pmax, 256, 0, st_>>>(inter, VQ2_DT_F32, val, a->I, vb, invvb);
   // down + combine
-  g.act = vb; g.inv_act = invvb; g.lo = a->w2_lo; g.hi = a->w2_hi; g.sc = a->w2_sc; g.cb = a->w2_cb;
+  g.inv_act = invvb; g.lo = a->w2_lo; g.hi = a->w2_hi; g.sc = a->w2_sc; g.cb = a->w2_cb;
   g.K = a->I; g.R = a->H;
   dim3 g2(a->H / PF_BN, (unsigned)L.nblk);
-  if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, false><<<g2, PF_THREADS, PF_SMEM, st_>>>(g);
-  else prefill_gemm_kernel<VQ2_PREC_F16, false><<<g2, PF_THREADS, PF_SMEM, st_>>>(g);
+  if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, false><<<g2, PF_THREADS, PF_SMEM, st_>>>(g, tm_v, tm_l2);
+  else prefill_gemm_kernel<VQ2_PREC_F16, false><<<g2, PF_THREADS, PF_SMEM, st_>>>(g, tm_v, tm_l2);
   return cudaGetLastError() == cudaSuccess ? VQ2_OK : VQ2_ERR_CUDA;
 }
