@@ -175,6 +175,39 @@ def time_decode(layers, xs, routes, steps, warmup, stream, soak_s=0.6):
     return s.elapsed_time(e) / steps
 
 
+def time_prefill(layers, dev, args, N=8192):
+    """Config 2: one prefill layer call (8192 tokens, Zipf(1.1) top-8), both operand precisions.
+    CUDA events around `reps` calls (layers cycled), after warm-up."""
+    from vq2_vllm import synth
+    from vq2_vllm.kernels.ds4_vq2_cuda import vq2_moe_grouped_wmma
+    _, bf16_peak, src = peaks()
+    x = synth.make_tokens(N, H, seed=300, device=dev)
+    ids, tw = synth.route_zipf(N, E, K, s=1.1, seed=301, device=dev)
+    flops = 2.0 * N * K * H * 2 * I + 2.0 * N * K * I * H
+    res = {"workload": "config2 prefill: 8192 tokens, Zipf(1.1) top-8, H=4096 I=2048 E=256",
+           "algorithmic_tflop_per_call": flops / 1e12}
+    reps = max(3, min(args.steps, 10))
+    for prec in ("fp8", "f16"):
+        for i in range(3):
+            vq2_moe_grouped_wmma(x, ids, tw, *synth.layer_args(layers[i % len(layers)]), precision=prec)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        s.record()
+        for i in range(reps):
+            vq2_moe_grouped_wmma(x, ids, tw, *synth.layer_args(layers[i % len(layers)]), precision=prec)
+        e.record()
+        e.synchronize()
+        ms = s.elapsed_time(e) / reps
+        tf = flops / (ms * 1e-3) / 1e12
+        peak = 2 * bf16_peak if prec == "fp8" else bf16_peak
+        res[prec] = {"ms_per_call": ms, "tok_per_s": N / (ms * 1e-3), "tflops": tf,
+                     "roofline": {"bound": "tensor", "achieved": tf, "peak": peak, "unit": "TFLOP/s",
+                                  "frac": tf / peak,
+                                  "peak_source": (f"2x {src} bf16 (fp8 dense rate is twice bf16)" if prec == "fp8"
+                                                  else f"{src} bf16 (fp16 rate equals bf16)")}}
+    return res
+
+
 def run_ours(args, rank, world):
     from vq2_vllm import synth
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
@@ -228,6 +261,8 @@ def run_ours(args, rank, world):
     h2d = H * 2 + K * 4 + K * 4
     d2h = H * 4
 
+    prefill = time_prefill(layers, dev, args)
+
     cpu_v, cpu_sample = (None, None)
     if not args.no_cpu:
         cpu_v, cpu_sample = cpu_reference_us_per_token(os.cpu_count() or 1)
@@ -249,6 +284,7 @@ def run_ours(args, rank, world):
             "cpu_baseline": {"value": cpu_v, "unit": "us/token", "cores": os.cpu_count(), "kind": "port",
                              "sample": cpu_sample},
             "e2e": {"value": e2e_ms * 1e3, "unit": "us/token", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "prefill": prefill,
             "gpu_launches": 2 * args.steps,
             "clocks": clocks}
     print(json.dumps(line), flush=True)
