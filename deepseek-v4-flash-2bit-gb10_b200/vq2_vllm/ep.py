@@ -17,6 +17,10 @@ and scales (codebooks are replicated). One layer call:
 
 Split sizes are read on the host (one device-to-host read of W counts per call), so a call is
 not capturable in a CUDA graph.
+
+Decode-sized batches use ``ep_moe_gather`` instead: one all_gather of every rank's packed
+(x, ids, w) rows and one reduce_scatter of the fp32 partial outputs — two collectives, no host
+read, every rank applies only its expert window to all gathered tokens.
 """
 from __future__ import annotations
 
@@ -83,6 +87,35 @@ def ep_moe(x, topk_ids, topk_w, expert_fn, E: int, group=None, combine_dtype=tor
     return out
 
 
+def ep_moe_gather(x, topk_ids, topk_w, expert_fn, E: int, group=None):
+    """Expert-parallel MoE for small per-rank batches (every rank the same N): all_gather of the
+    packed token rows, local experts applied to all of them, reduce_scatter of the partial sums."""
+    world = dist.get_world_size(group)
+    rank = dist.get_rank(group)
+    if E % world:
+        raise ValueError(f"vq2 ep: {E} experts do not split evenly over {world} ranks")
+    per = E // world
+    N, H = x.shape
+    k = topk_ids.shape[1]
+    xb = H * x.element_size()
+    row = torch.cat([x.contiguous().view(torch.uint8).view(N, xb),
+                     topk_ids.to(torch.int32).contiguous().view(torch.uint8).view(N, 4 * k),
+                     topk_w.float().contiguous().view(torch.uint8).view(N, 4 * k)], 1)
+    allrows = torch.empty(world * N, row.shape[1], dtype=torch.uint8, device=x.device)
+    dist.all_gather_into_tensor(allrows, row, group=group)
+    xa = allrows[:, :xb].contiguous().view(x.dtype).view(world * N, H)
+    ia = allrows[:, xb:xb + 4 * k].contiguous().view(torch.int32).view(world * N, k)
+    wa = allrows[:, xb + 4 * k:].contiguous().view(torch.float32).view(world * N, k)
+    part = expert_fn(xa, ia, wa, rank * per, per).float().contiguous()
+    out = torch.empty(N, H, dtype=torch.float32, device=x.device)
+    if dist.get_backend(group) == "gloo":        # gloo has no reduce_scatter
+        dist.all_reduce(part, group=group)
+        out.copy_(part[rank * N:(rank + 1) * N])
+    else:
+        dist.reduce_scatter_tensor(out, part, group=group)
+    return out
+
+
 def local_layer(layer: dict, rank: int, world: int) -> dict:
     """This rank's slice of a full layer dict (experts [rank*E/W, (rank+1)*E/W))."""
     E = layer["w13_lo"].shape[0]
@@ -126,7 +159,8 @@ def bench_ep(args, rank, world, metric):
     def run(per_rank, steps, warmup):
         xs = [synth.make_tokens(per_rank, H, seed=50 + 97 * rank + j, device=dev) for j in range(8)]
         rs = [synth.route_uniform(per_rank, E, K, seed=500 + 97 * rank + j, device=dev) for j in range(8)]
-        step = lambda i: ep_moe(xs[i % 8], rs[i % 8][0], rs[i % 8][1], fns[i % nlayers], E)
+        moe = ep_moe_gather if per_rank * world <= 512 else ep_moe
+        step = lambda i: moe(xs[i % 8], rs[i % 8][0], rs[i % 8][1], fns[i % nlayers], E)
         for i in range(warmup):
             step(i)
         torch.cuda.synchronize()

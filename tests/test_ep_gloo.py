@@ -44,8 +44,9 @@ def _worker(rank, world, port, q, fail_rank):
         if rank == fail_rank:
             raise RuntimeError("injected failure before dispatch")
         out = ep.ep_moe(x, ids, w, fn, E)
+        out_g = ep.ep_moe_gather(x, ids, w, fn, E)
         ref = torch_ref.moe_ref(x, ids, w, layer)
-        q.put((rank, "ok", torch_ref.rel_l2(out, ref)))
+        q.put((rank, "ok", max(torch_ref.rel_l2(out, ref), torch_ref.rel_l2(out_g, ref))))
     except Exception as ex:  # reported to the parent
         q.put((rank, "error", repr(ex)))
     finally:

@@ -1,0 +1,65 @@
+"""Expert-parallel decode and prefill over NCCL on 2 GPUs (skipped with fewer), against the fp32
+oracle of the same full layer. NVLS is off (NCCL_NVLS_ENABLE=0) in the child ranks."""
+import os
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, q):
+    import datetime
+    import sys
+    here = os.path.dirname(os.path.abspath(__file__))
+    sys.path.insert(0, os.path.join(os.path.dirname(here), "deepseek-v4-flash-2bit-gb10_b200"))
+    sys.path.insert(0, os.path.dirname(here))
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    import torch.distributed as dist
+    from oracle import torch_ref
+    from vq2_vllm import ep, synth
+    try:
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", rank=rank, world_size=world, device_id=dev,
+                                timeout=datetime.timedelta(seconds=60))
+        E, H, I = 32, 4096, 2048
+        layer = synth.make_layer(E, H, I, seed=0, device=dev)
+        local = {k: v.clone() for k, v in ep.local_layer(layer, rank, world).items()}
+        fn = ep.cuda_expert_fn(local)
+        res = []
+        for N, mode in ((4, "gather"), (4, "a2a"), (300, "a2a")):
+            x = synth.make_tokens(N, H, seed=10 + rank, device=dev)
+            ids, w = synth.route_uniform(N, E, 8, seed=20 + rank, device=dev)
+            out = (ep.ep_moe_gather if mode == "gather" else ep.ep_moe)(x, ids, w, fn, E)
+            res.append(torch_ref.rel_l2(out, torch_ref.moe_ref(x, ids, w, layer)))
+        q.put((rank, "ok", max(res)))
+        dist.destroy_process_group()
+    except Exception as ex:
+        q.put((rank, "error", repr(ex)))
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_two_gpus():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = sorted(q.get(timeout=300) for _ in range(2))
+    for p in ps:
+        p.join(timeout=60)
+    for rank, status, val in res:
+        assert status == "ok", val
+        assert val < 1e-2
