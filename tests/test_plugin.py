@@ -1,0 +1,64 @@
+"""The vLLM boundary: registration, parameter contract, weight loading (CPU) and apply (GPU)."""
+import pytest
+import torch
+
+
+def test_param_shapes_match_reference_contract():
+    from vq2_vllm.plugin import param_shapes
+    s = param_shapes(256, 4096, 2048)
+    assert s["w13_lo"] == ((256, 4096, 1024), torch.uint8)
+    assert s["w13_hi"] == ((256, 4096, 256), torch.uint8)
+    assert s["w13_sc"] == ((256, 4096, 64), torch.float16)
+    assert s["w2_lo"] == ((256, 4096, 512), torch.uint8)
+    assert s["w2_sc"] == ((256, 4096, 32), torch.float16)
+    assert s["w13_cb"] == ((1024, 4), torch.float16)
+
+
+def test_weight_loader_places_gate_and_up_halves():
+    from vq2_vllm.plugin import weight_loader
+    p = torch.nn.Parameter(torch.zeros(2, 8, 4, dtype=torch.uint8), requires_grad=False)
+    weight_loader(p, torch.full((4, 4), 1, dtype=torch.uint8), "w13_lo", "w1", 1)
+    weight_loader(p, torch.full((4, 4), 3, dtype=torch.uint8), "w13_lo", "w3", 1)
+    assert p[1, :4].eq(1).all() and p[1, 4:].eq(3).all() and p[0].eq(0).all()
+    cb = torch.nn.Parameter(torch.zeros(1024, 4, dtype=torch.float16), requires_grad=False)
+    weight_loader(cb, torch.ones(1024, 4), "w13_cb", None, None)
+    assert cb.eq(1).all()
+
+
+def test_register_with_vllm():
+    pytest.importorskip("vllm")
+    import vq2_vllm
+    from vllm.model_executor.layers.quantization import get_quantization_config
+    cls = vq2_vllm.register()
+    assert get_quantization_config("vq2") is cls
+    cfg = cls.from_config({"quant_method": "vq2", "vdim": 4, "k": 1024, "group": 64})
+    assert cfg.get_name() == "vq2" and cfg.group == 64
+    with pytest.raises(ValueError):
+        cls.from_config({"vdim": 8})
+
+
+def test_bare_module_names_resolve():
+    import sys
+
+    import vq2_vllm  # noqa: F401
+    assert hasattr(sys.modules["vq2_kernel"], "vq2_moe_fused_10b")
+    assert hasattr(sys.modules["moe_align"], "moe_align")
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("N", [3, 300])
+def test_apply_dispatch_matches_oracle(N):
+    """apply(): decode kernel below VQ2_WMMA_MIN tokens, grouped GEMM at or above (fp8 default)."""
+    from types import SimpleNamespace
+
+    from oracle import torch_ref
+    from vq2_vllm import synth
+    from vq2_vllm.plugin import apply_moe
+    L = synth.make_layer(16, 1024, 512, seed=0, device="cuda")
+    layer = SimpleNamespace(**L)
+    x = synth.make_tokens(N, 1024, seed=1, device="cuda")
+    ids, w = synth.route_uniform(N, 16, 8, seed=2, device="cuda")
+    out = apply_moe(layer, x, w, ids)
+    assert out.dtype == x.dtype
+    ref = torch_ref.moe_ref(x, ids, w, L) if N < 256 else torch_ref.moe_prefill_fp8_ref(x, ids, w, L)
+    assert torch_ref.rel_l2(out.float(), ref) < 3e-2
