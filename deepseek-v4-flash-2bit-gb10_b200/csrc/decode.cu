@@ -30,10 +30,19 @@ namespace vq2 {
 constexpr int DEC_NW = VQ2_DEC_NW;        // consumer warps
 constexpr int DEC_THREADS = (DEC_NW + 1) * 32;
 constexpr int DEC_TT = 1;                 // tokens per unit (a unit = one (expert, token) pair)
-constexpr int DEC_STAGES = 3;
+#ifndef VQ2_DEC_STAGES
+#define VQ2_DEC_STAGES 3
+#endif
+#ifndef VQ2_DEC_SA
+#define VQ2_DEC_SA 8
+#endif
+#ifndef VQ2_DEC_SB
+#define VQ2_DEC_SB 32
+#endif
+constexpr int DEC_STAGES = VQ2_DEC_STAGES;
 constexpr int DEC_GRAN = 8;               // row granule of the work split (keeps copies 16-B sized)
-constexpr int DEC_SA = 8;                 // gate/up row pairs per stage
-constexpr int DEC_SB = 32;                // down rows per stage
+constexpr int DEC_SA = VQ2_DEC_SA;        // gate/up row pairs per stage
+constexpr int DEC_SB = VQ2_DEC_SB;        // down rows per stage
 constexpr int DEC_MAXG = 64;              // max 64-groups per input row (4096 / 64)
 constexpr int CB_COPIES = 16;
 constexpr int CB_BYTES = 1024 * 8 * CB_COPIES;   // 128 KB
@@ -188,14 +197,20 @@ __device__ __forceinline__ void multi_dot(const uint4* lo, const uint32_t* hw, c
     for (int t = 0; t < NT; ++t) { a0[r][t] = __float2half2_rn(0.f); a1[r][t] = a0[r][t]; }
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
+    uint32_t ids[R][2];
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const uint32_t L = q == 0 ? lo[r].x : q == 1 ? lo[r].y : q == 2 ? lo[r].z : lo[r].w;
+      unpack_ids4(L, __byte_perm(hw[r], 0u, 0x4440 + q), ids[r][0], ids[r][1]);
+    }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int s = 4 * q + j;
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        const uint32_t L = q == 0 ? lo[r].x : q == 1 ? lo[r].y : q == 2 ? lo[r].z : lo[r].w;
-        const uint32_t off = (((L >> (8 * j)) & 0xFFu) << 7) | (((hw[r] >> (8 * q + 2 * j)) & 3u) << 15);
-        const uint2 c = *(const uint2*)(cbl + off);
+        const uint32_t w = ids[r][j & 1];
+        const uint32_t id = (j & 2) ? (w >> 16) : (w & 0xFFFFu);
+        const uint2 c = *(const uint2*)(cbl + (id << 7));
         const __half2 c01 = *(const __half2*)&c.x, c23 = *(const __half2*)&c.y;
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
@@ -496,7 +511,10 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
     if (!mbar_wait(&sh->full[slot], (c / DEC_STAGES) & 1)) break;
     if (threadIdx.x == 0 && c == 0) PROBE(0, 3);
     const uint8_t* st = d.stages + slot * stage_b;
-    if (S / rstep >= 2) {
+    if (S / rstep >= 4) {
+      for (int rr0 = rsub; rr0 < n; rr0 += 4 * rstep)
+        gateup_rows<4>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, sc_b, cbl, xr, inv, mcur, KH, h, I, i0, part);
+    } else if (S / rstep >= 2) {
       for (int rr0 = rsub; rr0 < n; rr0 += 2 * rstep)
         gateup_rows<2>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, sc_b, cbl, xr, inv, mcur, KH, h, I, i0, part);
     } else {
@@ -608,9 +626,12 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
     if (S / rstep >= 8) {
       for (int rr0 = rsub; rr0 < n; rr0 += 8 * rstep)
         down_rows<8>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, tok, H, h0, a.out);
-    } else {
+    } else if (S / rstep >= 4) {
       for (int rr0 = rsub; rr0 < n; rr0 += 4 * rstep)
         down_rows<4>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, tok, H, h0, a.out);
+    } else {
+      for (int rr0 = rsub; rr0 < n; rr0 += 2 * rstep)
+        down_rows<2>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, tok, H, h0, a.out);
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&sh->empty[slot]);

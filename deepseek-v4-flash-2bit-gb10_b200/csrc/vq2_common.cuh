@@ -103,6 +103,17 @@ __device__ __forceinline__ float2 f16_range_scale(float amax) {
   return make_float2(ldexpf(1.f, s), ldexpf(1.f, -s));
 }
 
+// The four 10-bit indices of one lo word (4 index low bytes) and its hi byte hb (four 2-bit
+// fields, sub-vector j in bits 2j..2j+1), as two words with two 16-bit ids each:
+// ids02 = id0 | id2 << 16, ids13 = id1 | id3 << 16. Byte permutes place the low bytes; a multiply
+// spreads hb into both halves so one masked OR adds the two hi bits.
+__device__ __forceinline__ void unpack_ids4(uint32_t lo_word, uint32_t hb, uint32_t& ids02, uint32_t& ids13) {
+  const uint32_t e02 = __byte_perm(lo_word, 0u, 0x4240);   // [b0, 0, b2, 0]
+  const uint32_t e13 = __byte_perm(lo_word, 0u, 0x4341);   // [b1, 0, b3, 0]
+  ids02 = e02 | ((hb * 0x00100100u) & 0x03000300u);         // hb bits 0-1 -> 8-9, bits 4-5 -> 24-25
+  ids13 = e13 | ((hb * 0x00040040u) & 0x03000300u);         // hb bits 2-3 -> 8-9, bits 6-7 -> 24-25
+}
+
 __device__ __forceinline__ int load_id(const void* ids, int ids_dtype, int m) {
   return ids_dtype == VQ2_ID_I64 ? (int)((const long long*)ids)[m] : ((const int*)ids)[m];
 }
