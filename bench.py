@@ -225,7 +225,7 @@ def run_ours(args, rank, world):
         routes = [make_routing(xs[j], seed=200 + j) for j in range(8)]
         distinct = sum(torch.unique(routes[j % 8][0]).numel() for j in range(args.steps)) / args.steps
         with Clocks(dev.index) as ck:
-            ms = time_decode(layers, xs, routes, args.steps, max(args.warmup, 3), stream)
+            ms = time_decode(layers, xs, routes, args.steps, max(args.warmup, 3), stream, soak_s=args.soak)
         res[B] = (ms, distinct, ck.summary())
     ms1, u1, clocks = res[1]
     us_tok = ms1 * 1e3 / 1
@@ -277,7 +277,11 @@ def run_ours(args, rank, world):
             "decode_b3": {"us_per_token": ms3 * 1e3 / 3, "us_per_layer_call": ms3 * 1e3, "distinct_experts": u3,
                           "idx_act_GBps": (u3 * IDX_BYTES_PER_EXPERT + 3 * H * 6) / (ms3 * 1e-3) / 1e9},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                         "frac": achieved / hbm, "traffic": None,
+                         "frac": achieved / hbm,
+                         # dram read+write of one layer call (both decode kernels), from the ncu
+                         # capture summarised in profiles/decode_config1_b1.txt (8 distinct experts)
+                         "traffic": 69.7e6, "traffic_unit": "bytes per layer call",
+                         "kernel": "decode layer call (gate/up + down kernels, CUDA events around both)",
                          "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src,
                          "bytes": "index planes of distinct experts + x + out per layer call",
                          "achieved_incl_scales": all_bytes / (ms1 * 1e-3) / 1e9},
@@ -297,6 +301,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
+    ap.add_argument("--soak", type=float, default=0.6, help="untimed seconds before the timed decode steps")
     args = ap.parse_args()
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
