@@ -34,29 +34,31 @@ int launch_align_ex(const void* ids, int dt, long N, int k, int E, int BM, int b
 
 constexpr int PF_BM = 128;            // slots per block (MMA M)
 constexpr int PF_BN = 128;            // weight rows per tile (MMA N)
-constexpr int PF_STAGES = 5;          // ring of (A tile, index planes): memory latency
+constexpr int PF_MB = 2;              // blocks of one expert sharing each decoded B tile
+constexpr int PF_STAGES = 3;          // ring of (A tiles of PF_MB blocks, index planes): memory latency
 constexpr int PF_BSTAGES = 2;         // ring of decoded B tiles: produced in the CTA
-constexpr int PF_DEC_WARPS = 8;
+constexpr int PF_DEC_WARPS = 16;      // decoders; four per TMEM lane quarter in the epilogue
 constexpr int PF_THREADS = (2 + PF_DEC_WARPS) * 32;
 constexpr int PF_TILE = 16384;        // one 128 x 128-byte operand tile
+constexpr int PF_ATILE = PF_MB * PF_TILE;
 constexpr int PF_CB_COPIES = 8;
 constexpr int PF_CB_BYTES = 1024 * 8 * PF_CB_COPIES;
 constexpr int PF_IDX = 6144;   // staged index planes of one stage: lo 4096 B, hi 1024 B, sc 512 B (padded)
 static_assert(PF_IDX % 1024 == 0, "index stages keep the following tiles 1024-byte aligned");
-constexpr int PF_TMEM_COLS = 128;
+constexpr int PF_TMEM_COLS = PF_MB * PF_BN;
 
 struct PfShared {
   uint64_t full_a[PF_STAGES];
   uint64_t empty[PF_STAGES];
   uint64_t full_b[PF_BSTAGES];
   uint64_t empty_b[PF_BSTAGES];
-  uint64_t done;
+  uint64_t done[2];             // per pass: all MMAs of the pass complete
   uint64_t cbbar;
   uint32_t tmem_base;
-  int slot_tok[PF_BM];
+  int slot_tok[PF_MB * PF_BM];
 };
 
-constexpr size_t PF_SMEM = (size_t)PF_CB_BYTES + (size_t)PF_STAGES * (PF_TILE + PF_IDX) + (size_t)PF_BSTAGES * PF_TILE +
+constexpr size_t PF_SMEM = (size_t)PF_CB_BYTES + (size_t)PF_STAGES * (PF_ATILE + PF_IDX) + (size_t)PF_BSTAGES * PF_TILE +
                            sizeof(PfShared) + 1024;
 
 struct PfGemmArgs {
@@ -132,6 +134,17 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
+  uint32_t r[16];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]),
+                 "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile("cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
                ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
@@ -150,52 +163,57 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int kc) {
 }
 
 // ------------------------------------------------------------------ weight tile decode
-// Decode 16-byte chunks [4h, 4h+4) of B row r of one stage:
-// fp8: 16 sub-vectors (one 64-group) -> 64 e4m3 values = e4m3(sat(C[id] * sc)) (reference
-//      vq2_grouped.cu:434-446); f16: 8 sub-vectors -> 32 f16 values C[id] * sc.
+// Decoder thread (row r, quarter h) fills 16-byte chunks 2h, 2h+1 of B row r of one stage:
+// fp8: 8 sub-vectors -> 32 e4m3 values = e4m3(sat(C[id] * sc)) (reference vq2_grouped.cu:434-446);
+// f16: 4 sub-vectors -> 16 f16 values C[id] * sc. lo: the sub-vectors' low bytes (little-endian
+// in lo.x, lo.y); hw: their hi bits (2 per sub-vector from bit 0). cbl: this lane's codebook copy.
 template <int PREC>
-__device__ __forceinline__ void decode_b_row(const uint8_t* cbl, uint4 lo, uint32_t hw, float scf, uint8_t* tile,
-                                             int r, int h) {
+__device__ __forceinline__ void decode_b_quarter(const uint8_t* cbl, uint2 lo, uint32_t hw, float scf, uint8_t* tile,
+                                                 int r, int h) {
   if (PREC == VQ2_PREC_FP8) {
-    const uint32_t lw[4] = {lo.x, lo.y, lo.z, lo.w};
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
+    for (int q = 0; q < 2; ++q) {            // chunk 2h+q: sub-vectors 4q..4q+3
+      uint32_t ids[2];
+      unpack_ids4(q ? lo.y : lo.x, (hw >> (8 * q)) & 0xFFu, ids[0], ids[1]);
       uint32_t packed[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
-        const uint32_t off = (((lw[q] >> (8 * j)) & 0xFFu) << 6) | (((hw >> (8 * q + 2 * j)) & 3u) << 14);
-        const uint2 c = *(const uint2*)(cbl + off);
+        const uint32_t id = (j & 2) ? (ids[j & 1] >> 16) : (ids[j & 1] & 0xFFFFu);
+        const uint2 c = *(const uint2*)(cbl + (id << 6));
         const float2 a = __half22float2(*(const __half2*)&c.x), b = __half22float2(*(const __half2*)&c.y);
         const __nv_fp8x2_storage_t p0 = __nv_cvt_float2_to_fp8x2(make_float2(a.x * scf, a.y * scf), __NV_SATFINITE, __NV_E4M3);
         const __nv_fp8x2_storage_t p1 = __nv_cvt_float2_to_fp8x2(make_float2(b.x * scf, b.y * scf), __NV_SATFINITE, __NV_E4M3);
         packed[j] = (uint32_t)p0 | ((uint32_t)p1 << 16);
       }
-      *(uint4*)(tile + sw128_off(r, 4 * h + q)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      *(uint4*)(tile + sw128_off(r, 2 * h + q)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
     }
   } else {
     const __half2 s2 = __float2half2_rn(scf);
-    const uint32_t lw[2] = {lo.x, lo.y};
+    uint32_t ids[2];
+    unpack_ids4(lo.x, hw & 0xFFu, ids[0], ids[1]);
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {         // chunk q: sub-vectors 2q, 2q+1 (8 f16)
+    for (int q = 0; q < 2; ++q) {            // chunk 2h+q: sub-vectors 2q, 2q+1 (8 f16)
       uint32_t w[4];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
-        const int s = 2 * q + j;
-        const uint32_t off = (((lw[s >> 2] >> (8 * (s & 3))) & 0xFFu) << 6) | (((hw >> (2 * s)) & 3u) << 14);
-        const uint2 c = *(const uint2*)(cbl + off);
+      for (int jj = 0; jj < 2; ++jj) {
+        const int j = 2 * q + jj;
+        const uint32_t id = (j & 2) ? (ids[j & 1] >> 16) : (ids[j & 1] & 0xFFFFu);
+        const uint2 c = *(const uint2*)(cbl + (id << 6));
         const __half2 v0 = __hmul2(*(const __half2*)&c.x, s2), v1 = __hmul2(*(const __half2*)&c.y, s2);
-        w[2 * j] = *(const uint32_t*)&v0;
-        w[2 * j + 1] = *(const uint32_t*)&v1;
+        w[2 * jj] = *(const uint32_t*)&v0;
+        w[2 * jj + 1] = *(const uint32_t*)&v1;
       }
-      *(uint4*)(tile + sw128_off(r, 4 * h + q)) = make_uint4(w[0], w[1], w[2], w[3]);
+      *(uint4*)(tile + sw128_off(r, 2 * h + q)) = make_uint4(w[0], w[1], w[2], w[3]);
     }
   }
 }
 
 // ------------------------------------------------------------------ grouped GEMM kernel
-// grid (tiles along N, blocks of 128 slots). GATEUP: tile n covers gate rows [64n, 64n+64) and
-// the matching up rows; the epilogue writes inter. Otherwise tile n covers output rows
-// [128n, 128n+128) and the epilogue accumulates into out.
+// grid (tiles along N, pairs of 128-slot blocks). GATEUP: tile n covers gate rows [64n, 64n+64)
+// and the matching up rows; the epilogue writes inter. Otherwise tile n covers output rows
+// [128n, 128n+128) and the epilogue accumulates into out. Two blocks of the same expert run as
+// one pass (each decoded B tile feeds two MMAs, two TMEM accumulators); two blocks of different
+// experts run as two passes, one accumulator each.
 #ifdef VQ2_PF_PROBE
 // Development probe (off in the product build): global-timer stamps per stage of CTA (0, 0).
 __device__ unsigned long long g_pf_probe[4][64];
@@ -215,26 +233,41 @@ __device__ __forceinline__ long pf_weight_row(const PfGemmArgs& a, int e, int ti
   return (long)e * a.R + tile * PF_BN + r;
 }
 
+struct PfPass {
+  int blk;      // first block of the pass
+  int mb;       // blocks in the pass (1 or 2)
+  int e;        // local expert
+  int acc;      // first TMEM accumulator
+};
+
 template <int PREC, bool GATEUP>
 __global__ void __launch_bounds__(PF_THREADS, 1)
-prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_lo) {
+prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_lo,
+                    int nblk) {
   extern __shared__ __align__(1024) uint8_t pf_smem_raw[];
   uint8_t* smem = (uint8_t*)(((uintptr_t)pf_smem_raw + 1023) & ~(uintptr_t)1023);
   uint8_t* cbs = smem;
-  uint8_t* atiles = smem + PF_CB_BYTES;                // A ring
-  uint8_t* btiles = atiles + PF_STAGES * PF_TILE;      // B ring
+  uint8_t* atiles = smem + PF_CB_BYTES;                // A ring (PF_MB tiles per stage)
+  uint8_t* btiles = atiles + PF_STAGES * PF_ATILE;     // B ring
   uint8_t* itiles = btiles + PF_BSTAGES * PF_TILE;     // index-plane ring
   PfShared* sh = (PfShared*)(itiles + PF_STAGES * PF_IDX);
-  const int blk = blockIdx.y, tile = blockIdx.x;
+  const int tile = blockIdx.x, b0 = blockIdx.y * PF_MB;
   if (threadIdx.x == 0) PF_PROBE(3, 0);
-  if (!a.val[(size_t)blk * PF_BM]) return;           // blocks past the last expert hold no pair
+  if (!a.val[(size_t)b0 * PF_BM]) return;            // blocks past the last expert hold no pair
+  const bool v1 = b0 + 1 < nblk && a.val[(size_t)(b0 + 1) * PF_BM];
+  const int e0 = a.be[b0], e1 = v1 ? a.be[b0 + 1] : -1;
+  PfPass pass[2];
+  int npass;
+  if (v1 && e1 == e0) { pass[0] = {b0, 2, e0, 0}; npass = 1; }
+  else if (v1) { pass[0] = {b0, 1, e0, 0}; pass[1] = {b0 + 1, 1, e1, 1}; npass = 2; }
+  else { pass[0] = {b0, 1, e0, 0}; npass = 1; }
+
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int e = a.be[blk];
   constexpr int elem = PREC == VQ2_PREC_FP8 ? 1 : 2;
   constexpr int KE = 128 / elem;                      // K elements per stage (128 bytes per row)
   const int nchunks = a.K / KE;
   const int nsub = a.K / 4, ngk = a.K / 64;
-  auto A_t = [&](int slot) { return atiles + slot * PF_TILE; };
+  auto A_t = [&](int slot) { return atiles + slot * PF_ATILE; };
   auto B_t = [&](int slot) { return btiles + slot * PF_TILE; };
   auto I_t = [&](int slot) { return itiles + slot * PF_IDX; };   // lo | hi | sc
 
@@ -247,15 +280,17 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
       mbar_init(&sh->full_b[s], PF_DEC_WARPS);
       mbar_init(&sh->empty_b[s], 1);
     }
-    mbar_init(&sh->done, 1);
+    mbar_init(&sh->done[0], 1);
+    mbar_init(&sh->done[1], 1);
     mbar_init(&sh->cbbar, 1);
     fence_mbar_init();
     mbar_arrive_expect_tx(&sh->cbbar, 1024 * 8);
-    bulk_g2s(B_t(0), a.cb, 1024 * 8, &sh->cbbar);     // codebook lands in stage 0's B tile first
+    bulk_g2s(B_t(0), a.cb, 1024 * 8, &sh->cbbar);     // codebook lands in a B tile first
   }
-  for (int i = threadIdx.x; i < PF_BM; i += blockDim.x) {
-    const size_t p = (size_t)blk * PF_BM + i;
-    sh->slot_tok[i] = a.val[p] ? a.st[p] : -1;
+  for (int i = threadIdx.x; i < PF_MB * PF_BM; i += blockDim.x) {
+    const size_t p = (size_t)b0 * PF_BM + i;
+    const bool in = b0 + i / PF_BM < nblk;
+    sh->slot_tok[i] = (in && a.val[p]) ? a.st[p] : -1;
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -278,128 +313,148 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
   const uint32_t tmem = sh->tmem_base;
 
   if (warp == 0) {
-    // ---------------- loader: A tile + lo plane by TMA, hi / scale planes by cp.async
+    // ---------------- loader: A tiles + lo plane by TMA, hi / scale planes by cp.async
     constexpr int LOB = 128 / elem / 4;               // lo bytes per row per stage (32 fp8, 16 f16)
-    const uint8_t* hi_r[4];
-    const uint8_t* sc_r[4];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const long wr = pf_weight_row<GATEUP>(a, e, tile, lane + 32 * i);
-      hi_r[i] = a.hi + wr * (nsub / 4);
-      sc_r[i] = (const uint8_t*)(a.sc + wr * ngk);
-    }
-    const int row0 = (int)pf_weight_row<GATEUP>(a, e, tile, 0), row1 = (int)pf_weight_row<GATEUP>(a, e, tile, 64);
-    for (int c = 0; c < nchunks; ++c) {
-      const int slot = c % PF_STAGES;
-      if (c >= PF_STAGES && !mbar_wait(&sh->empty[slot], ((c / PF_STAGES) - 1) & 1)) break;
-      const uint32_t ibase = smem_u32(I_t(slot));
-      if (lane == 0) {
-        mbar_arrive_expect_tx(&sh->full_a[slot], PF_TILE + 128 * LOB);
-        tma_load_2d(A_t(slot), &tm_act, c * 128, blk * PF_BM, &sh->full_a[slot]);
-        tma_load_2d(I_t(slot), &tm_lo, c * LOB, row0, &sh->full_a[slot]);
-        tma_load_2d(I_t(slot) + 64 * LOB, &tm_lo, c * LOB, row1, &sh->full_a[slot]);
-      }
+    int gc = 0;                                       // stage counter across passes
+    for (int pi = 0; pi < npass; ++pi) {
+      const PfPass P = pass[pi];
+      const uint8_t* hi_r[4];
+      const uint8_t* sc_r[4];
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const int r = lane + 32 * i;
-        if (PREC == VQ2_PREC_FP8) {          // hi: 8 bytes (32 sub-vectors); scales of 2 groups
-          asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(ibase + 4096 + r * 8), "l"(hi_r[i] + c * 8) : "memory");
-          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + 5120 + r * 4), "l"(sc_r[i] + c * 4) : "memory");
-        } else {                             // hi: 4 bytes (16 sub-vectors); the scale pair holding this group
-          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + 4096 + r * 8), "l"(hi_r[i] + c * 4) : "memory");
-          asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + 5120 + r * 4), "l"(sc_r[i] + (c & ~1) * 2) : "memory");
-        }
+        const long wr = pf_weight_row<GATEUP>(a, P.e, tile, lane + 32 * i);
+        hi_r[i] = a.hi + wr * (nsub / 4);
+        sc_r[i] = (const uint8_t*)(a.sc + wr * ngk);
       }
-      // the stage's full barrier also gets one arrival per lane when its copies above have landed
-      asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&sh->full_a[slot])) : "memory");
-      if (lane == 0) PF_PROBE(0, c);
+      const int row0 = (int)pf_weight_row<GATEUP>(a, P.e, tile, 0), row1 = (int)pf_weight_row<GATEUP>(a, P.e, tile, 64);
+      for (int c = 0; c < nchunks; ++c, ++gc) {
+        const int slot = gc % PF_STAGES;
+        if (gc >= PF_STAGES && !mbar_wait(&sh->empty[slot], ((gc / PF_STAGES) - 1) & 1)) { pi = npass; break; }
+        const uint32_t ibase = smem_u32(I_t(slot));
+        if (lane == 0) {
+          mbar_arrive_expect_tx(&sh->full_a[slot], P.mb * PF_TILE + 128 * LOB);
+          tma_load_2d(A_t(slot), &tm_act, c * 128, P.blk * PF_BM, &sh->full_a[slot]);
+          if (P.mb == 2) tma_load_2d(A_t(slot) + PF_TILE, &tm_act, c * 128, (P.blk + 1) * PF_BM, &sh->full_a[slot]);
+          tma_load_2d(I_t(slot), &tm_lo, c * LOB, row0, &sh->full_a[slot]);
+          tma_load_2d(I_t(slot) + 64 * LOB, &tm_lo, c * LOB, row1, &sh->full_a[slot]);
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int r = lane + 32 * i;
+          if (PREC == VQ2_PREC_FP8) {          // hi: 8 bytes (32 sub-vectors); scales of 2 groups
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(ibase + 4096 + r * 8), "l"(hi_r[i] + c * 8) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + 5120 + r * 4), "l"(sc_r[i] + c * 4) : "memory");
+          } else {                             // hi: 4 bytes (16 sub-vectors); the scale pair holding this group
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + 4096 + r * 8), "l"(hi_r[i] + c * 4) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + 5120 + r * 4), "l"(sc_r[i] + (c & ~1) * 2) : "memory");
+          }
+        }
+        // the stage's full barrier also gets one arrival per lane when its copies above have landed
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&sh->full_a[slot])) : "memory");
+        if (lane == 0) PF_PROBE(0, gc);
+      }
     }
     cp_async_wait<0>();                               // nothing in flight when the CTA retires
   } else if (warp == 1) {
     // ---------------- MMA issuer
     if (lane == 0) {
-      for (int c = 0; c < nchunks; ++c) {
-        const int slot = c % PF_STAGES, bslot = c % PF_BSTAGES;
-        if (!mbar_wait(&sh->full_a[slot], (c / PF_STAGES) & 1)) break;
-        PF_PROBE(1, c);
-        if (!mbar_wait(&sh->full_b[bslot], (c / PF_BSTAGES) & 1)) break;
-        PF_PROBE(2, c);
-        fence_async_smem();                               // cp.async-written A visible to the tensor core
-        tc_fence_after();
-        const uint32_t abase = smem_u32(A_t(slot)), bbase = smem_u32(B_t(bslot));
+      int gc = 0;
+      bool ok = true;
+      for (int pi = 0; pi < npass && ok; ++pi) {
+        const PfPass P = pass[pi];
+        for (int c = 0; c < nchunks; ++c, ++gc) {
+          const int slot = gc % PF_STAGES, bslot = gc % PF_BSTAGES;
+          if (!mbar_wait(&sh->full_a[slot], (gc / PF_STAGES) & 1)) { ok = false; break; }
+          PF_PROBE(1, gc);
+          if (!mbar_wait(&sh->full_b[bslot], (gc / PF_BSTAGES) & 1)) { ok = false; break; }
+          PF_PROBE(2, gc);
+          fence_async_smem();                             // cp.async-written data visible to the tensor core
+          tc_fence_after();
+          const uint32_t abase = smem_u32(A_t(slot)), bbase = smem_u32(B_t(bslot));
+          for (int b = 0; b < P.mb; ++b) {
+            const uint32_t td = tmem + (uint32_t)((P.acc + b) * PF_BN);
 #pragma unroll
-        for (int ks = 0; ks < 4; ++ks)
-          umma<PREC>(tmem, umma_desc_sw128(abase + ks * 32), umma_desc_sw128(bbase + ks * 32), (c | ks) != 0);
-        umma_commit(&sh->empty[slot]);
-        umma_commit(&sh->empty_b[bslot]);
+            for (int ks = 0; ks < 4; ++ks)
+              umma<PREC>(td, umma_desc_sw128(abase + b * PF_TILE + ks * 32), umma_desc_sw128(bbase + ks * 32),
+                         (c | ks) != 0);
+          }
+          umma_commit(&sh->empty[slot]);
+          umma_commit(&sh->empty_b[bslot]);
+        }
+        umma_commit(&sh->done[pi]);   // arrives once every MMA issued so far has completed
       }
-      umma_commit(&sh->done);   // arrives once every MMA issued above has completed
+      for (int pi = 0; pi < npass; ++pi)
+        if (!ok) umma_commit(&sh->done[pi]);          // let the epilogue finish (results invalid)
     }
   } else {
-    // ---------------- weight decoders (256 threads: row r, half h of the 128-byte row)
+    // ---------------- weight decoders (512 threads: row r, quarter h of the 128-byte row)
     const int dt = threadIdx.x - 64, r = dt & 127, h = dt >> 7;
     const uint8_t* cbl = cbs + (lane & (PF_CB_COPIES - 1)) * 8;
-    for (int c = 0; c < nchunks; ++c) {
-      const int slot = c % PF_STAGES, bslot = c % PF_BSTAGES;
-      // the index planes of this stage come with the A tile
-      if (!mbar_wait(&sh->full_a[slot], (c / PF_STAGES) & 1)) break;
-      if (c >= PF_BSTAGES && !mbar_wait(&sh->empty_b[bslot], ((c / PF_BSTAGES) - 1) & 1)) break;
-      const uint8_t* ip = I_t(slot);
-      uint4 lo;
-      uint32_t hw;
-      float scf;
-      if (PREC == VQ2_PREC_FP8) {
-        lo = *(const uint4*)(ip + r * 32 + h * 16);           // lo rows 32 bytes apart
-        hw = *(const uint32_t*)(ip + 4096 + r * 8 + h * 4);
-        scf = __half2float(*(const __half*)(ip + 5120 + r * 4 + h * 2));
-      } else {
-        const uint2 l2 = *(const uint2*)(ip + r * 16 + h * 8);  // lo rows 16 bytes apart
-        lo = make_uint4(l2.x, l2.y, 0, 0);
-        hw = *(const uint16_t*)(ip + 4096 + r * 8 + h * 2);
-        scf = __half2float(*(const __half*)(ip + 5120 + r * 4 + (c & 1) * 2));
+    int gc = 0;
+    bool ok = true;
+    for (int pi = 0; pi < npass; ++pi) {
+      const PfPass P = pass[pi];
+      for (int c = 0; c < nchunks && ok; ++c, ++gc) {
+        const int slot = gc % PF_STAGES, bslot = gc % PF_BSTAGES;
+        // the index planes of this stage come with the A tile
+        if (!mbar_wait(&sh->full_a[slot], (gc / PF_STAGES) & 1)) { ok = false; break; }
+        if (gc >= PF_BSTAGES && !mbar_wait(&sh->empty_b[bslot], ((gc / PF_BSTAGES) - 1) & 1)) { ok = false; break; }
+        const uint8_t* ip = I_t(slot);
+        uint2 lo;
+        uint32_t hw;
+        float scf;
+        if (PREC == VQ2_PREC_FP8) {                   // 8 sub-vectors: lo rows 32 bytes apart
+          lo = *(const uint2*)(ip + r * 32 + h * 8);
+          hw = *(const uint16_t*)(ip + 4096 + r * 8 + h * 2);
+          scf = __half2float(*(const __half*)(ip + 5120 + r * 4 + (h >> 1) * 2));
+        } else {                                      // 4 sub-vectors: lo rows 16 bytes apart
+          lo = make_uint2(*(const uint32_t*)(ip + r * 16 + h * 4), 0u);
+          hw = *(const uint8_t*)(ip + 4096 + r * 8 + h);
+          scf = __half2float(*(const __half*)(ip + 5120 + r * 4 + (c & 1) * 2));
+        }
+        decode_b_quarter<PREC>(cbl, lo, hw, scf, B_t(bslot), r, h);
+        fence_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&sh->full_b[bslot]);
       }
-      decode_b_row<PREC>(cbl, lo, hw, scf, B_t(bslot), r, h);
-      fence_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&sh->full_b[bslot]);
-    }
-    // ---------------- epilogue out of TMEM
-    const int q = warp & 3, ch = (warp - 2) >> 2;       // TMEM lane quarter, column half
-    const int slot_i = q * 32 + lane;
-    const int tok = sh->slot_tok[slot_i];
-    const size_t p = (size_t)blk * PF_BM + slot_i;
-    if (mbar_wait(&sh->done, 0)) {
-      if (threadIdx.x == 64) PF_PROBE(3, 2);
+      // ---------------- epilogue of the pass out of TMEM
+      const int q = warp & 3, cq = (warp - 2) >> 2;        // TMEM lane quarter, column quarter
+      if (!mbar_wait(&sh->done[pi], 0)) continue;
       tc_fence_after();
-      const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16);
-      if (GATEUP) {
-        float g[32], u[32];
-        tmem_ld32(trow + ch * 32, g);
-        tmem_ld32(trow + 64 + ch * 32, u);
-        const float inv = tok >= 0 ? a.inv_act[tok] : 0.f;
-        float* dst = a.inter + p * a.I + tile * 64 + ch * 32;
+      for (int b = 0; b < P.mb; ++b) {
+        const int slot_i = q * 32 + lane;
+        const int tok = sh->slot_tok[(P.blk - b0 + b) * PF_BM + slot_i];
+        const size_t p = (size_t)(P.blk + b) * PF_BM + slot_i;
+        const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((P.acc + b) * PF_BN);
+        if (GATEUP) {
+          float g[16], u[16];
+          tmem_ld16(trow + cq * 16, g);
+          tmem_ld16(trow + 64 + cq * 16, u);
+          const float inv = tok >= 0 ? a.inv_act[tok] : 0.f;
+          float* dst = a.inter + p * a.I + tile * 64 + cq * 16;
 #pragma unroll
-        for (int j = 0; j < 32; j += 4) {
-          float rr[4];
+          for (int j = 0; j < 16; j += 4) {
+            float rr[4];
 #pragma unroll
-          for (int t = 0; t < 4; ++t) {
-            const float gg = g[j + t] * inv, uu = u[j + t] * inv;
-            rr[t] = gg / (1.f + __expf(-gg)) * uu;
+            for (int t = 0; t < 4; ++t) {
+              const float gg = g[j + t] * inv, uu = u[j + t] * inv;
+              rr[t] = gg / (1.f + __expf(-gg)) * uu;
+            }
+            *(float4*)(dst + j) = make_float4(rr[0], rr[1], rr[2], rr[3]);
           }
-          *(float4*)(dst + j) = make_float4(rr[0], rr[1], rr[2], rr[3]);
-        }
-      } else {
-        float v[64];
-        tmem_ld32(trow + ch * 64, v);
-        tmem_ld32(trow + ch * 64 + 32, v + 32);
-        if (tok >= 0) {
-          const float w = a.topk_w[(size_t)tok * a.topk + a.ss[p]] * a.inv_act[p];
-          float* dst = a.out + (size_t)tok * a.H + tile * PF_BN + ch * 64;
+        } else {
+          float v[32];
+          tmem_ld32(trow + cq * 32, v);
+          if (tok >= 0) {
+            const float w = a.topk_w[(size_t)tok * a.topk + a.ss[p]] * a.inv_act[p];
+            float* dst = a.out + (size_t)tok * a.H + tile * PF_BN + cq * 32;
 #pragma unroll
-          for (int j = 0; j < 64; j += 4)
-            atomicAdd((float4*)(dst + j), make_float4(v[j] * w, v[j + 1] * w, v[j + 2] * w, v[j + 3] * w));
+            for (int j = 0; j < 32; j += 4)
+              atomicAdd((float4*)(dst + j), make_float4(v[j] * w, v[j + 1] * w, v[j + 2] * w, v[j + 3] * w));
+          }
         }
       }
+      if (threadIdx.x == 64) PF_PROBE(3, 2);
     }
   }
   tc_fence_before();
@@ -631,9 +686,9 @@ extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_
   // gate/up
   g.inv_act = invx; g.lo = a->w13_lo; g.hi = a->w13_hi; g.sc = a->w13_sc; g.cb = a->w13_cb;
   g.K = a->H; g.R = 2 * a->I;
-  dim3 g1(a->I / 64, (unsigned)L.nblk);
-  if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, true><<<g1, PF_THREADS, PF_SMEM, st_>>>(g, tm_x, tm_l13);
-  else prefill_gemm_kernel<VQ2_PREC_F16, true><<<g1, PF_THREADS, PF_SMEM, st_>>>(g, tm_x, tm_l13);
+  dim3 g1(a->I / 64, (unsigned)((L.nblk + PF_MB - 1) / PF_MB));
+  if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, true><<<g1, PF_THREADS, PF_SMEM, st_>>>(g, tm_x, tm_l13, (int)L.nblk);
+  else prefill_gemm_kernel<VQ2_PREC_F16, true><<<g1, PF_THREADS, PF_SMEM, st_>>>(g, tm_x, tm_l13, (int)L.nblk);
   // inter -> Hadamard -> quantised activation of the down projection
   if (prec == VQ2_PREC_FP8)
     had_quant_rows_kernel<VQ2_PREC_FP8><<<(unsigned)L.Pmax, 256, 0, st_>>>(inter, VQ2_DT_F32, val, a->I, vb, invvb);
@@ -642,8 +697,8 @@ extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_
   // down + combine
   g.inv_act = invvb; g.lo = a->w2_lo; g.hi = a->w2_hi; g.sc = a->w2_sc; g.cb = a->w2_cb;
   g.K = a->I; g.R = a->H;
-  dim3 g2(a->H / PF_BN, (unsigned)L.nblk);
-  if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, false><<<g2, PF_THREADS, PF_SMEM, st_>>>(g, tm_v, tm_l2);
-  else prefill_gemm_kernel<VQ2_PREC_F16, false><<<g2, PF_THREADS, PF_SMEM, st_>>>(g, tm_v, tm_l2);
+  dim3 g2(a->H / PF_BN, (unsigned)((L.nblk + PF_MB - 1) / PF_MB));
+  if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, false><<<g2, PF_THREADS, PF_SMEM, st_>>>(g, tm_v, tm_l2, (int)L.nblk);
+  else prefill_gemm_kernel<VQ2_PREC_F16, false><<<g2, PF_THREADS, PF_SMEM, st_>>>(g, tm_v, tm_l2, (int)L.nblk);
   return cudaGetLastError() == cudaSuccess ? VQ2_OK : VQ2_ERR_CUDA;
 }
