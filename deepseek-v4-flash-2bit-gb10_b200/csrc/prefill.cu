@@ -33,17 +33,19 @@ int launch_align_ex(const void* ids, int dt, long N, int k, int E, int BM, int b
                     int32_t* ss, uint8_t* val, int32_t* be, int* counts, cudaStream_t stream);
 
 constexpr int PF_BM = 128;            // slots per block (MMA M)
-constexpr int PF_BN = 128;            // weight rows per tile (MMA N)
+constexpr int PF_BN = 256;            // weight rows per tile (MMA N)
 constexpr int PF_MB = 2;              // blocks of one expert sharing each decoded B tile
-constexpr int PF_STAGES = 3;          // ring of (A tiles of PF_MB blocks, index planes): memory latency
+constexpr int PF_STAGES = 2;          // ring of (A tiles of PF_MB blocks, index planes): memory latency
 constexpr int PF_BSTAGES = 2;         // ring of decoded B tiles: produced in the CTA
 constexpr int PF_DEC_WARPS = 16;      // decoders; four per TMEM lane quarter in the epilogue
 constexpr int PF_THREADS = (2 + PF_DEC_WARPS) * 32;
-constexpr int PF_TILE = 16384;        // one 128 x 128-byte operand tile
+constexpr int PF_TILE = 16384;        // one 128-row x 128-byte activation tile
+constexpr int PF_BTILE = PF_BN * 128; // the weight tile: 256 rows x 128 bytes
 constexpr int PF_ATILE = PF_MB * PF_TILE;
 constexpr int PF_CB_COPIES = 8;
 constexpr int PF_CB_BYTES = 1024 * 8 * PF_CB_COPIES;
-constexpr int PF_IDX = 6144;   // staged index planes of one stage: lo 4096 B, hi 1024 B, sc 512 B (padded)
+constexpr int PF_IDX = 12288;  // staged index planes of one stage: lo 8192 B, hi 2048 B, sc 1024 B (padded)
+constexpr int PF_IDX_HI = 8192, PF_IDX_SC = 10240;
 static_assert(PF_IDX % 1024 == 0, "index stages keep the following tiles 1024-byte aligned");
 constexpr int PF_TMEM_COLS = PF_MB * PF_BN;
 
@@ -58,7 +60,7 @@ struct PfShared {
   int slot_tok[PF_MB * PF_BM];
 };
 
-constexpr size_t PF_SMEM = (size_t)PF_CB_BYTES + (size_t)PF_STAGES * (PF_ATILE + PF_IDX) + (size_t)PF_BSTAGES * PF_TILE +
+constexpr size_t PF_SMEM = (size_t)PF_CB_BYTES + (size_t)PF_STAGES * (PF_ATILE + PF_IDX) + (size_t)PF_BSTAGES * PF_BTILE +
                            sizeof(PfShared) + 1024;
 
 struct PfGemmArgs {
@@ -209,9 +211,9 @@ __device__ __forceinline__ void decode_b_quarter(const uint8_t* cbl, uint2 lo, u
 }
 
 // ------------------------------------------------------------------ grouped GEMM kernel
-// grid (tiles along N, pairs of 128-slot blocks). GATEUP: tile n covers gate rows [64n, 64n+64)
+// grid (tiles along N, pairs of 128-slot blocks). GATEUP: tile n covers gate rows [128n, 128n+128)
 // and the matching up rows; the epilogue writes inter. Otherwise tile n covers output rows
-// [128n, 128n+128) and the epilogue accumulates into out. Two blocks of the same expert run as
+// [256n, 256n+256) and the epilogue accumulates into out. Two blocks of the same expert run as
 // one pass (each decoded B tile feeds two MMAs, two TMEM accumulators); two blocks of different
 // experts run as two passes, one accumulator each.
 #ifdef VQ2_PF_PROBE
@@ -229,7 +231,8 @@ __device__ __forceinline__ unsigned long long pf_time() {
 
 template <bool GATEUP>
 __device__ __forceinline__ long pf_weight_row(const PfGemmArgs& a, int e, int tile, int r) {
-  if (GATEUP) return (long)e * a.R + (r < 64 ? tile * 64 + r : a.I + tile * 64 + (r - 64));
+  constexpr int HALF = PF_BN / 2;
+  if (GATEUP) return (long)e * a.R + (r < HALF ? tile * HALF + r : a.I + tile * HALF + (r - HALF));
   return (long)e * a.R + tile * PF_BN + r;
 }
 
@@ -249,7 +252,7 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
   uint8_t* cbs = smem;
   uint8_t* atiles = smem + PF_CB_BYTES;                // A ring (PF_MB tiles per stage)
   uint8_t* btiles = atiles + PF_STAGES * PF_ATILE;     // B ring
-  uint8_t* itiles = btiles + PF_BSTAGES * PF_TILE;     // index-plane ring
+  uint8_t* itiles = btiles + PF_BSTAGES * PF_BTILE;    // index-plane ring
   PfShared* sh = (PfShared*)(itiles + PF_STAGES * PF_IDX);
   const int tile = blockIdx.x, b0 = blockIdx.y * PF_MB;
   if (threadIdx.x == 0) PF_PROBE(3, 0);
@@ -268,7 +271,7 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
   const int nchunks = a.K / KE;
   const int nsub = a.K / 4, ngk = a.K / 64;
   auto A_t = [&](int slot) { return atiles + slot * PF_ATILE; };
-  auto B_t = [&](int slot) { return btiles + slot * PF_TILE; };
+  auto B_t = [&](int slot) { return btiles + slot * PF_BTILE; };
   auto I_t = [&](int slot) { return itiles + slot * PF_IDX; };   // lo | hi | sc
 
   if (threadIdx.x == 0) {
@@ -318,35 +321,36 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
     int gc = 0;                                       // stage counter across passes
     for (int pi = 0; pi < npass; ++pi) {
       const PfPass P = pass[pi];
-      const uint8_t* hi_r[4];
-      const uint8_t* sc_r[4];
+      const uint8_t* hi_r[8];
+      const uint8_t* sc_r[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
+      for (int i = 0; i < 8; ++i) {
         const long wr = pf_weight_row<GATEUP>(a, P.e, tile, lane + 32 * i);
         hi_r[i] = a.hi + wr * (nsub / 4);
         sc_r[i] = (const uint8_t*)(a.sc + wr * ngk);
       }
-      const int row0 = (int)pf_weight_row<GATEUP>(a, P.e, tile, 0), row1 = (int)pf_weight_row<GATEUP>(a, P.e, tile, 64);
+      const int row0 = (int)pf_weight_row<GATEUP>(a, P.e, tile, 0);
+      const int row1 = (int)pf_weight_row<GATEUP>(a, P.e, tile, PF_BN / 2);
       for (int c = 0; c < nchunks; ++c, ++gc) {
         const int slot = gc % PF_STAGES;
         if (gc >= PF_STAGES && !mbar_wait(&sh->empty[slot], ((gc / PF_STAGES) - 1) & 1)) { pi = npass; break; }
         const uint32_t ibase = smem_u32(I_t(slot));
         if (lane == 0) {
-          mbar_arrive_expect_tx(&sh->full_a[slot], P.mb * PF_TILE + 128 * LOB);
+          mbar_arrive_expect_tx(&sh->full_a[slot], P.mb * PF_TILE + PF_BN * LOB);
           tma_load_2d(A_t(slot), &tm_act, c * 128, P.blk * PF_BM, &sh->full_a[slot]);
           if (P.mb == 2) tma_load_2d(A_t(slot) + PF_TILE, &tm_act, c * 128, (P.blk + 1) * PF_BM, &sh->full_a[slot]);
           tma_load_2d(I_t(slot), &tm_lo, c * LOB, row0, &sh->full_a[slot]);
-          tma_load_2d(I_t(slot) + 64 * LOB, &tm_lo, c * LOB, row1, &sh->full_a[slot]);
+          tma_load_2d(I_t(slot) + (PF_BN / 2) * LOB, &tm_lo, c * LOB, row1, &sh->full_a[slot]);
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
+        for (int i = 0; i < 8; ++i) {
           const int r = lane + 32 * i;
           if (PREC == VQ2_PREC_FP8) {          // hi: 8 bytes (32 sub-vectors); scales of 2 groups
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(ibase + 4096 + r * 8), "l"(hi_r[i] + c * 8) : "memory");
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + 5120 + r * 4), "l"(sc_r[i] + c * 4) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(ibase + PF_IDX_HI + r * 8), "l"(hi_r[i] + c * 8) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + PF_IDX_SC + r * 4), "l"(sc_r[i] + c * 4) : "memory");
           } else {                             // hi: 4 bytes (16 sub-vectors); the scale pair holding this group
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + 4096 + r * 8), "l"(hi_r[i] + c * 4) : "memory");
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + 5120 + r * 4), "l"(sc_r[i] + (c & ~1) * 2) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + PF_IDX_HI + r * 8), "l"(hi_r[i] + c * 4) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + PF_IDX_SC + r * 4), "l"(sc_r[i] + (c & ~1) * 2) : "memory");
           }
         }
         // the stage's full barrier also gets one arrival per lane when its copies above have landed
@@ -370,7 +374,7 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
           PF_PROBE(2, gc);
           fence_async_smem();                             // cp.async-written data visible to the tensor core
           tc_fence_after();
-          const uint32_t abase = smem_u32(A_t(slot)), bbase = smem_u32(B_t(bslot));
+          const uint32_t abase = smem_u32(A_t(slot)), bbase = smem_u32(B_t(bslot));   // B: 256 rows
           for (int b = 0; b < P.mb; ++b) {
             const uint32_t td = tmem + (uint32_t)((P.acc + b) * PF_BN);
 #pragma unroll
@@ -387,8 +391,8 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
         if (!ok) umma_commit(&sh->done[pi]);          // let the epilogue finish (results invalid)
     }
   } else {
-    // ---------------- weight decoders (512 threads: row r, quarter h of the 128-byte row)
-    const int dt = threadIdx.x - 64, r = dt & 127, h = dt >> 7;
+    // ---------------- weight decoders (512 threads: row r, half h of the 128-byte row)
+    const int dt = threadIdx.x - 64, r = dt & (PF_BN - 1), h = dt / PF_BN;
     const uint8_t* cbl = cbs + (lane & (PF_CB_COPIES - 1)) * 8;
     int gc = 0;
     bool ok = true;
@@ -400,19 +404,20 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
         if (!mbar_wait(&sh->full_a[slot], (gc / PF_STAGES) & 1)) { ok = false; break; }
         if (gc >= PF_BSTAGES && !mbar_wait(&sh->empty_b[bslot], ((gc / PF_BSTAGES) - 1) & 1)) { ok = false; break; }
         const uint8_t* ip = I_t(slot);
-        uint2 lo;
-        uint32_t hw;
-        float scf;
-        if (PREC == VQ2_PREC_FP8) {                   // 8 sub-vectors: lo rows 32 bytes apart
-          lo = *(const uint2*)(ip + r * 32 + h * 8);
-          hw = *(const uint16_t*)(ip + 4096 + r * 8 + h * 2);
-          scf = __half2float(*(const __half*)(ip + 5120 + r * 4 + (h >> 1) * 2));
-        } else {                                      // 4 sub-vectors: lo rows 16 bytes apart
-          lo = make_uint2(*(const uint32_t*)(ip + r * 16 + h * 4), 0u);
-          hw = *(const uint8_t*)(ip + 4096 + r * 8 + h);
-          scf = __half2float(*(const __half*)(ip + 5120 + r * 4 + (c & 1) * 2));
+        uint8_t* bt = B_t(bslot);
+        if (PREC == VQ2_PREC_FP8) {                   // 16 sub-vectors = one 64-group; lo rows 32 B apart
+          const uint4 lo = *(const uint4*)(ip + r * 32 + h * 16);
+          const uint32_t hw = *(const uint32_t*)(ip + PF_IDX_HI + r * 8 + h * 4);
+          const float scf = __half2float(*(const __half*)(ip + PF_IDX_SC + r * 4 + h * 2));
+          decode_b_quarter<PREC>(cbl, make_uint2(lo.x, lo.y), hw & 0xFFFFu, scf, bt, r, 2 * h);
+          decode_b_quarter<PREC>(cbl, make_uint2(lo.z, lo.w), hw >> 16, scf, bt, r, 2 * h + 1);
+        } else {                                      // 8 sub-vectors; lo rows 16 B apart
+          const uint2 lo = *(const uint2*)(ip + r * 16 + h * 8);
+          const uint32_t hw = *(const uint16_t*)(ip + PF_IDX_HI + r * 8 + h * 2);
+          const float scf = __half2float(*(const __half*)(ip + PF_IDX_SC + r * 4 + (c & 1) * 2));
+          decode_b_quarter<PREC>(cbl, make_uint2(lo.x, 0u), hw & 0xFFu, scf, bt, r, 2 * h);
+          decode_b_quarter<PREC>(cbl, make_uint2(lo.y, 0u), hw >> 8, scf, bt, r, 2 * h + 1);
         }
-        decode_b_quarter<PREC>(cbl, lo, hw, scf, B_t(bslot), r, h);
         fence_async_smem();
         __syncwarp();
         if (lane == 0) mbar_arrive(&sh->full_b[bslot]);
@@ -426,14 +431,14 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
         const int tok = sh->slot_tok[(P.blk - b0 + b) * PF_BM + slot_i];
         const size_t p = (size_t)(P.blk + b) * PF_BM + slot_i;
         const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((P.acc + b) * PF_BN);
-        if (GATEUP) {
-          float g[16], u[16];
-          tmem_ld16(trow + cq * 16, g);
-          tmem_ld16(trow + 64 + cq * 16, u);
+        if (GATEUP) {                                  // 32 gate + the 32 matching up columns
+          float g[32], u[32];
+          tmem_ld32(trow + cq * 32, g);
+          tmem_ld32(trow + PF_BN / 2 + cq * 32, u);
           const float inv = tok >= 0 ? a.inv_act[tok] : 0.f;
-          float* dst = a.inter + p * a.I + tile * 64 + cq * 16;
+          float* dst = a.inter + p * a.I + tile * (PF_BN / 2) + cq * 32;
 #pragma unroll
-          for (int j = 0; j < 16; j += 4) {
+          for (int j = 0; j < 32; j += 4) {
             float rr[4];
 #pragma unroll
             for (int t = 0; t < 4; ++t) {
@@ -442,15 +447,18 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
             }
             *(float4*)(dst + j) = make_float4(rr[0], rr[1], rr[2], rr[3]);
           }
-        } else {
-          float v[32];
-          tmem_ld32(trow + cq * 32, v);
-          if (tok >= 0) {
-            const float w = a.topk_w[(size_t)tok * a.topk + a.ss[p]] * a.inv_act[p];
-            float* dst = a.out + (size_t)tok * a.H + tile * PF_BN + cq * 32;
+        } else {                                       // 64 output columns
+          const float w = tok >= 0 ? a.topk_w[(size_t)tok * a.topk + a.ss[p]] * a.inv_act[p] : 0.f;
+          float* dst = a.out + (size_t)(tok >= 0 ? tok : 0) * a.H + tile * PF_BN + cq * 64;
 #pragma unroll
-            for (int j = 0; j < 32; j += 4)
-              atomicAdd((float4*)(dst + j), make_float4(v[j] * w, v[j + 1] * w, v[j + 2] * w, v[j + 3] * w));
+          for (int hh = 0; hh < 2; ++hh) {
+            float v[32];
+            tmem_ld32(trow + cq * 64 + hh * 32, v);     // collective: every lane loads
+            if (tok >= 0) {
+#pragma unroll
+              for (int j = 0; j < 32; j += 4)
+                atomicAdd((float4*)(dst + hh * 32 + j), make_float4(v[j] * w, v[j + 1] * w, v[j + 2] * w, v[j + 3] * w));
+            }
           }
         }
       }
@@ -625,7 +633,7 @@ extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_
       !a->w13_sc || !a->w2_cb || !a->w2_lo || !a->w2_hi || !a->w2_sc)
     return VQ2_ERR_NULL;
   if (prec != VQ2_PREC_FP8 && prec != VQ2_PREC_F16) return VQ2_ERR_DTYPE;
-  if (a->N <= 0 || a->topk <= 0 || a->E <= 0 || a->E > 1024 || a->H % 128 || a->I % 128 || a->H > 4096 ||
+  if (a->N <= 0 || a->topk <= 0 || a->E <= 0 || a->E > 1024 || a->H % 256 || a->I % 128 || a->H > 4096 ||
       a->I > 4096)
     return VQ2_ERR_SHAPE;
   if (a->x_dtype < 0 || a->x_dtype > 2 || a->ids_dtype < 0 || a->ids_dtype > 1) return VQ2_ERR_DTYPE;
@@ -680,13 +688,13 @@ extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_
   CUtensorMap tm_x, tm_v, tm_l13, tm_l2;
   if (encode_2d(&tm_x, xs, (uint64_t)a->H * elem, L.Pmax, 128, 128, true) ||
       encode_2d(&tm_v, vb, (uint64_t)a->I * elem, L.Pmax, 128, 128, true) ||
-      encode_2d(&tm_l13, a->w13_lo, a->H / 4, (uint64_t)a->E * 2 * a->I, lob, 64, false) ||
-      encode_2d(&tm_l2, a->w2_lo, a->I / 4, (uint64_t)a->E * a->H, lob, 64, false))
+      encode_2d(&tm_l13, a->w13_lo, a->H / 4, (uint64_t)a->E * 2 * a->I, lob, PF_BN / 2, false) ||
+      encode_2d(&tm_l2, a->w2_lo, a->I / 4, (uint64_t)a->E * a->H, lob, PF_BN / 2, false))
     return VQ2_ERR_CUDA;
   // gate/up
   g.inv_act = invx; g.lo = a->w13_lo; g.hi = a->w13_hi; g.sc = a->w13_sc; g.cb = a->w13_cb;
   g.K = a->H; g.R = 2 * a->I;
-  dim3 g1(a->I / 64, (unsigned)((L.nblk + PF_MB - 1) / PF_MB));
+  dim3 g1(a->I / (PF_BN / 2), (unsigned)((L.nblk + PF_MB - 1) / PF_MB));
   if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, true><<<g1, PF_THREADS, PF_SMEM, st_>>>(g, tm_x, tm_l13, (int)L.nblk);
   else prefill_gemm_kernel<VQ2_PREC_F16, true><<<g1, PF_THREADS, PF_SMEM, st_>>>(g, tm_x, tm_l13, (int)L.nblk);
   // inter -> Hadamard -> quantised activation of the down projection
