@@ -35,32 +35,34 @@ int launch_align_ex(const void* ids, int dt, long N, int k, int E, int BM, int b
 constexpr int PF_BM = 128;            // slots per block (MMA M)
 constexpr int PF_BN = 256;            // weight rows per tile (MMA N)
 constexpr int PF_MB = 2;              // blocks of one expert sharing each decoded B tile
-constexpr int PF_STAGES = 2;          // ring of (A tiles of PF_MB blocks, index planes): memory latency
+constexpr int PF_STAGES = 2;          // ring of A tiles (PF_MB blocks each): TMA from L2
+constexpr int PF_ISTAGES = 3;         // ring of staged index planes: run ahead of the activations
 constexpr int PF_BSTAGES = 2;         // ring of decoded B tiles: produced in the CTA
 constexpr int PF_DEC_WARPS = 16;      // decoders; four per TMEM lane quarter in the epilogue
-constexpr int PF_THREADS = (2 + PF_DEC_WARPS) * 32;
+constexpr int PF_THREADS = (3 + PF_DEC_WARPS) * 32;   // A loader, index loader, MMA issuer, decoders
 constexpr int PF_TILE = 16384;        // one 128-row x 128-byte activation tile
 constexpr int PF_BTILE = PF_BN * 128; // the weight tile: 256 rows x 128 bytes
 constexpr int PF_ATILE = PF_MB * PF_TILE;
 constexpr int PF_CB_COPIES = 8;
 constexpr int PF_CB_BYTES = 1024 * 8 * PF_CB_COPIES;
-constexpr int PF_IDX = 12288;  // staged index planes of one stage: lo 8192 B, hi 2048 B, sc 1024 B (padded)
+constexpr int PF_IDX = 11264;  // staged index planes of one stage: lo 8192 B, hi 2048 B, sc 1024 B
 constexpr int PF_IDX_HI = 8192, PF_IDX_SC = 10240;
-static_assert(PF_IDX % 1024 == 0, "index stages keep the following tiles 1024-byte aligned");
+static_assert(PF_IDX % 16 == 0, "index stages keep 16-byte alignment");
 constexpr int PF_TMEM_COLS = PF_MB * PF_BN;
 
 struct PfShared {
   uint64_t full_a[PF_STAGES];
   uint64_t empty[PF_STAGES];
+  uint64_t full_i[PF_ISTAGES];
+  uint64_t empty_i[PF_ISTAGES];
   uint64_t full_b[PF_BSTAGES];
   uint64_t empty_b[PF_BSTAGES];
   uint64_t done[2];             // per pass: all MMAs of the pass complete
   uint64_t cbbar;
   uint32_t tmem_base;
-  int slot_tok[PF_MB * PF_BM];
 };
 
-constexpr size_t PF_SMEM = (size_t)PF_CB_BYTES + (size_t)PF_STAGES * (PF_ATILE + PF_IDX) + (size_t)PF_BSTAGES * PF_BTILE +
+constexpr size_t PF_SMEM = (size_t)PF_CB_BYTES + (size_t)PF_STAGES * PF_ATILE + (size_t)PF_ISTAGES * PF_IDX + (size_t)PF_BSTAGES * PF_BTILE +
                            sizeof(PfShared) + 1024;
 
 struct PfGemmArgs {
@@ -253,7 +255,7 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
   uint8_t* atiles = smem + PF_CB_BYTES;                // A ring (PF_MB tiles per stage)
   uint8_t* btiles = atiles + PF_STAGES * PF_ATILE;     // B ring
   uint8_t* itiles = btiles + PF_BSTAGES * PF_BTILE;    // index-plane ring
-  PfShared* sh = (PfShared*)(itiles + PF_STAGES * PF_IDX);
+  PfShared* sh = (PfShared*)(itiles + PF_ISTAGES * PF_IDX);
   const int tile = blockIdx.x, b0 = blockIdx.y * PF_MB;
   if (threadIdx.x == 0) PF_PROBE(3, 0);
   if (!a.val[(size_t)b0 * PF_BM]) return;            // blocks past the last expert hold no pair
@@ -276,8 +278,12 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < PF_STAGES; ++s) {
-      mbar_init(&sh->full_a[s], 33);        // TMA bytes (1 arrival) + 32 lanes' cp.async
+      mbar_init(&sh->full_a[s], 1);         // TMA bytes
       mbar_init(&sh->empty[s], 1);
+    }
+    for (int s = 0; s < PF_ISTAGES; ++s) {
+      mbar_init(&sh->full_i[s], 33);        // TMA bytes (1 arrival) + 32 lanes' cp.async
+      mbar_init(&sh->empty_i[s], PF_DEC_WARPS);
     }
     for (int s = 0; s < PF_BSTAGES; ++s) {
       mbar_init(&sh->full_b[s], PF_DEC_WARPS);
@@ -289,11 +295,6 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
     fence_mbar_init();
     mbar_arrive_expect_tx(&sh->cbbar, 1024 * 8);
     bulk_g2s(B_t(0), a.cb, 1024 * 8, &sh->cbbar);     // codebook lands in a B tile first
-  }
-  for (int i = threadIdx.x; i < PF_MB * PF_BM; i += blockDim.x) {
-    const size_t p = (size_t)b0 * PF_BM + i;
-    const bool in = b0 + i / PF_BM < nblk;
-    sh->slot_tok[i] = (in && a.val[p]) ? a.st[p] : -1;
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
@@ -316,9 +317,25 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
   const uint32_t tmem = sh->tmem_base;
 
   if (warp == 0) {
-    // ---------------- loader: A tiles + lo plane by TMA, hi / scale planes by cp.async
+    // ---------------- activation loader: A tiles of the pass's blocks by TMA (lane 0)
+    if (lane == 0) {
+      int gc = 0;
+      for (int pi = 0; pi < npass; ++pi) {
+        const PfPass P = pass[pi];
+        for (int c = 0; c < nchunks; ++c, ++gc) {
+          const int slot = gc % PF_STAGES;
+          if (gc >= PF_STAGES && !mbar_wait(&sh->empty[slot], ((gc / PF_STAGES) - 1) & 1)) { pi = npass; break; }
+          mbar_arrive_expect_tx(&sh->full_a[slot], P.mb * PF_TILE);
+          tma_load_2d(A_t(slot), &tm_act, c * 128, P.blk * PF_BM, &sh->full_a[slot]);
+          if (P.mb == 2) tma_load_2d(A_t(slot) + PF_TILE, &tm_act, c * 128, (P.blk + 1) * PF_BM, &sh->full_a[slot]);
+          PF_PROBE(0, gc);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- index loader: lo plane by TMA, hi / scale planes by cp.async
     constexpr int LOB = 128 / elem / 4;               // lo bytes per row per stage (32 fp8, 16 f16)
-    int gc = 0;                                       // stage counter across passes
+    int gc = 0;
     for (int pi = 0; pi < npass; ++pi) {
       const PfPass P = pass[pi];
       const uint8_t* hi_r[8];
@@ -332,15 +349,13 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
       const int row0 = (int)pf_weight_row<GATEUP>(a, P.e, tile, 0);
       const int row1 = (int)pf_weight_row<GATEUP>(a, P.e, tile, PF_BN / 2);
       for (int c = 0; c < nchunks; ++c, ++gc) {
-        const int slot = gc % PF_STAGES;
-        if (gc >= PF_STAGES && !mbar_wait(&sh->empty[slot], ((gc / PF_STAGES) - 1) & 1)) { pi = npass; break; }
+        const int slot = gc % PF_ISTAGES;
+        if (gc >= PF_ISTAGES && !mbar_wait(&sh->empty_i[slot], ((gc / PF_ISTAGES) - 1) & 1)) { pi = npass; break; }
         const uint32_t ibase = smem_u32(I_t(slot));
         if (lane == 0) {
-          mbar_arrive_expect_tx(&sh->full_a[slot], P.mb * PF_TILE + PF_BN * LOB);
-          tma_load_2d(A_t(slot), &tm_act, c * 128, P.blk * PF_BM, &sh->full_a[slot]);
-          if (P.mb == 2) tma_load_2d(A_t(slot) + PF_TILE, &tm_act, c * 128, (P.blk + 1) * PF_BM, &sh->full_a[slot]);
-          tma_load_2d(I_t(slot), &tm_lo, c * LOB, row0, &sh->full_a[slot]);
-          tma_load_2d(I_t(slot) + (PF_BN / 2) * LOB, &tm_lo, c * LOB, row1, &sh->full_a[slot]);
+          mbar_arrive_expect_tx(&sh->full_i[slot], PF_BN * LOB);
+          tma_load_2d(I_t(slot), &tm_lo, c * LOB, row0, &sh->full_i[slot]);
+          tma_load_2d(I_t(slot) + (PF_BN / 2) * LOB, &tm_lo, c * LOB, row1, &sh->full_i[slot]);
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
@@ -353,13 +368,12 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
             asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + PF_IDX_SC + r * 4), "l"(sc_r[i] + (c & ~1) * 2) : "memory");
           }
         }
-        // the stage's full barrier also gets one arrival per lane when its copies above have landed
-        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&sh->full_a[slot])) : "memory");
-        if (lane == 0) PF_PROBE(0, gc);
+        // one more arrival per lane when its copies above have landed
+        asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&sh->full_i[slot])) : "memory");
       }
     }
     cp_async_wait<0>();                               // nothing in flight when the CTA retires
-  } else if (warp == 1) {
+  } else if (warp == 2) {
     // ---------------- MMA issuer
     if (lane == 0) {
       int gc = 0;
@@ -392,16 +406,15 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
     }
   } else {
     // ---------------- weight decoders (512 threads: row r, half h of the 128-byte row)
-    const int dt = threadIdx.x - 64, r = dt & (PF_BN - 1), h = dt / PF_BN;
+    const int dt = threadIdx.x - 96, r = dt & (PF_BN - 1), h = dt / PF_BN;
     const uint8_t* cbl = cbs + (lane & (PF_CB_COPIES - 1)) * 8;
     int gc = 0;
     bool ok = true;
     for (int pi = 0; pi < npass; ++pi) {
       const PfPass P = pass[pi];
       for (int c = 0; c < nchunks && ok; ++c, ++gc) {
-        const int slot = gc % PF_STAGES, bslot = gc % PF_BSTAGES;
-        // the index planes of this stage come with the A tile
-        if (!mbar_wait(&sh->full_a[slot], (gc / PF_STAGES) & 1)) { ok = false; break; }
+        const int slot = gc % PF_ISTAGES, bslot = gc % PF_BSTAGES;
+        if (!mbar_wait(&sh->full_i[slot], (gc / PF_ISTAGES) & 1)) { ok = false; break; }
         if (gc >= PF_BSTAGES && !mbar_wait(&sh->empty_b[bslot], ((gc / PF_BSTAGES) - 1) & 1)) { ok = false; break; }
         const uint8_t* ip = I_t(slot);
         uint8_t* bt = B_t(bslot);
@@ -420,16 +433,19 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
         }
         fence_async_smem();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sh->full_b[bslot]);
+        if (lane == 0) {
+          mbar_arrive(&sh->full_b[bslot]);
+          mbar_arrive(&sh->empty_i[slot]);
+        }
       }
       // ---------------- epilogue of the pass out of TMEM
-      const int q = warp & 3, cq = (warp - 2) >> 2;        // TMEM lane quarter, column quarter
+      const int q = warp & 3, cq = (warp - 3) >> 2;        // TMEM lane quarter, column quarter
       if (!mbar_wait(&sh->done[pi], 0)) continue;
       tc_fence_after();
       for (int b = 0; b < P.mb; ++b) {
         const int slot_i = q * 32 + lane;
-        const int tok = sh->slot_tok[(P.blk - b0 + b) * PF_BM + slot_i];
         const size_t p = (size_t)(P.blk + b) * PF_BM + slot_i;
+        const int tok = a.val[p] ? a.st[p] : -1;
         const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((P.acc + b) * PF_BN);
         if (GATEUP) {                                  // 32 gate + the 32 matching up columns
           float g[32], u[32];
@@ -462,7 +478,7 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
           }
         }
       }
-      if (threadIdx.x == 64) PF_PROBE(3, 2);
+      if (threadIdx.x == 96) PF_PROBE(3, 2);
     }
   }
   tc_fence_before();
