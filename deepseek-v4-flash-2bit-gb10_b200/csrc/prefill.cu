@@ -406,7 +406,8 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
     }
   } else {
     // ---------------- weight decoders (512 threads: row r, half h of the 128-byte row)
-    const int dt = threadIdx.x - 96, r = dt & (PF_BN - 1), h = dt / PF_BN;
+    // the two half-row threads of a row are adjacent lanes: index-plane reads are contiguous
+    const int dt = threadIdx.x - 96, r = dt >> 1, h = dt & 1;
     const uint8_t* cbl = cbs + (lane & (PF_CB_COPIES - 1)) * 8;
     int gc = 0;
     bool ok = true;
