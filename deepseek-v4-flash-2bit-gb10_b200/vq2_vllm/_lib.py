@@ -93,9 +93,11 @@ def require_cuda(*ts):
 _WS = {}
 
 
-def workspace(nbytes: int, device) -> torch.Tensor:
+def workspace(nbytes: int, device, stream=None) -> torch.Tensor:
     """Cached per-(device, stream) byte workspace, grown on demand (graph-safe once sized)."""
-    key = (str(device), torch.cuda.current_stream(device).cuda_stream)
+    if stream is None:
+        stream = torch.cuda.current_stream(device).cuda_stream
+    key = (device.index if isinstance(device, torch.device) else device, stream)
     buf = _WS.get(key)
     if buf is None or buf.numel() < nbytes:
         buf = torch.empty(max(nbytes, 1 << 20), dtype=torch.uint8, device=device)
@@ -103,15 +105,27 @@ def workspace(nbytes: int, device) -> torch.Tensor:
     return buf
 
 
+_ARGS = {}
+
+
 def moe_args(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, out, expert_base=0, E=None):
+    """The vq2_moe_args struct for one call. The weight part is cached per layer (keyed by the
+    weight pointers and shapes), so a call only rewrites the per-call fields."""
+    wkey = (Cgu.data_ptr(), lgu.data_ptr(), hgu.data_ptr(), sgu.data_ptr(), Cd.data_ptr(), ld.data_ptr(),
+            hd.data_ptr(), sdn.data_ptr(), lgu.shape, E)
+    a = _ARGS.get(wkey)
+    if a is None:
+        a = Vq2MoeArgs()
+        a.I = lgu.shape[1] // 2
+        a.E = lgu.shape[0] if E is None else E
+        a.w13_cb, a.w13_lo, a.w13_hi, a.w13_sc = wkey[0], wkey[1], wkey[2], wkey[3]
+        a.w2_cb, a.w2_lo, a.w2_hi, a.w2_sc = wkey[4], wkey[5], wkey[6], wkey[7]
+        if len(_ARGS) > 4096:
+            _ARGS.clear()
+        _ARGS[wkey] = a
     N, H = x.shape
-    a = Vq2MoeArgs()
-    a.N, a.H, a.I = N, H, lgu.shape[1] // 2
-    a.E = lgu.shape[0] if E is None else E
+    a.N, a.H = N, H
     a.topk = topk_ids.shape[1]
     a.x_dtype, a.ids_dtype, a.expert_base = DT[x.dtype], ID[topk_ids.dtype], expert_base
-    a.x, a.topk_ids, a.topk_w = ptr(x), ptr(topk_ids), ptr(topk_w)
-    a.w13_cb, a.w13_lo, a.w13_hi, a.w13_sc = ptr(Cgu), ptr(lgu), ptr(hgu), ptr(sgu)
-    a.w2_cb, a.w2_lo, a.w2_hi, a.w2_sc = ptr(Cd), ptr(ld), ptr(hd), ptr(sdn)
-    a.out = ptr(out)
+    a.x, a.topk_ids, a.topk_w, a.out = x.data_ptr(), topk_ids.data_ptr(), topk_w.data_ptr(), out.data_ptr()
     return a

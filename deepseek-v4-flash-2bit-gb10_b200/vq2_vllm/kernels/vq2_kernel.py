@@ -51,16 +51,34 @@ def had_act(x, group=64):
     return had_act_batch(x[None], group)[0]
 
 
+_F16, _U8, _F32, _I32, _I64 = torch.float16, torch.uint8, torch.float32, torch.int32, torch.int64
+
+
+def _ok(t, dtype):
+    return t.dtype is dtype and t.is_contiguous()
+
+
 def _prep(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn):
-    _lib.require_cuda(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn)
+    """Normalise dtypes / contiguity (copies only when needed) and require CUDA tensors."""
+    if not x.is_cuda:
+        _lib.require_cuda(x)
     if x.dtype not in _lib.DT:
         x = x.to(torch.bfloat16)
-    if topk_ids.dtype not in _lib.ID:
-        topk_ids = topk_ids.to(torch.int32)
-    t = [x.contiguous(), topk_ids.contiguous(), topk_w.float().contiguous()]
-    t += [Cgu.half().contiguous(), lgu.contiguous(), hgu.contiguous(), sgu.half().contiguous(),
-          Cd.half().contiguous(), ld.contiguous(), hd.contiguous(), sdn.half().contiguous()]
-    return t
+    if not x.is_contiguous():
+        x = x.contiguous()
+    if topk_ids.dtype is not _I32 and topk_ids.dtype is not _I64:
+        topk_ids = topk_ids.to(_I32)
+    if not topk_ids.is_contiguous():
+        topk_ids = topk_ids.contiguous()
+    if not _ok(topk_w, _F32):
+        topk_w = topk_w.float().contiguous()
+    ws = [Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn]
+    want = (_F16, _U8, _U8, _F16, _F16, _U8, _U8, _F16)
+    for i, (t, d) in enumerate(zip(ws, want)):
+        if not _ok(t, d):
+            ws[i] = t.to(d).contiguous()
+    _lib.require_cuda(topk_ids, topk_w, *ws)
+    return [x, topk_ids, topk_w] + ws
 
 
 def vq2_moe_fused_10b(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, group=64, expert_base=0):
@@ -80,7 +98,10 @@ def vq2_moe_fused_10b(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, 
     out = torch.empty(N, x.shape[1], device=x.device, dtype=torch.float32)
     L = _lib.lib()
     a = _lib.moe_args(*t, out, expert_base=expert_base)
-    nb = L.vq2_decode_workspace_size(a.N, a.topk, a.H, a.I)
-    ws = _lib.workspace(nb, x.device)
-    _lib.check(L.vq2_decode(a, ws.data_ptr(), ws.numel(), _lib.stream_ptr(x.device)), "vq2_moe_fused_10b")
+    nb = (N * k * ((x.shape[1] // 64 + 31) // 32) * 2 * a.I) * 4 + 256     # vq2_decode_workspace_size
+    stream = torch.cuda.current_stream(x.device).cuda_stream
+    ws = _lib.workspace(nb, x.device, stream)
+    rc = L.vq2_decode(a, ws.data_ptr(), ws.numel(), stream)
+    if rc:
+        _lib.check(rc, "vq2_moe_fused_10b")
     return out
