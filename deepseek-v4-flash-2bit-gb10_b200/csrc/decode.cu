@@ -25,7 +25,7 @@
 namespace vq2 {
 
 #ifndef VQ2_DEC_NW
-#define VQ2_DEC_NW 8
+#define VQ2_DEC_NW 16
 #endif
 constexpr int DEC_NW = VQ2_DEC_NW;        // consumer warps
 constexpr int DEC_THREADS = (DEC_NW + 1) * 32;
@@ -44,8 +44,12 @@ constexpr int DEC_GRAN = 8;               // row granule of the work split (keep
 constexpr int DEC_SA = VQ2_DEC_SA;        // gate/up row pairs per stage
 constexpr int DEC_SB = VQ2_DEC_SB;        // down rows per stage
 constexpr int DEC_MAXG = 64;              // max 64-groups per input row (4096 / 64)
-constexpr int CB_COPIES = 16;
-constexpr int CB_BYTES = 1024 * 8 * CB_COPIES;   // 128 KB
+#ifndef VQ2_DEC_CB_COPIES
+#define VQ2_DEC_CB_COPIES 16
+#endif
+constexpr int CB_COPIES = VQ2_DEC_CB_COPIES;     // codebook copies in shared memory (16: 128 KB)
+constexpr int CB_SHIFT = CB_COPIES == 16 ? 7 : 6;  // log2(bytes per entry = 8 x copies)
+constexpr int CB_BYTES = 1024 * 8 * CB_COPIES;
 
 struct DecodeShared {
   uint64_t full[DEC_STAGES];
@@ -210,7 +214,7 @@ __device__ __forceinline__ void multi_dot(const uint4* lo, const uint32_t* hw, c
       for (int r = 0; r < R; ++r) {
         const uint32_t w = ids[r][j & 1];
         const uint32_t id = (j & 2) ? (w >> 16) : (w & 0xFFFFu);
-        const uint2 c = *(const uint2*)(cbl + (id << 7));
+        const uint2 c = *(const uint2*)(cbl + (id << CB_SHIFT));
         const __half2 c01 = *(const __half2*)&c.x, c23 = *(const __half2*)&c.y;
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
@@ -263,39 +267,63 @@ __device__ __forceinline__ float warp_reduce_multi(float* v) {
   return v[0];
 }
 
-// CTA-wide staging of one unit's activation: consumer thread g (< ng) holds the fp32 values of
-// 64-group g in v; it is rotated (FWHT), the max over its 32-group K-slice is formed in shared
-// memory, and the group is scaled by a power of two so that max|x| * max|C| * 32 <= 2^15 over the
-// slice (no half2 partial can overflow) and stored as half2 in sh->xs[g]. sh->slice_inv[s] gets
-// the factor undoing the scale and the Hadamard's 1/8. Called by all consumer threads.
-__device__ __forceinline__ void stage_activation(float* v, bool valid, int g, DecodeShared* sh) {
-  const int tid = threadIdx.x;
+// CTA-wide staging of one unit's activation. Consumer warp w rotates the 64-groups g = w, w + NW,
+// ... with a shuffle FWHT (lane holds elements lane and lane + 32 of a group; ld(i) reads element i
+// of the row as fp32); the max over each 32-group K-slice is formed in shared memory; every group
+// is scaled by a power of two so that max|x| * max|C| * 32 <= 2^15 over its slice (no half2
+// partial can overflow) and stored as half2 in sh->xs[g]. sh->slice_inv[s] gets the factor undoing
+// the scale and the Hadamard's 1/8. Called by all consumer threads.
+template <typename LoadF>
+__device__ __forceinline__ void stage_activation(LoadF ld, int ng, DecodeShared* sh) {
+  constexpr int GPW = (DEC_MAXG + DEC_NW - 1) / DEC_NW;   // groups per warp
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid < 2) sh->slice_max[tid] = 0u;
   consumer_sync();                         // previous unit's xs no longer read; maxima reset
-  float amax = 0.f;
-  if (valid) {
-    fwht64(v);
+  float va[GPW], vb[GPW];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) amax = fmaxf(amax, fabsf(v[i]));
-    atomicMax(&sh->slice_max[g >> 5], __float_as_uint(amax));   // non-negative floats order as ints
+  for (int i = 0; i < GPW; ++i) {
+    const int g = warp + i * DEC_NW;
+    va[i] = vb[i] = 0.f;
+    if (g < ng) {
+      float a = ld(g * 64 + lane), b = ld(g * 64 + 32 + lane);
+      const float t = a + b;
+      b = a - b;
+      a = t;
+#pragma unroll
+      for (int len = 16; len >= 1; len >>= 1) {
+        const float pa = __shfl_xor_sync(0xffffffffu, a, len), pb = __shfl_xor_sync(0xffffffffu, b, len);
+        a = (lane & len) ? (pa - a) : (a + pa);
+        b = (lane & len) ? (pb - b) : (b + pb);
+      }
+      va[i] = a;
+      vb[i] = b;
+      const float m = warp_max(fmaxf(fabsf(a), fabsf(b)));
+      if (lane == 0) atomicMax(&sh->slice_max[g >> 5], __float_as_uint(m));   // non-negative: int order
+    }
   }
   consumer_sync();
-  if (valid) {
-    const float smax = __uint_as_float(sh->slice_max[g >> 5]);
-    float sc = 1.f, inv = 1.f;
-    if (smax > 0.f) {
-      int ex;
-      frexpf((1024.f / sh->cmax) / smax, &ex);      // ratio in [2^(ex-1), 2^ex)
-      const int s = max(-100, min(100, ex - 1));
-      sc = ldexpf(1.f, s);
-      inv = ldexpf(1.f, -s);
-    }
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      __half2 h = __floats2half2_rn(v[2 * i] * sc, v[2 * i + 1] * sc);
-      sh->xs[g][i] = *(uint32_t*)&h;
+  for (int i = 0; i < GPW; ++i) {
+    const int g = warp + i * DEC_NW;
+    if (g < ng) {
+      const float smax = __uint_as_float(sh->slice_max[g >> 5]);
+      float sc = 1.f, inv = 1.f;
+      if (smax > 0.f) {
+        int ex;
+        frexpf((1024.f / sh->cmax) / smax, &ex);      // ratio in [2^(ex-1), 2^ex)
+        const int s = max(-100, min(100, ex - 1));
+        sc = ldexpf(1.f, s);
+        inv = ldexpf(1.f, -s);
+      }
+      const float ea = va[i] * sc, eb = vb[i] * sc;
+      const float na = __shfl_down_sync(0xffffffffu, ea, 1), nb = __shfl_down_sync(0xffffffffu, eb, 1);
+      if (!(lane & 1)) {                          // element pairs (2j, 2j+1) -> half2 j
+        __half2 h0 = __floats2half2_rn(ea, na), h1 = __floats2half2_rn(eb, nb);
+        sh->xs[g][lane >> 1] = *(uint32_t*)&h0;
+        sh->xs[g][16 + (lane >> 1)] = *(uint32_t*)&h1;
+      }
+      if (lane == 0 && (g & 31) == 0) sh->slice_inv[g >> 5] = inv * 0.125f;
     }
-    if ((g & 31) == 0) sh->slice_inv[g >> 5] = inv * 0.125f;
   }
   consumer_sync();
 }
@@ -306,32 +334,6 @@ __device__ __forceinline__ void load_xs(const DecodeShared* sh, int g, bool gv, 
   for (int i = 0; i < 32; i += 4) {
     const uint4 q = gv ? *(const uint4*)&sh->xs[g][i] : make_uint4(0, 0, 0, 0);
     xr[i] = q.x; xr[i + 1] = q.y; xr[i + 2] = q.z; xr[i + 3] = q.w;
-  }
-}
-
-// 64 consecutive activations of one token (bf16 / f16 / f32) -> fp32 registers.
-__device__ __forceinline__ void load_x64(const void* x, int dt, size_t base, float* v) {
-  if (dt == VQ2_DT_F32) {
-    const float4* p = (const float4*)((const float*)x + base);
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      const float4 f = p[i];
-      v[4 * i] = f.x; v[4 * i + 1] = f.y; v[4 * i + 2] = f.z; v[4 * i + 3] = f.w;
-    }
-  } else {
-    const uint4* p = (const uint4*)((const uint16_t*)x + base);
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint4 u = p[i];
-      const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-#pragma unroll
-      for (int k = 0; k < 4; ++k) {
-        float2 f;
-        if (dt == VQ2_DT_BF16) f = __bfloat1622float2(*(const __nv_bfloat162*)&w[k]);
-        else f = __half22float2(*(const __half2*)&w[k]);
-        v[8 * i + 2 * k] = f.x; v[8 * i + 2 * k + 1] = f.y;
-      }
-    }
   }
 }
 
@@ -499,11 +501,10 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
     if (u != ucur) {   // uniform across consumer warps: all walk the same chunk list
       ucur = u;
       mcur = sh->unit_m[u][0];
-      const int tg = threadIdx.x;
-      float v[64];
-      const bool ok = tg < ng;
-      if (ok) load_x64(a.x, a.x_dtype, (size_t)(mcur / a.topk) * H + tg * 64, v);
-      stage_activation(v, ok, tg, sh);
+      const size_t xrow = (size_t)(mcur / a.topk) * H;
+      const void* xp = a.x;
+      const int xdt = a.x_dtype;
+      stage_activation([&](int i) { return load_act(xp, xdt, xrow + i); }, ng, sh);
       load_xs(sh, g, gv, xr[0]);
       inv = sh->slice_inv[h];
       if (threadIdx.x == 0 && c == 0) PROBE(0, 5);
@@ -606,16 +607,8 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
         *(float4*)&sh->scratch[4 * i4] = r;
       }
       consumer_sync();
-      float v[64];
-      const bool ok = tg < ng;
-      if (ok) {
-#pragma unroll
-        for (int k4 = 0; k4 < 16; ++k4) {
-          const float4 f = *(const float4*)&sh->scratch[tg * 64 + 4 * k4];
-          v[4 * k4] = f.x; v[4 * k4 + 1] = f.y; v[4 * k4 + 2] = f.z; v[4 * k4 + 3] = f.w;
-        }
-      }
-      stage_activation(v, ok, tg, sh);
+      const float* scr = sh->scratch;
+      stage_activation([&](int i) { return scr[i]; }, ng, sh);
       load_xs(sh, g, gv, xr[0]);
       wsc = a.topk_w[m] * sh->slice_inv[h];
       if (threadIdx.x == 0 && c == 0) PROBE(1, 5);
