@@ -191,9 +191,16 @@ __device__ __forceinline__ void fill_codebook(uint8_t* cbs, DecodeShared* sh) {
 // R independent 64-group dot products for NT tokens: for each row r, sum over the group's 16
 // sub-vectors of <codebook[id_s], x_s>, accumulated in two half2 chains, returned in fp32.
 // lo[r]: the 16 index low bytes; hw[r]: the 4 hi bytes; x[t]: 32 half2 regs of the rotated group.
+__device__ __forceinline__ uint2 lds64(uint32_t addr) {
+  uint2 v;
+  asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
+  return v;
+}
+
 template <int R, int NT>
-__device__ __forceinline__ void multi_dot(const uint4* lo, const uint32_t* hw, const uint8_t* cbl,
+__device__ __forceinline__ void multi_dot(const uint4* lo, const uint32_t* hw, const uint8_t* cbl_ptr,
                                           const uint32_t (*x)[32], float (*out)[NT]) {
+  const uint32_t cbl = smem_u32(cbl_ptr);          // 32-bit shared-window address of this lane's copy
   __half2 a0[R][NT], a1[R][NT];
 #pragma unroll
   for (int r = 0; r < R; ++r)
@@ -214,7 +221,7 @@ __device__ __forceinline__ void multi_dot(const uint4* lo, const uint32_t* hw, c
       for (int r = 0; r < R; ++r) {
         const uint32_t w = ids[r][j & 1];
         const uint32_t id = (j & 2) ? (w >> 16) : (w & 0xFFFFu);
-        const uint2 c = *(const uint2*)(cbl + (id << CB_SHIFT));
+        const uint2 c = lds64(cbl + (id << CB_SHIFT));
         const __half2 c01 = *(const __half2*)&c.x, c23 = *(const __half2*)&c.y;
 #pragma unroll
         for (int t = 0; t < NT; ++t) {
