@@ -156,13 +156,33 @@ def bench_ep(args, rank, world, metric):
         layers.append(full)
     fns = [cuda_expert_fn(L) for L in layers]
 
+    graphs_used = {}
+
     def run(per_rank, steps, warmup):
         xs = [synth.make_tokens(per_rank, H, seed=50 + 97 * rank + j, device=dev) for j in range(8)]
         rs = [synth.route_uniform(per_rank, E, K, seed=500 + 97 * rank + j, device=dev) for j in range(8)]
-        moe = ep_moe_gather if per_rank * world <= 512 else ep_moe
+        gather = per_rank * world <= 512
+        moe = ep_moe_gather if gather else ep_moe
         step = lambda i: moe(xs[i % 8], rs[i % 8][0], rs[i % 8][1], fns[i % nlayers], E)
         for i in range(warmup):
             step(i)
+        torch.cuda.synchronize()
+        if gather:
+            # the gather-mode step has no host read: replay it from CUDA graphs, one per input set
+            try:
+                gs = []
+                for j in range(8):
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g):
+                        step(j)
+                    gs.append(g)
+                torch.cuda.synchronize()
+                dist.barrier()
+                step = lambda i: gs[i % 8].replay()
+                graphs_used[per_rank] = True
+            except Exception as ex:            # fall back to eager launches
+                graphs_used[per_rank] = f"eager ({type(ex).__name__})"
+                torch.cuda.synchronize()
         torch.cuda.synchronize()
         dist.barrier()
         torch.cuda.synchronize()
@@ -192,6 +212,7 @@ def bench_ep(args, rank, world, metric):
                 "config": {"workload": "expert-parallel decode, 1 token per rank per step",
                            "H": H, "I": I, "E": E, "topk": K, "experts_per_rank": per,
                            "parallelism": f"ep{world}", "l2": f"{nlayers} layers cycled"},
-                "ep": extra, "gpu_launches": 2 * args.steps}
+                "ep": extra, "cuda_graphs": {str(k): v for k, v in graphs_used.items()},
+                "gpu_launches": 2 * args.steps}
         print(json.dumps(line), flush=True)
     dist.destroy_process_group()
