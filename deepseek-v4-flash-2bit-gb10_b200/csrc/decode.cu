@@ -124,20 +124,26 @@ __device__ void build_plan(const void* ids, int ids_dtype, int M, int E, int exp
 
 // ------------------------------------------------------------------ chunk iteration
 struct ChunkIter {
-  long r, end;       // flattened row position [unit][row]
+  // The CTA's range [r, end) is contiguous, so the (unit, row) position is found by one division
+  // here and then advanced incrementally (no 64-bit divide per chunk).
+  int u, row0, left;  // current unit, row within it, rows of the range still to hand out
   int rows_per_unit, S;
   __device__ ChunkIter(long total_rows, int rpu, int S_) : rows_per_unit(rpu), S(S_) {
-    long ng = total_rows / DEC_GRAN;
-    r = (long)blockIdx.x * ng / gridDim.x * DEC_GRAN;
-    end = (long)(blockIdx.x + 1) * ng / gridDim.x * DEC_GRAN;
+    const long ng = total_rows / DEC_GRAN;
+    const long r = (long)blockIdx.x * ng / gridDim.x * DEC_GRAN;
+    const long end = (long)(blockIdx.x + 1) * ng / gridDim.x * DEC_GRAN;
+    u = (int)(r / rpu);
+    row0 = (int)(r % rpu);
+    left = (int)(end - r);
   }
-  __device__ bool next(int& u, int& row0, int& n) {
-    if (r >= end) return false;
-    u = (int)(r / rows_per_unit);
-    row0 = (int)(r % rows_per_unit);
-    long lim = min((long)(rows_per_unit - row0), end - r);
-    n = (int)min((long)S, lim);
-    r += n;
+  __device__ bool next(int& uo, int& row0o, int& n) {
+    if (left <= 0) return false;
+    n = min(S, min(rows_per_unit - row0, left));
+    uo = u;
+    row0o = row0;
+    left -= n;
+    row0 += n;
+    if (row0 == rows_per_unit) { row0 = 0; ++u; }
     return true;
   }
 };
@@ -406,7 +412,7 @@ __device__ __forceinline__ void gateup_rows(const uint8_t* st, int rr0, int rste
   const int lane = threadIdx.x & 31;
   const int r = reduce_index<R>(lane);
   const int rr = rr0 + (r >> 1) * rstep;
-  if ((lane & (32 / R - 1)) == 0 && rr < n) part[(((size_t)m * KH + h) * 2 + (r & 1)) * I + i0 + rr] = tot;
+  if ((lane & (32 / R - 1)) == 0 && rr < n) part[((m * KH + h) * 2 + (r & 1)) * I + i0 + rr] = tot;
 }
 
 // One pass of a consumer warp over R down rows of a stage (rows rr0 + r*rstep).
