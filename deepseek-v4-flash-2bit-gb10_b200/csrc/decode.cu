@@ -59,67 +59,77 @@ struct DecodeShared {
   int abort;
   float cmax;
   float red[32];
-  unsigned slice_max[2];
-  float slice_inv[2];
+  float ginv[DEC_MAXG];                     // per 64-group: 2^-scale / 8 of the staged activation
   alignas(16) uint32_t xs[DEC_MAXG][32];    // rotated, scaled activation of the current unit (half2 per group)
   // prologue: the codebook as loaded (bulk-copy destination, 8 KB); main loop (down kernel): the
   // combined silu(gate) * up row of the current unit, fp32, before rotation
   alignas(16) float scratch[DEC_MAXG * 64];
   short unit_e[VQ2_DECODE_MAX_PAIRS];
   short unit_m[VQ2_DECODE_MAX_PAIRS][DEC_TT];
-  int ekey[VQ2_DECODE_MAX_PAIRS];
-  int cnt[1024];
+  alignas(16) int ekey[VQ2_DECODE_MAX_PAIRS];
 };
 
+#ifdef VQ2_DEC_PROBE
+// Development probe (off in the product build): per-CTA global-timer stamps of the phases.
+__device__ unsigned long long g_probe[2][1024][16];
+__device__ __forceinline__ unsigned long long gtime() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+// slot 15: globaltimer anchor, slot 14: clock64 at the anchor; other slots: clock64
+__device__ unsigned long long g_sprobe[1024][2][8];
+__device__ unsigned long long g_bprobe[2][1024][8];
+#define BP(i) do { if (threadIdx.x == 0) g_bprobe[pk][blockIdx.x][i] = clock64(); } while (0)
+#define SP(i) do { if (pk == 2 && (threadIdx.x & 31) == 0 && (threadIdx.x >> 5) % 15 == 0) \
+    g_sprobe[blockIdx.x][(threadIdx.x >> 5) / 15][i] = clock64(); } while (0)
+#define PROBE(k, i) do { \
+    if ((i) == 0) { g_probe[k][blockIdx.x][14] = clock64(); g_probe[k][blockIdx.x][15] = gtime(); } \
+    g_probe[k][blockIdx.x][i] = clock64(); } while (0)
+#else
+#define PROBE(k, i) do {} while (0)
+#define SP(i) do {} while (0)
+#define BP(i) do {} while (0)
+#endif
+
 // ------------------------------------------------------------------ plan: group pairs by expert
-// Unit u = (local expert, up to DEC_TT pair indices), units ordered by expert, pairs of an
-// expert in pair order. Every CTA builds the same plan.
+// Unit u = one (local expert, pair) with units ordered by expert and, within an expert, by pair
+// index. Pair m's unit is its rank: the number of valid pairs q with (e_q, q) < (e_m, m). Every
+// CTA builds the same plan (M <= VQ2_DECODE_MAX_PAIRS, so the O(M) rank scan per pair is short;
+// it reads the keys four at a time as shared-memory broadcasts).
+static_assert(DEC_TT == 1, "one pair per unit");
 __device__ void build_plan(const void* ids, int ids_dtype, int M, int E, int expert_base,
-                           DecodeShared* sh) {
+                           DecodeShared* sh, int pk = 0) {
   const int tid = threadIdx.x, nt = blockDim.x;
-  for (int e = tid; e < E; e += nt) sh->cnt[e] = 0;
-  for (int u = tid; u < M; u += nt)
-    for (int t = 0; t < DEC_TT; ++t) sh->unit_m[u][t] = -1;
-  for (int m = tid; m < M; m += nt) {
-    int e = load_id(ids, ids_dtype, m) - expert_base;
-    sh->ekey[m] = (e >= 0 && e < E) ? e : -1;
-  }
-  __syncthreads();
-  for (int m = tid; m < M; m += nt) {
-    int e = sh->ekey[m];
-    if (e >= 0) atomicAdd(&sh->cnt[e], 1);
-  }
-  __syncthreads();
-  if (tid < 32) {  // warp 0: exclusive scan over experts of ceil(cnt/TT) -> unit offsets
-    const int per = (E + 31) / 32;
-    const int b0 = tid * per;
-    int local = 0;
-    for (int e = b0; e < min(E, b0 + per); ++e) local += (sh->cnt[e] + DEC_TT - 1) / DEC_TT;
-    int incl = local;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      int v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (tid >= o) incl += v;
+  static_assert(DEC_THREADS >= VQ2_DECODE_MAX_PAIRS, "build_plan holds one pair per thread");
+  BP(0);
+  const int M4 = (M + 3) & ~3;
+  int valid = 0;
+  if (tid < M4) {                               // one pair per thread (blockDim > max pairs)
+    int key = 0x7FFFFFFF;                       // padding / foreign expert: sorts last, never counted
+    if (tid < M) {
+      const int e = load_id(ids, ids_dtype, tid) - expert_base;
+      if (e >= 0 && e < E) { key = e; valid = 1; }
     }
-    int run = incl - local;
-    for (int e = b0; e < min(E, b0 + per); ++e) {
-      int c = sh->cnt[e];
-      sh->cnt[e] = run;
-      run += (c + DEC_TT - 1) / DEC_TT;
-    }
-    if (tid == 31) sh->nunits = incl;
+    sh->ekey[tid] = key;
   }
-  __syncthreads();
+  const int nunits = __syncthreads_count(valid);
+  BP(1);
   for (int m = tid; m < M; m += nt) {
-    int e = sh->ekey[m];
-    if (e < 0) continue;
+    const int e = sh->ekey[m];
+    if (e == 0x7FFFFFFF) continue;
     int rank = 0;
-    for (int q = 0; q < m; ++q) rank += (sh->ekey[q] == e);
-    int u = sh->cnt[e] + rank / DEC_TT;
-    sh->unit_e[u] = (short)e;
-    sh->unit_m[u][rank % DEC_TT] = (short)m;
+    for (int q = 0; q < M4; q += 4) {
+      const int4 k4 = *(const int4*)&sh->ekey[q];
+      rank += (k4.x < e || (k4.x == e && q < m)) + (k4.y < e || (k4.y == e && q + 1 < m)) +
+              (k4.z < e || (k4.z == e && q + 2 < m)) + (k4.w < e || (k4.w == e && q + 3 < m));
+    }
+    sh->unit_e[rank] = (short)e;
+    sh->unit_m[rank][0] = (short)m;
   }
+  if (tid == 0) sh->nunits = nunits;
   __syncthreads();
+  BP(2);
 }
 
 // ------------------------------------------------------------------ chunk iteration
@@ -128,12 +138,13 @@ struct ChunkIter {
   // here and then advanced incrementally (no 64-bit divide per chunk).
   int u, row0, left;  // current unit, row within it, rows of the range still to hand out
   int rows_per_unit, S;
+  // 32-bit arithmetic: total_rows <= max pairs * 4096 rows = 2^21, grid <= 1024 CTAs.
   __device__ ChunkIter(long total_rows, int rpu, int S_) : rows_per_unit(rpu), S(S_) {
-    const long ng = total_rows / DEC_GRAN;
-    const long r = (long)blockIdx.x * ng / gridDim.x * DEC_GRAN;
-    const long end = (long)(blockIdx.x + 1) * ng / gridDim.x * DEC_GRAN;
-    u = (int)(r / rpu);
-    row0 = (int)(r % rpu);
+    const unsigned ng = (unsigned)total_rows / DEC_GRAN;
+    const unsigned r = blockIdx.x * ng / gridDim.x * DEC_GRAN;
+    const unsigned end = (blockIdx.x + 1) * ng / gridDim.x * DEC_GRAN;
+    u = (int)(r / (unsigned)rpu);
+    row0 = (int)(r - (unsigned)u * rpu);
     left = (int)(end - r);
   }
   __device__ bool next(int& uo, int& row0o, int& n) {
@@ -148,18 +159,6 @@ struct ChunkIter {
   }
 };
 
-#ifdef VQ2_DEC_PROBE
-// Development probe (off in the product build): per-CTA global-timer stamps of the phases.
-__device__ unsigned long long g_probe[2][1024][8];
-__device__ __forceinline__ unsigned long long gtime() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-#define PROBE(k, i) do { g_probe[k][blockIdx.x][i] = gtime(); } while (0)
-#else
-#define PROBE(k, i) do {} while (0)
-#endif
 
 // consumer-only barrier (named barrier 1; the producer warp never joins it)
 __device__ __forceinline__ void consumer_sync() {
@@ -282,23 +281,31 @@ __device__ __forceinline__ float warp_reduce_multi(float* v) {
 
 // CTA-wide staging of one unit's activation. Consumer warp w rotates the 64-groups g = w, w + NW,
 // ... with a shuffle FWHT (lane holds elements lane and lane + 32 of a group; ld(i) reads element i
-// of the row as fp32); the max over each 32-group K-slice is formed in shared memory; every group
-// is scaled by a power of two so that max|x| * max|C| * 32 <= 2^15 over its slice (no half2
-// partial can overflow) and stored as half2 in sh->xs[g]. sh->slice_inv[s] gets the factor undoing
-// the scale and the Hadamard's 1/8. Called by all consumer threads.
+// of the row as fp32), scales each group by a power of two chosen from the group's max so that
+// max|x| * max|C| * 32 <= 2^15 (no half2 partial of the group's dot products can overflow), and
+// stores it as half2 in sh->xs[g]; sh->ginv[g] gets the factor undoing the scale and the
+// Hadamard's 1/8. Called by all consumer threads.
 template <typename LoadF>
-__device__ __forceinline__ void stage_activation(LoadF ld, int ng, DecodeShared* sh) {
+__device__ __forceinline__ void stage_activation(LoadF ld, int ng, DecodeShared* sh, int pk = 0) {
   constexpr int GPW = (DEC_MAXG + DEC_NW - 1) / DEC_NW;   // groups per warp
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  if (tid < 2) sh->slice_max[tid] = 0u;
-  consumer_sync();                         // previous unit's xs no longer read; maxima reset
+  SP(0);
+  consumer_sync();                         // the previous unit's xs / ginv are no longer read
+  SP(1);
   float va[GPW], vb[GPW];
+#pragma unroll
+  for (int i = 0; i < GPW; ++i) {   // all loads first, so their latencies overlap
+    const int g = warp + i * DEC_NW;
+    va[i] = vb[i] = 0.f;
+    if (g < ng) { va[i] = ld(g * 64 + lane); vb[i] = ld(g * 64 + 32 + lane); }
+  }
+  SP(2);
+  const float climit = 1024.f / sh->cmax;
 #pragma unroll
   for (int i = 0; i < GPW; ++i) {
     const int g = warp + i * DEC_NW;
-    va[i] = vb[i] = 0.f;
     if (g < ng) {
-      float a = ld(g * 64 + lane), b = ld(g * 64 + 32 + lane);
+      float a = va[i], b = vb[i];
       const float t = a + b;
       b = a - b;
       a = t;
@@ -308,37 +315,29 @@ __device__ __forceinline__ void stage_activation(LoadF ld, int ng, DecodeShared*
         a = (lane & len) ? (pa - a) : (a + pa);
         b = (lane & len) ? (pb - b) : (b + pb);
       }
-      va[i] = a;
-      vb[i] = b;
-      const float m = warp_max(fmaxf(fabsf(a), fabsf(b)));
-      if (lane == 0) atomicMax(&sh->slice_max[g >> 5], __float_as_uint(m));   // non-negative: int order
-    }
-  }
-  consumer_sync();
-#pragma unroll
-  for (int i = 0; i < GPW; ++i) {
-    const int g = warp + i * DEC_NW;
-    if (g < ng) {
-      const float smax = __uint_as_float(sh->slice_max[g >> 5]);
+      const float gmax = warp_max(fmaxf(fabsf(a), fabsf(b)));
       float sc = 1.f, inv = 1.f;
-      if (smax > 0.f) {
-        int ex;
-        frexpf((1024.f / sh->cmax) / smax, &ex);      // ratio in [2^(ex-1), 2^ex)
-        const int s = max(-100, min(100, ex - 1));
-        sc = ldexpf(1.f, s);
-        inv = ldexpf(1.f, -s);
+      if (gmax > 0.f) {
+        // s = floor(log2(ratio)) from the exponent field (ratio > 0; subnormal reads as -127,
+        // inf as +128, both clamped); 2^s and 2^-s are built from exponent bits (|s| <= 100)
+        const float ratio = climit / gmax;
+        const int s = max(-100, min(100, (int)((__float_as_uint(ratio) >> 23) & 0xFF) - 127));
+        sc = __uint_as_float((uint32_t)(127 + s) << 23);
+        inv = __uint_as_float((uint32_t)(127 - s) << 23);
       }
-      const float ea = va[i] * sc, eb = vb[i] * sc;
+      const float ea = a * sc, eb = b * sc;
       const float na = __shfl_down_sync(0xffffffffu, ea, 1), nb = __shfl_down_sync(0xffffffffu, eb, 1);
       if (!(lane & 1)) {                          // element pairs (2j, 2j+1) -> half2 j
         __half2 h0 = __floats2half2_rn(ea, na), h1 = __floats2half2_rn(eb, nb);
         sh->xs[g][lane >> 1] = *(uint32_t*)&h0;
         sh->xs[g][16 + (lane >> 1)] = *(uint32_t*)&h1;
       }
-      if (lane == 0 && (g & 31) == 0) sh->slice_inv[g >> 5] = inv * 0.125f;
+      if (lane == 0) sh->ginv[g] = inv * 0.125f;
     }
   }
+  SP(5);
   consumer_sync();
+  SP(6);
 }
 
 // A consumer lane's copy of its group's staged activation (zeros past the row's groups).
@@ -365,7 +364,7 @@ __device__ __forceinline__ DecSmem dec_smem(uint8_t* smem) {
 }
 
 // Barrier init, codebook bulk copy, expert plan (all threads; ends with __syncthreads).
-__device__ __forceinline__ void dec_prologue(const vq2_moe_args& a, const uint16_t* cb, DecSmem d) {
+__device__ __forceinline__ void dec_prologue(const vq2_moe_args& a, const uint16_t* cb, DecSmem d, int pk) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < DEC_STAGES; ++s) { mbar_init(&d.sh->full[s], 1); mbar_init(&d.sh->empty[s], DEC_NW); }
     mbar_init(&d.sh->cbbar, 1);
@@ -374,7 +373,7 @@ __device__ __forceinline__ void dec_prologue(const vq2_moe_args& a, const uint16
     mbar_arrive_expect_tx(&d.sh->cbbar, 1024 * 4 * 2);
     bulk_g2s(d.sh->scratch, cb, 1024 * 4 * 2, &d.sh->cbbar);
   }
-  build_plan(a.topk_ids, a.ids_dtype, a.N * a.topk, a.E, a.expert_base, d.sh);
+  build_plan(a.topk_ids, a.ids_dtype, a.N * a.topk, a.E, a.expert_base, d.sh, pk);
 }
 
 // One pass of a consumer warp over RB gate/up row pairs of a stage (rows rr0 + k*rstep):
@@ -462,12 +461,19 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
   const uint32_t lo_b = S * nsub, hi_b = S * (nsub / 4), sc_b = S * ng * 2;
   const uint32_t stage_b = 2 * (lo_b + hi_b + sc_b);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  {  // warm the path to the activations (first 64 KB) while the plan is built
+    const size_t xbytes = (size_t)a.N * H * (a.x_dtype == VQ2_DT_F32 ? 4 : 2);
+    const size_t lim = xbytes < 65536 ? xbytes : 65536;
+    for (size_t o = (size_t)threadIdx.x * 128; o < lim; o += DEC_THREADS * 128)
+      asm volatile("prefetch.global.L2 [%0];" ::"l"((const char*)a.x + o));
+  }
 
-  dec_prologue(a, a.w13_cb, d);
+  dec_prologue(a, a.w13_cb, d, 0);
   const long total = (long)sh->nunits * I;
 
   if (warp == DEC_NW) {   // ---------------- producer
     if (lane == 0) {
+      const uint64_t pol = l2_evict_first();
       ChunkIter it(total, I, S);
       int u, i0, n, c = 0;
       while (it.next(u, i0, n)) {
@@ -477,12 +483,15 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
         const long rg = e * 2 * I + i0, ru = rg + I;
         uint8_t* st = d.stages + slot * stage_b;
         mbar_arrive_expect_tx(&sh->full[slot], 2u * n * (nsub + nsub / 4 + ng * 2));
-        bulk_g2s(st, a.w13_lo + rg * nsub, n * nsub, &sh->full[slot]);
-        bulk_g2s(st + lo_b, a.w13_lo + ru * nsub, n * nsub, &sh->full[slot]);
-        bulk_g2s(st + 2 * lo_b, a.w13_hi + rg * (nsub / 4), n * (nsub / 4), &sh->full[slot]);
-        bulk_g2s(st + 2 * lo_b + hi_b, a.w13_hi + ru * (nsub / 4), n * (nsub / 4), &sh->full[slot]);
-        bulk_g2s(st + 2 * (lo_b + hi_b), a.w13_sc + rg * ng, n * ng * 2, &sh->full[slot]);
-        bulk_g2s(st + 2 * (lo_b + hi_b) + sc_b, a.w13_sc + ru * ng, n * ng * 2, &sh->full[slot]);
+        bulk_g2s_stream(st, a.w13_lo + rg * nsub, n * nsub, &sh->full[slot], pol);
+        bulk_g2s_stream(st + lo_b, a.w13_lo + ru * nsub, n * nsub, &sh->full[slot], pol);
+        bulk_g2s_stream(st + 2 * lo_b, a.w13_hi + rg * (nsub / 4), n * (nsub / 4), &sh->full[slot], pol);
+        bulk_g2s_stream(st + 2 * lo_b + hi_b, a.w13_hi + ru * (nsub / 4), n * (nsub / 4), &sh->full[slot], pol);
+        bulk_g2s_stream(st + 2 * (lo_b + hi_b), a.w13_sc + rg * ng, n * ng * 2, &sh->full[slot], pol);
+        bulk_g2s_stream(st + 2 * (lo_b + hi_b) + sc_b, a.w13_sc + ru * ng, n * ng * 2, &sh->full[slot], pol);
+#ifdef VQ2_DEC_PROBE
+        if (c == 0) { PROBE(0, 8); mbar_wait(&sh->full[0], 0); PROBE(0, 9); }
+#endif
         ++c;
       }
       // drain: every issued copy must land before the CTA exits
@@ -513,14 +522,25 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
     const int slot = c % DEC_STAGES;
     if (u != ucur) {   // uniform across consumer warps: all walk the same chunk list
       ucur = u;
+      const int mprev = mcur;
       mcur = sh->unit_m[u][0];
-      const size_t xrow = (size_t)(mcur / a.topk) * H;
-      const void* xp = a.x;
-      const int xdt = a.x_dtype;
-      stage_activation([&](int i) { return load_act(xp, xdt, xrow + i); }, ng, sh);
-      load_xs(sh, g, gv, xr[0]);
-      inv = sh->slice_inv[h];
-      if (threadIdx.x == 0 && c == 0) PROBE(0, 5);
+      if (mprev < 0 || mprev / a.topk != mcur / a.topk) {   // same token: xs is still valid
+        const size_t xrow = (size_t)(mcur / a.topk) * H;
+        const void* xp = a.x;
+        const int xdt = a.x_dtype;
+        stage_activation([&](int i) { return load_act(xp, xdt, xrow + i); }, ng, sh);
+        load_xs(sh, g, gv, xr[0]);
+        inv = gv ? sh->ginv[g] : 0.f;
+        if (threadIdx.x == 0 && c == 0) PROBE(0, 5);
+#ifdef VQ2_DEC_PROBE2
+        if (c == 0) {
+          stage_activation([&](int i) { return load_act(xp, xdt, xrow + i); }, ng, sh, 2);
+          load_xs(sh, g, gv, xr[0]);
+          { const int pk = 2; SP(7); }
+          if (threadIdx.x == 0) PROBE(0, 10);
+        }
+#endif
+      }
     }
     if (!mbar_wait(&sh->full[slot], (c / DEC_STAGES) & 1)) break;
     if (threadIdx.x == 0 && c == 0) PROBE(0, 3);
@@ -557,23 +577,27 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
   const uint32_t stage_b = lo_b + hi_b + sc_b;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  dec_prologue(a, a.w2_cb, d);
+  dec_prologue(a, a.w2_cb, d, 1);
   const long total = (long)sh->nunits * H;
 
   if (warp == DEC_NW) {   // ---------------- producer: weights do not depend on the gate/up grid
     if (lane == 0) {
+      const uint64_t pol = l2_evict_first();
       ChunkIter it(total, H, S);
       int u, h0, n, c = 0;
       while (it.next(u, h0, n)) {
         const int slot = c % DEC_STAGES;
         if (c >= DEC_STAGES && !mbar_wait(&sh->empty[slot], ((c / DEC_STAGES) - 1) & 1)) { sh->abort = 1; break; }
         const long r = (long)sh->unit_e[u] * H + h0;
-        if (c == 0) PROBE(1, 6);
+        if (c == 0) PROBE(1, 8);
         uint8_t* st = d.stages + slot * stage_b;
         mbar_arrive_expect_tx(&sh->full[slot], (uint32_t)n * (nsub + nsub / 4 + ng * 2));
-        bulk_g2s(st, a.w2_lo + r * nsub, n * nsub, &sh->full[slot]);
-        bulk_g2s(st + lo_b, a.w2_hi + r * (nsub / 4), n * (nsub / 4), &sh->full[slot]);
-        bulk_g2s(st + lo_b + hi_b, a.w2_sc + r * ng, n * ng * 2, &sh->full[slot]);
+        bulk_g2s_stream(st, a.w2_lo + r * nsub, n * nsub, &sh->full[slot], pol);
+        bulk_g2s_stream(st + lo_b, a.w2_hi + r * (nsub / 4), n * (nsub / 4), &sh->full[slot], pol);
+        bulk_g2s_stream(st + lo_b + hi_b, a.w2_sc + r * ng, n * ng * 2, &sh->full[slot], pol);
+#ifdef VQ2_DEC_PROBE
+        if (c == 0) { mbar_wait(&sh->full[0], 0); PROBE(1, 9); }
+#endif
         ++c;
       }
       for (int q = max(0, c - DEC_STAGES); q < c; ++q) mbar_wait(&sh->full[q % DEC_STAGES], (q / DEC_STAGES) & 1);
@@ -621,9 +645,9 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
       }
       consumer_sync();
       const float* scr = sh->scratch;
-      stage_activation([&](int i) { return scr[i]; }, ng, sh);
+      stage_activation([&](int i) { return scr[i]; }, ng, sh, 1);
       load_xs(sh, g, gv, xr[0]);
-      wsc = a.topk_w[m] * sh->slice_inv[h];
+      wsc = a.topk_w[m] * (gv ? sh->ginv[g] : 0.f);
       if (threadIdx.x == 0 && c == 0) PROBE(1, 5);
     }
     if (!mbar_wait(&sh->full[slot], (c / DEC_STAGES) & 1)) break;
@@ -663,6 +687,12 @@ static DecodeLaunchCache g_dec_cache[64];
 using namespace vq2;
 
 #ifdef VQ2_DEC_PROBE
+extern "C" int vq2_bprobe_read(void* host) {
+  return (int)cudaMemcpyFromSymbol(host, g_bprobe, sizeof(g_bprobe));
+}
+extern "C" int vq2_sprobe_read(void* host) {
+  return (int)cudaMemcpyFromSymbol(host, g_sprobe, sizeof(g_sprobe));
+}
 extern "C" int vq2_probe_read(void* host) {
   return (int)cudaMemcpyFromSymbol(host, g_probe, sizeof(g_probe));
 }
@@ -728,6 +758,7 @@ extern "C" int vq2_decode(const vq2_moe_args* a, void* ws, size_t ws_bytes, void
 
 static_assert(offsetof(vq2::DecodeShared, xs) % 16 == 0, "xs must be 16-byte aligned");
 static_assert(offsetof(vq2::DecodeShared, scratch) % 16 == 0, "bulk-copy destination must be 16-byte aligned");
+static_assert(offsetof(vq2::DecodeShared, ekey) % 16 == 0, "ekey is read as int4");
 
 // ------------------------------------------------------------------ allocation-free decode
 // For callers that cannot allocate device memory at call time — for example code running under a
