@@ -60,11 +60,14 @@ struct DecodeShared {
   float cmax;
   float red[32];
   float ginv[DEC_MAXG];                     // per 64-group: 2^-scale / 8 of the staged activation
-  alignas(16) uint32_t xs[DEC_MAXG][32];    // rotated, scaled activation of the current unit (half2 per group)
+  // rotated, scaled activation of the staged unit(s), half2 per group; rows padded to 36 words so
+  // that lane l's 16-byte reads of row (base + l) start at bank 4l mod 32 (conflict-free)
+  alignas(16) uint32_t xs[DEC_MAXG][36];
   // prologue: the codebook as loaded (bulk-copy destination, 8 KB); main loop (down kernel): the
   // combined silu(gate) * up row of the current unit, fp32, before rotation
   alignas(16) float scratch[DEC_MAXG * 64];
   short unit_e[VQ2_DECODE_MAX_PAIRS];
+  float unit_w[VQ2_DECODE_MAX_PAIRS];       // routing weight of the unit's pair
   short unit_m[VQ2_DECODE_MAX_PAIRS][DEC_TT];
   alignas(16) int ekey[VQ2_DECODE_MAX_PAIRS];
 };
@@ -80,6 +83,7 @@ __device__ __forceinline__ unsigned long long gtime() {
 // slot 15: globaltimer anchor, slot 14: clock64 at the anchor; other slots: clock64
 __device__ unsigned long long g_sprobe[1024][2][8];
 __device__ unsigned long long g_bprobe[2][1024][8];
+__device__ unsigned long long g_cprobe[1024][48];
 #define BP(i) do { if (threadIdx.x == 0) g_bprobe[pk][blockIdx.x][i] = clock64(); } while (0)
 #define SP(i) do { if (pk == 2 && (threadIdx.x & 31) == 0 && (threadIdx.x >> 5) % 15 == 0) \
     g_sprobe[blockIdx.x][(threadIdx.x >> 5) / 15][i] = clock64(); } while (0)
@@ -98,26 +102,27 @@ __device__ unsigned long long g_bprobe[2][1024][8];
 // CTA builds the same plan (M <= VQ2_DECODE_MAX_PAIRS, so the O(M) rank scan per pair is short;
 // it reads the keys four at a time as shared-memory broadcasts).
 static_assert(DEC_TT == 1, "one pair per unit");
-__device__ void build_plan(const void* ids, int ids_dtype, int M, int E, int expert_base,
+__device__ void build_plan(const void* ids, int ids_dtype, const float* topk_w, int M, int E, int expert_base,
                            DecodeShared* sh, int pk = 0) {
-  const int tid = threadIdx.x, nt = blockDim.x;
+  const int tid = threadIdx.x;
   static_assert(DEC_THREADS >= VQ2_DECODE_MAX_PAIRS, "build_plan holds one pair per thread");
   BP(0);
   const int M4 = (M + 3) & ~3;
   int valid = 0;
+  float w = 0.f;
   if (tid < M4) {                               // one pair per thread (blockDim > max pairs)
     int key = 0x7FFFFFFF;                       // padding / foreign expert: sorts last, never counted
     if (tid < M) {
       const int e = load_id(ids, ids_dtype, tid) - expert_base;
+      w = topk_w[tid];
       if (e >= 0 && e < E) { key = e; valid = 1; }
     }
     sh->ekey[tid] = key;
   }
   const int nunits = __syncthreads_count(valid);
   BP(1);
-  for (int m = tid; m < M; m += nt) {
-    const int e = sh->ekey[m];
-    if (e == 0x7FFFFFFF) continue;
+  if (tid < M && sh->ekey[tid] != 0x7FFFFFFF) {
+    const int m = tid, e = sh->ekey[m];
     int rank = 0;
     for (int q = 0; q < M4; q += 4) {
       const int4 k4 = *(const int4*)&sh->ekey[q];
@@ -126,6 +131,7 @@ __device__ void build_plan(const void* ids, int ids_dtype, int M, int E, int exp
     }
     sh->unit_e[rank] = (short)e;
     sh->unit_m[rank][0] = (short)m;
+    sh->unit_w[rank] = w;
   }
   if (tid == 0) sh->nunits = nunits;
   __syncthreads();
@@ -373,7 +379,7 @@ __device__ __forceinline__ void dec_prologue(const vq2_moe_args& a, const uint16
     mbar_arrive_expect_tx(&d.sh->cbbar, 1024 * 4 * 2);
     bulk_g2s(d.sh->scratch, cb, 1024 * 4 * 2, &d.sh->cbbar);
   }
-  build_plan(a.topk_ids, a.ids_dtype, a.N * a.topk, a.E, a.expert_base, d.sh, pk);
+  build_plan(a.topk_ids, a.ids_dtype, a.topk_w, a.N * a.topk, a.E, a.expert_base, d.sh, pk);
 }
 
 // One pass of a consumer warp over RB gate/up row pairs of a stage (rows rr0 + k*rstep):
@@ -618,6 +624,36 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
   float wsc = 0.f;
   int tok = -1, ucur = -1;
   ChunkIter it(total, H, S);
+  // Units of this CTA's row range: when all of their activations fit the staging buffer they are
+  // staged together before the loop (a range that crosses a unit boundary then pays one staging).
+  const int ub = it.u, nu = it.left > 0 ? (it.row0 + it.left - 1) / H + 1 : 0;
+  const bool all_at_once = nu * ng <= DEC_MAXG;
+  // Combine the K-slice partials of units ub + k0 .. ub + k0 + cnt - 1, apply silu(gate) * up
+  // (rows of I floats in scratch) and stage them as groups k * ng + g. All consumer threads.
+  auto stage_units = [&](int k0, int cnt) {
+    const int q4 = I / 4;
+    for (int i4 = threadIdx.x; i4 < cnt * q4; i4 += DEC_NW * 32) {
+      const int k = i4 / q4, j4 = i4 - k * q4;
+      const int m = sh->unit_m[ub + k0 + k][0];
+      const float* p = part + (size_t)m * khA * 2 * I + 4 * j4;
+      float4 G = *(const float4*)p, U = *(const float4*)(p + I);
+      if (khA > 1) {
+        const float4 g2 = *(const float4*)(p + 2 * I), u2 = *(const float4*)(p + 3 * I);
+        G.x += g2.x; G.y += g2.y; G.z += g2.z; G.w += g2.w;
+        U.x += u2.x; U.y += u2.y; U.z += u2.z; U.w += u2.w;
+      }
+      float4 r;
+      r.x = G.x / (1.f + __expf(-G.x)) * U.x;
+      r.y = G.y / (1.f + __expf(-G.y)) * U.y;
+      r.z = G.z / (1.f + __expf(-G.z)) * U.z;
+      r.w = G.w / (1.f + __expf(-G.w)) * U.w;
+      *(float4*)&sh->scratch[4 * i4] = r;
+    }
+    consumer_sync();
+    const float* scr = sh->scratch;
+    stage_activation([&](int i) { return scr[i]; }, cnt * ng, sh, 1);
+  };
+  if (all_at_once && nu > 0) stage_units(0, nu);
   int u, h0, n, c = 0;
   while (it.next(u, h0, n)) {
     const int slot = c % DEC_STAGES;
@@ -625,32 +661,31 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
       ucur = u;
       const int m = sh->unit_m[u][0];
       tok = m / a.topk;
-      const int tg = threadIdx.x;
-      // combine the K-slice partials and apply silu(gate) * up: all consumer threads, 4 columns
-      // per step, loads independent so they overlap
-      for (int i4 = tg; i4 < I / 4; i4 += DEC_NW * 32) {
-        const float* p = part + (size_t)m * khA * 2 * I + 4 * i4;
-        float4 G = *(const float4*)p, U = *(const float4*)(p + I);
-        if (khA > 1) {
-          const float4 g2 = *(const float4*)(p + 2 * I), u2 = *(const float4*)(p + 3 * I);
-          G.x += g2.x; G.y += g2.y; G.z += g2.z; G.w += g2.w;
-          U.x += u2.x; U.y += u2.y; U.z += u2.z; U.w += u2.w;
-        }
-        float4 r;
-        r.x = G.x / (1.f + __expf(-G.x)) * U.x;
-        r.y = G.y / (1.f + __expf(-G.y)) * U.y;
-        r.z = G.z / (1.f + __expf(-G.z)) * U.z;
-        r.w = G.w / (1.f + __expf(-G.w)) * U.w;
-        *(float4*)&sh->scratch[4 * i4] = r;
+      int gi = g;                      // this lane's group in the staging buffer
+#ifdef VQ2_DEC_PROBE
+      if (threadIdx.x == 0 && c > 0) g_cprobe[blockIdx.x][44] = clock64();
+#endif
+      if (all_at_once) gi += (u - ub) * ng;
+      else stage_units(u - ub, 1);
+      load_xs(sh, gi, gv, xr[0]);
+      wsc = sh->unit_w[u] * (gv ? sh->ginv[gi] : 0.f);
+#ifdef VQ2_DEC_PROBE
+      if (c > 0) {
+        uint32_t t = 0;
+        for (int i = 0; i < 32; ++i) t ^= xr[0][i];
+        if (t == 0x12345u) sh->red[0] = wsc;
+        if (threadIdx.x == 0) g_cprobe[blockIdx.x][45] = clock64();
       }
-      consumer_sync();
-      const float* scr = sh->scratch;
-      stage_activation([&](int i) { return scr[i]; }, ng, sh, 1);
-      load_xs(sh, g, gv, xr[0]);
-      wsc = a.topk_w[m] * (gv ? sh->ginv[g] : 0.f);
+#endif
       if (threadIdx.x == 0 && c == 0) PROBE(1, 5);
     }
+#ifdef VQ2_DEC_PROBE
+    if (threadIdx.x == 0 && c < 12) g_cprobe[blockIdx.x][24 + 2 * c] = clock64();
+#endif
     if (!mbar_wait(&sh->full[slot], (c / DEC_STAGES) & 1)) break;
+#ifdef VQ2_DEC_PROBE
+    if (threadIdx.x == 0 && c < 12) g_cprobe[blockIdx.x][25 + 2 * c] = clock64();
+#endif
     if (threadIdx.x == 0 && c == 0) PROBE(1, 3);
     const uint8_t* st = d.stages + slot * stage_b;
     if (S / rstep >= 8) {
@@ -665,6 +700,9 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&sh->empty[slot]);
+#ifdef VQ2_DEC_PROBE
+    if (threadIdx.x == 0 && c < 12) { g_cprobe[blockIdx.x][2 * c] = clock64(); g_cprobe[blockIdx.x][2 * c + 1] = (u << 16) | n; }
+#endif
     ++c;
   }
   if (threadIdx.x == 0) PROBE(1, 4);
@@ -687,6 +725,9 @@ static DecodeLaunchCache g_dec_cache[64];
 using namespace vq2;
 
 #ifdef VQ2_DEC_PROBE
+extern "C" int vq2_cprobe_read(void* host) {
+  return (int)cudaMemcpyFromSymbol(host, g_cprobe, sizeof(g_cprobe));
+}
 extern "C" int vq2_bprobe_read(void* host) {
   return (int)cudaMemcpyFromSymbol(host, g_bprobe, sizeof(g_bprobe));
 }
