@@ -81,19 +81,11 @@ __device__ __forceinline__ unsigned long long gtime() {
   return t;
 }
 // slot 15: globaltimer anchor, slot 14: clock64 at the anchor; other slots: clock64
-__device__ unsigned long long g_sprobe[1024][2][8];
-__device__ unsigned long long g_bprobe[2][1024][8];
-__device__ unsigned long long g_cprobe[1024][48];
-#define BP(i) do { if (threadIdx.x == 0) g_bprobe[pk][blockIdx.x][i] = clock64(); } while (0)
-#define SP(i) do { if (pk == 2 && (threadIdx.x & 31) == 0 && (threadIdx.x >> 5) % 15 == 0) \
-    g_sprobe[blockIdx.x][(threadIdx.x >> 5) / 15][i] = clock64(); } while (0)
 #define PROBE(k, i) do { \
     if ((i) == 0) { g_probe[k][blockIdx.x][14] = clock64(); g_probe[k][blockIdx.x][15] = gtime(); } \
     g_probe[k][blockIdx.x][i] = clock64(); } while (0)
 #else
 #define PROBE(k, i) do {} while (0)
-#define SP(i) do {} while (0)
-#define BP(i) do {} while (0)
 #endif
 
 // ------------------------------------------------------------------ plan: group pairs by expert
@@ -103,10 +95,9 @@ __device__ unsigned long long g_cprobe[1024][48];
 // it reads the keys four at a time as shared-memory broadcasts).
 static_assert(DEC_TT == 1, "one pair per unit");
 __device__ void build_plan(const void* ids, int ids_dtype, const float* topk_w, int M, int E, int expert_base,
-                           DecodeShared* sh, int pk = 0) {
+                           DecodeShared* sh) {
   const int tid = threadIdx.x;
   static_assert(DEC_THREADS >= VQ2_DECODE_MAX_PAIRS, "build_plan holds one pair per thread");
-  BP(0);
   const int M4 = (M + 3) & ~3;
   int valid = 0;
   float w = 0.f;
@@ -120,7 +111,6 @@ __device__ void build_plan(const void* ids, int ids_dtype, const float* topk_w, 
     sh->ekey[tid] = key;
   }
   const int nunits = __syncthreads_count(valid);
-  BP(1);
   if (tid < M && sh->ekey[tid] != 0x7FFFFFFF) {
     const int m = tid, e = sh->ekey[m];
     int rank = 0;
@@ -135,7 +125,6 @@ __device__ void build_plan(const void* ids, int ids_dtype, const float* topk_w, 
   }
   if (tid == 0) sh->nunits = nunits;
   __syncthreads();
-  BP(2);
 }
 
 // ------------------------------------------------------------------ chunk iteration
@@ -252,12 +241,12 @@ __device__ __forceinline__ void multi_dot(const uint4* lo, const uint32_t* hw, c
     }
 }
 
-// Sum V (= 2, 4 or 8) per-lane values over the warp with V + 1 shuffles instead of 5V: each
+// Sum V (= 1, 2, 4 or 8) per-lane values over the warp with V + 1 shuffles instead of 5V: each
 // halving step keeps half of the values per lane. Afterwards every lane holds the total of value
 // reduce_index<V>(lane).
 template <int V>
 __device__ __forceinline__ int reduce_index(int lane) {
-  return V == 8 ? (lane >> 2) & 7 : V == 4 ? (lane >> 3) & 3 : (lane >> 4) & 1;
+  return V == 8 ? (lane >> 2) & 7 : V == 4 ? (lane >> 3) & 3 : V == 2 ? (lane >> 4) & 1 : 0;
 }
 template <int V>
 __device__ __forceinline__ float warp_reduce_multi(float* v) {
@@ -292,12 +281,10 @@ __device__ __forceinline__ float warp_reduce_multi(float* v) {
 // stores it as half2 in sh->xs[g]; sh->ginv[g] gets the factor undoing the scale and the
 // Hadamard's 1/8. Called by all consumer threads.
 template <typename LoadF>
-__device__ __forceinline__ void stage_activation(LoadF ld, int ng, DecodeShared* sh, int pk = 0) {
+__device__ __forceinline__ void stage_activation(LoadF ld, int ng, DecodeShared* sh) {
   constexpr int GPW = (DEC_MAXG + DEC_NW - 1) / DEC_NW;   // groups per warp
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  SP(0);
   consumer_sync();                         // the previous unit's xs / ginv are no longer read
-  SP(1);
   float va[GPW], vb[GPW];
 #pragma unroll
   for (int i = 0; i < GPW; ++i) {   // all loads first, so their latencies overlap
@@ -305,7 +292,6 @@ __device__ __forceinline__ void stage_activation(LoadF ld, int ng, DecodeShared*
     va[i] = vb[i] = 0.f;
     if (g < ng) { va[i] = ld(g * 64 + lane); vb[i] = ld(g * 64 + 32 + lane); }
   }
-  SP(2);
   const float climit = 1024.f / sh->cmax;
 #pragma unroll
   for (int i = 0; i < GPW; ++i) {
@@ -341,9 +327,7 @@ __device__ __forceinline__ void stage_activation(LoadF ld, int ng, DecodeShared*
       if (lane == 0) sh->ginv[g] = inv * 0.125f;
     }
   }
-  SP(5);
   consumer_sync();
-  SP(6);
 }
 
 // A consumer lane's copy of its group's staged activation (zeros past the row's groups).
@@ -370,7 +354,7 @@ __device__ __forceinline__ DecSmem dec_smem(uint8_t* smem) {
 }
 
 // Barrier init, codebook bulk copy, expert plan (all threads; ends with __syncthreads).
-__device__ __forceinline__ void dec_prologue(const vq2_moe_args& a, const uint16_t* cb, DecSmem d, int pk) {
+__device__ __forceinline__ void dec_prologue(const vq2_moe_args& a, const uint16_t* cb, DecSmem d) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < DEC_STAGES; ++s) { mbar_init(&d.sh->full[s], 1); mbar_init(&d.sh->empty[s], DEC_NW); }
     mbar_init(&d.sh->cbbar, 1);
@@ -379,7 +363,7 @@ __device__ __forceinline__ void dec_prologue(const vq2_moe_args& a, const uint16
     mbar_arrive_expect_tx(&d.sh->cbbar, 1024 * 4 * 2);
     bulk_g2s(d.sh->scratch, cb, 1024 * 4 * 2, &d.sh->cbbar);
   }
-  build_plan(a.topk_ids, a.ids_dtype, a.topk_w, a.N * a.topk, a.E, a.expert_base, d.sh, pk);
+  build_plan(a.topk_ids, a.ids_dtype, a.topk_w, a.N * a.topk, a.E, a.expert_base, d.sh);
 }
 
 // One pass of a consumer warp over RB gate/up row pairs of a stage (rows rr0 + k*rstep):
@@ -474,7 +458,7 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
       asm volatile("prefetch.global.L2 [%0];" ::"l"((const char*)a.x + o));
   }
 
-  dec_prologue(a, a.w13_cb, d, 0);
+  dec_prologue(a, a.w13_cb, d);
   const long total = (long)sh->nunits * I;
 
   if (warp == DEC_NW) {   // ---------------- producer
@@ -538,14 +522,6 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
         load_xs(sh, g, gv, xr[0]);
         inv = gv ? sh->ginv[g] : 0.f;
         if (threadIdx.x == 0 && c == 0) PROBE(0, 5);
-#ifdef VQ2_DEC_PROBE2
-        if (c == 0) {
-          stage_activation([&](int i) { return load_act(xp, xdt, xrow + i); }, ng, sh, 2);
-          load_xs(sh, g, gv, xr[0]);
-          { const int pk = 2; SP(7); }
-          if (threadIdx.x == 0) PROBE(0, 10);
-        }
-#endif
       }
     }
     if (!mbar_wait(&sh->full[slot], (c / DEC_STAGES) & 1)) break;
@@ -583,7 +559,7 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
   const uint32_t stage_b = lo_b + hi_b + sc_b;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
-  dec_prologue(a, a.w2_cb, d, 1);
+  dec_prologue(a, a.w2_cb, d);
   const long total = (long)sh->nunits * H;
 
   if (warp == DEC_NW) {   // ---------------- producer: weights do not depend on the gate/up grid
@@ -651,7 +627,7 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
     }
     consumer_sync();
     const float* scr = sh->scratch;
-    stage_activation([&](int i) { return scr[i]; }, cnt * ng, sh, 1);
+    stage_activation([&](int i) { return scr[i]; }, cnt * ng, sh);
   };
   if (all_at_once && nu > 0) stage_units(0, nu);
   int u, h0, n, c = 0;
@@ -662,30 +638,13 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
       const int m = sh->unit_m[u][0];
       tok = m / a.topk;
       int gi = g;                      // this lane's group in the staging buffer
-#ifdef VQ2_DEC_PROBE
-      if (threadIdx.x == 0 && c > 0) g_cprobe[blockIdx.x][44] = clock64();
-#endif
       if (all_at_once) gi += (u - ub) * ng;
       else stage_units(u - ub, 1);
       load_xs(sh, gi, gv, xr[0]);
       wsc = sh->unit_w[u] * (gv ? sh->ginv[gi] : 0.f);
-#ifdef VQ2_DEC_PROBE
-      if (c > 0) {
-        uint32_t t = 0;
-        for (int i = 0; i < 32; ++i) t ^= xr[0][i];
-        if (t == 0x12345u) sh->red[0] = wsc;
-        if (threadIdx.x == 0) g_cprobe[blockIdx.x][45] = clock64();
-      }
-#endif
       if (threadIdx.x == 0 && c == 0) PROBE(1, 5);
     }
-#ifdef VQ2_DEC_PROBE
-    if (threadIdx.x == 0 && c < 12) g_cprobe[blockIdx.x][24 + 2 * c] = clock64();
-#endif
     if (!mbar_wait(&sh->full[slot], (c / DEC_STAGES) & 1)) break;
-#ifdef VQ2_DEC_PROBE
-    if (threadIdx.x == 0 && c < 12) g_cprobe[blockIdx.x][25 + 2 * c] = clock64();
-#endif
     if (threadIdx.x == 0 && c == 0) PROBE(1, 3);
     const uint8_t* st = d.stages + slot * stage_b;
     if (S / rstep >= 8) {
@@ -695,14 +654,15 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
       for (int rr0 = rsub; rr0 < n; rr0 += 4 * rstep)
         down_rows<4>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, tok, H, h0, a.out);
     } else {
-      for (int rr0 = rsub; rr0 < n; rr0 += 2 * rstep)
-        down_rows<2>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, tok, H, h0, a.out);
+      for (int rr0 = rsub; rr0 < n; rr0 += 2 * rstep) {
+        if (rr0 + rstep < n)     // both rows of the pass exist
+          down_rows<2>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, tok, H, h0, a.out);
+        else                     // ragged end of a chunk: one row
+          down_rows<1>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, tok, H, h0, a.out);
+      }
     }
     __syncwarp();
     if (lane == 0) mbar_arrive(&sh->empty[slot]);
-#ifdef VQ2_DEC_PROBE
-    if (threadIdx.x == 0 && c < 12) { g_cprobe[blockIdx.x][2 * c] = clock64(); g_cprobe[blockIdx.x][2 * c + 1] = (u << 16) | n; }
-#endif
     ++c;
   }
   if (threadIdx.x == 0) PROBE(1, 4);
@@ -725,15 +685,6 @@ static DecodeLaunchCache g_dec_cache[64];
 using namespace vq2;
 
 #ifdef VQ2_DEC_PROBE
-extern "C" int vq2_cprobe_read(void* host) {
-  return (int)cudaMemcpyFromSymbol(host, g_cprobe, sizeof(g_cprobe));
-}
-extern "C" int vq2_bprobe_read(void* host) {
-  return (int)cudaMemcpyFromSymbol(host, g_bprobe, sizeof(g_bprobe));
-}
-extern "C" int vq2_sprobe_read(void* host) {
-  return (int)cudaMemcpyFromSymbol(host, g_sprobe, sizeof(g_sprobe));
-}
 extern "C" int vq2_probe_read(void* host) {
   return (int)cudaMemcpyFromSymbol(host, g_probe, sizeof(g_probe));
 }
