@@ -280,18 +280,25 @@ __device__ __forceinline__ float warp_reduce_multi(float* v) {
 // max|x| * max|C| * 32 <= 2^15 (no half2 partial of the group's dot products can overflow), and
 // stores it as half2 in sh->xs[g]; sh->ginv[g] gets the factor undoing the scale and the
 // Hadamard's 1/8. Called by all consumer threads.
+constexpr int STAGE_GPW = (DEC_MAXG + DEC_NW - 1) / DEC_NW;   // groups per consumer warp
+
+// Load half of the staging: this lane's elements (lane, lane + 32) of the warp's groups.
 template <typename LoadF>
-__device__ __forceinline__ void stage_activation(LoadF ld, int ng, DecodeShared* sh) {
-  constexpr int GPW = (DEC_MAXG + DEC_NW - 1) / DEC_NW;   // groups per warp
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-  consumer_sync();                         // the previous unit's xs / ginv are no longer read
-  float va[GPW], vb[GPW];
+__device__ __forceinline__ void stage_load(LoadF ld, int ng, float* va, float* vb) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 #pragma unroll
-  for (int i = 0; i < GPW; ++i) {   // all loads first, so their latencies overlap
+  for (int i = 0; i < STAGE_GPW; ++i) {   // all loads first, so their latencies overlap
     const int g = warp + i * DEC_NW;
     va[i] = vb[i] = 0.f;
     if (g < ng) { va[i] = ld(g * 64 + lane); vb[i] = ld(g * 64 + 32 + lane); }
   }
+}
+
+// Rotate-and-store half of the staging (needs sh->cmax; the caller has synchronised the consumers
+// since xs / ginv were last read).
+__device__ __forceinline__ void stage_rotate(int ng, DecodeShared* sh, const float* va, const float* vb) {
+  constexpr int GPW = STAGE_GPW;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const float climit = 1024.f / sh->cmax;
 #pragma unroll
   for (int i = 0; i < GPW; ++i) {
@@ -328,6 +335,14 @@ __device__ __forceinline__ void stage_activation(LoadF ld, int ng, DecodeShared*
     }
   }
   consumer_sync();
+}
+
+template <typename LoadF>
+__device__ __forceinline__ void stage_activation(LoadF ld, int ng, DecodeShared* sh) {
+  float va[STAGE_GPW], vb[STAGE_GPW];
+  consumer_sync();                         // the previous unit's xs / ginv are no longer read
+  stage_load(ld, ng, va, vb);
+  stage_rotate(ng, sh, va, vb);
 }
 
 // A consumer lane's copy of its group's staged activation (zeros past the row's groups).
@@ -435,70 +450,97 @@ __device__ __forceinline__ void down_rows(const uint8_t* st, int rr0, int rstep,
   if ((lane & (32 / R - 1)) == 0 && rr < n) atomicAdd(&out[(size_t)tok * H + h0 + rr], tot);
 }
 
-// ------------------------------------------------------------------ kernel A: gate/up partials
-// KH = K-slices of the H-wide input (H/64 groups, 32 per warp).
-template <int KH>
-__global__ void __launch_bounds__(DEC_THREADS, 1)
-decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const DecSmem d = dec_smem(smem);
+// ------------------------------------------------------------------ phases
+// Every kernel's ring slot is DEC_STAGE_BYTES: gate/up stages DEC_SA row pairs of an H-wide
+// expert (H <= 4096), down stages down_rows_per_stage(KH) rows of an I-wide one (I <= 4096).
+constexpr uint32_t DEC_ROW_BYTES_4K = 4096 / 4 + 4096 / 16 + 4096 / 32;   // lo + hi + scales, 4096 wide
+constexpr uint32_t DEC_STAGE_BYTES = DEC_SA * 2 * DEC_ROW_BYTES_4K;
+__host__ __device__ constexpr int down_rows_per_stage(int KH) { return DEC_SB / KH; }
+static_assert(DEC_SB * DEC_ROW_BYTES_4K / 2 <= DEC_STAGE_BYTES, "down stage (I <= 4096) exceeds the slot");
+
+// Producer (one lane): gate/up row chunks of this CTA's range into the ring, chunk counter c.
+__device__ __forceinline__ void gateup_produce(const vq2_moe_args& a, const DecSmem& d, uint64_t pol, int& c) {
   DecodeShared* sh = d.sh;
-  if (threadIdx.x == 0) PROBE(0, 0);
-  pdl_launch_dependents();
-  const int H = a.H, I = a.I;
-  const int nsub = H / 4, ng = H / 64;
+  const int H = a.H, I = a.I, nsub = H / 4, ng = H / 64;
   constexpr int S = DEC_SA;
   const uint32_t lo_b = S * nsub, hi_b = S * (nsub / 4), sc_b = S * ng * 2;
-  const uint32_t stage_b = 2 * (lo_b + hi_b + sc_b);
+  ChunkIter it((long)sh->nunits * I, I, S);
+  int u, i0, n;
+  while (it.next(u, i0, n)) {
+    const int slot = c % DEC_STAGES;
+    if (c >= DEC_STAGES && !mbar_wait(&sh->empty[slot], ((c / DEC_STAGES) - 1) & 1)) { sh->abort = 1; return; }
+    const long e = sh->unit_e[u];
+    const long rg = e * 2 * I + i0, ru = rg + I;
+    uint8_t* st = d.stages + slot * DEC_STAGE_BYTES;
+    mbar_arrive_expect_tx(&sh->full[slot], 2u * n * (nsub + nsub / 4 + ng * 2));
+    bulk_g2s_stream(st, a.w13_lo + rg * nsub, n * nsub, &sh->full[slot], pol);
+    bulk_g2s_stream(st + lo_b, a.w13_lo + ru * nsub, n * nsub, &sh->full[slot], pol);
+    bulk_g2s_stream(st + 2 * lo_b, a.w13_hi + rg * (nsub / 4), n * (nsub / 4), &sh->full[slot], pol);
+    bulk_g2s_stream(st + 2 * lo_b + hi_b, a.w13_hi + ru * (nsub / 4), n * (nsub / 4), &sh->full[slot], pol);
+    bulk_g2s_stream(st + 2 * (lo_b + hi_b), a.w13_sc + rg * ng, n * ng * 2, &sh->full[slot], pol);
+    bulk_g2s_stream(st + 2 * (lo_b + hi_b) + sc_b, a.w13_sc + ru * ng, n * ng * 2, &sh->full[slot], pol);
+    ++c;
+  }
+}
+
+// Producer (one lane): down row chunks. The weights do not depend on the gate/up results.
+template <int KH>
+__device__ __forceinline__ void down_produce(const vq2_moe_args& a, const DecSmem& d, uint64_t pol, int& c) {
+  DecodeShared* sh = d.sh;
+  const int H = a.H, I = a.I, nsub = I / 4, ng = I / 64;
+  constexpr int S = down_rows_per_stage(KH);
+  const uint32_t lo_b = S * nsub, hi_b = S * (nsub / 4);
+  ChunkIter it((long)sh->nunits * H, H, S);
+  int u, h0, n;
+  while (it.next(u, h0, n)) {
+    const int slot = c % DEC_STAGES;
+    if (c >= DEC_STAGES && !mbar_wait(&sh->empty[slot], ((c / DEC_STAGES) - 1) & 1)) { sh->abort = 1; return; }
+    const long r = (long)sh->unit_e[u] * H + h0;
+    uint8_t* st = d.stages + slot * DEC_STAGE_BYTES;
+    mbar_arrive_expect_tx(&sh->full[slot], (uint32_t)n * (nsub + nsub / 4 + ng * 2));
+    bulk_g2s_stream(st, a.w2_lo + r * nsub, n * nsub, &sh->full[slot], pol);
+    bulk_g2s_stream(st + lo_b, a.w2_hi + r * (nsub / 4), n * (nsub / 4), &sh->full[slot], pol);
+    bulk_g2s_stream(st + lo_b + hi_b, a.w2_sc + r * ng, n * ng * 2, &sh->full[slot], pol);
+    ++c;
+  }
+}
+
+// Producer: every issued copy must land before the CTA exits.
+__device__ __forceinline__ void produce_drain(const DecSmem& d, int c) {
+  for (int q = max(0, c - DEC_STAGES); q < c; ++q) mbar_wait(&d.sh->full[q % DEC_STAGES], (q / DEC_STAGES) & 1);
+}
+
+// Consumers, before the gate/up phase: load the first unit's activation (its latency overlaps the
+// codebook fill that follows), zero the output rows the down phase accumulates into.
+struct GateupPre {
+  float va[STAGE_GPW], vb[STAGE_GPW];
+  int m = -1;
+};
+__device__ __forceinline__ void gateup_pre(const vq2_moe_args& a, const DecSmem& d, GateupPre& pre) {
+  DecodeShared* sh = d.sh;
+  const ChunkIter it0((long)sh->nunits * a.I, a.I, DEC_SA);
+  if (it0.left > 0) {
+    pre.m = sh->unit_m[it0.u][0];
+    const size_t xrow = (size_t)(pre.m / a.topk) * a.H;
+    const void* xp = a.x;
+    const int xdt = a.x_dtype;
+    stage_load([&](int i) { return load_act(xp, xdt, xrow + i); }, a.H / 64, pre.va, pre.vb);
+  }
+  const long tot = (long)a.N * a.H;
+  for (long i = (long)blockIdx.x * DEC_NW * 32 + threadIdx.x; i < tot; i += (long)gridDim.x * DEC_NW * 32)
+    a.out[i] = 0.f;
+}
+
+// Consumers: gate/up K-slice partials of this CTA's rows into `part`. KH = K-slices of the
+// H-wide input (H/64 groups, 32 per warp). Needs the gate/up codebook in d.cbs.
+template <int KH>
+__device__ __forceinline__ void gateup_consume(const vq2_moe_args& a, const DecSmem& d, float* __restrict__ part,
+                                               const GateupPre& pre, int& c) {
+  DecodeShared* sh = d.sh;
+  const int H = a.H, I = a.I, nsub = H / 4, ng = H / 64;
+  constexpr int S = DEC_SA;
+  const uint32_t lo_b = S * nsub, hi_b = S * (nsub / 4), sc_b = S * ng * 2;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  {  // warm the path to the activations (first 64 KB) while the plan is built
-    const size_t xbytes = (size_t)a.N * H * (a.x_dtype == VQ2_DT_F32 ? 4 : 2);
-    const size_t lim = xbytes < 65536 ? xbytes : 65536;
-    for (size_t o = (size_t)threadIdx.x * 128; o < lim; o += DEC_THREADS * 128)
-      asm volatile("prefetch.global.L2 [%0];" ::"l"((const char*)a.x + o));
-  }
-
-  dec_prologue(a, a.w13_cb, d);
-  const long total = (long)sh->nunits * I;
-
-  if (warp == DEC_NW) {   // ---------------- producer
-    if (lane == 0) {
-      const uint64_t pol = l2_evict_first();
-      ChunkIter it(total, I, S);
-      int u, i0, n, c = 0;
-      while (it.next(u, i0, n)) {
-        const int slot = c % DEC_STAGES;
-        if (c >= DEC_STAGES && !mbar_wait(&sh->empty[slot], ((c / DEC_STAGES) - 1) & 1)) { sh->abort = 1; break; }
-        const long e = sh->unit_e[u];
-        const long rg = e * 2 * I + i0, ru = rg + I;
-        uint8_t* st = d.stages + slot * stage_b;
-        mbar_arrive_expect_tx(&sh->full[slot], 2u * n * (nsub + nsub / 4 + ng * 2));
-        bulk_g2s_stream(st, a.w13_lo + rg * nsub, n * nsub, &sh->full[slot], pol);
-        bulk_g2s_stream(st + lo_b, a.w13_lo + ru * nsub, n * nsub, &sh->full[slot], pol);
-        bulk_g2s_stream(st + 2 * lo_b, a.w13_hi + rg * (nsub / 4), n * (nsub / 4), &sh->full[slot], pol);
-        bulk_g2s_stream(st + 2 * lo_b + hi_b, a.w13_hi + ru * (nsub / 4), n * (nsub / 4), &sh->full[slot], pol);
-        bulk_g2s_stream(st + 2 * (lo_b + hi_b), a.w13_sc + rg * ng, n * ng * 2, &sh->full[slot], pol);
-        bulk_g2s_stream(st + 2 * (lo_b + hi_b) + sc_b, a.w13_sc + ru * ng, n * ng * 2, &sh->full[slot], pol);
-#ifdef VQ2_DEC_PROBE
-        if (c == 0) { PROBE(0, 8); mbar_wait(&sh->full[0], 0); PROBE(0, 9); }
-#endif
-        ++c;
-      }
-      // drain: every issued copy must land before the CTA exits
-      for (int q = max(0, c - DEC_STAGES); q < c; ++q) mbar_wait(&sh->full[q % DEC_STAGES], (q / DEC_STAGES) & 1);
-    }
-    return;
-  }
-
-  // ---------------- consumers
-  {  // zero the output (the down kernel accumulates into it after its grid-dependency wait)
-    const long tot = (long)a.N * a.H;
-    for (long i = (long)blockIdx.x * DEC_NW * 32 + threadIdx.x; i < tot; i += (long)gridDim.x * DEC_NW * 32)
-      a.out[i] = 0.f;
-  }
-  if (threadIdx.x == 0) PROBE(0, 1);
-  fill_codebook(d.cbs, sh);
-  if (threadIdx.x == 0) PROBE(0, 2);
   const int h = warp % KH, rsub = warp / KH, rstep = DEC_NW / KH;
   const int g = h * 32 + lane;
   const bool gv = g < ng;
@@ -506,27 +548,31 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
   uint32_t xr[1][32];
   float inv = 0.f;
   int mcur = -1, ucur = -1;
-  ChunkIter it(total, I, S);
-  int u, i0, n, c = 0;
+  ChunkIter it((long)sh->nunits * I, I, S);
+  int u, i0, n;
   while (it.next(u, i0, n)) {
     const int slot = c % DEC_STAGES;
     if (u != ucur) {   // uniform across consumer warps: all walk the same chunk list
       ucur = u;
       const int mprev = mcur;
       mcur = sh->unit_m[u][0];
-      if (mprev < 0 || mprev / a.topk != mcur / a.topk) {   // same token: xs is still valid
+      if (mprev < 0 && mcur == pre.m) {       // first unit: loaded before the codebook fill
+        stage_rotate(ng, sh, pre.va, pre.vb);
+        load_xs(sh, g, gv, xr[0]);
+        inv = gv ? sh->ginv[g] : 0.f;
+      } else if (mprev < 0 || mprev / a.topk != mcur / a.topk) {   // same token: xs is still valid
         const size_t xrow = (size_t)(mcur / a.topk) * H;
         const void* xp = a.x;
         const int xdt = a.x_dtype;
         stage_activation([&](int i) { return load_act(xp, xdt, xrow + i); }, ng, sh);
         load_xs(sh, g, gv, xr[0]);
         inv = gv ? sh->ginv[g] : 0.f;
-        if (threadIdx.x == 0 && c == 0) PROBE(0, 5);
       }
+      if (threadIdx.x == 0 && c == 0) PROBE(0, 5);
     }
-    if (!mbar_wait(&sh->full[slot], (c / DEC_STAGES) & 1)) break;
+    if (!mbar_wait(&sh->full[slot], (c / DEC_STAGES) & 1)) { ++c; break; }
     if (threadIdx.x == 0 && c == 0) PROBE(0, 3);
-    const uint8_t* st = d.stages + slot * stage_b;
+    const uint8_t* st = d.stages + slot * DEC_STAGE_BYTES;
     if (S / rstep >= 4) {
       for (int rr0 = rsub; rr0 < n; rr0 += 4 * rstep)
         gateup_rows<4>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, sc_b, cbl, xr, inv, mcur, KH, h, I, i0, part);
@@ -541,57 +587,19 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
     if (lane == 0) mbar_arrive(&sh->empty[slot]);
     ++c;
   }
-  if (threadIdx.x == 0) PROBE(0, 4);
 }
 
-// ------------------------------------------------------------------ kernel B: down + combine
-// KH = K-slices of the I-wide input; khA = K-slices the gate/up kernel used (partials to sum).
+// Consumers: down rows of this CTA's range, combined into a.out with fp32 atomics. KH = K-slices
+// of the I-wide input; khA = K-slices of the gate/up partials to sum. Needs the down codebook in
+// d.cbs and every CTA's gate/up partials visible.
 template <int KH>
-__global__ void __launch_bounds__(DEC_THREADS, 1)
-decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
-  extern __shared__ __align__(128) uint8_t smem[];
-  const DecSmem d = dec_smem(smem);
+__device__ __forceinline__ void down_consume(const vq2_moe_args& a, const DecSmem& d, const float* __restrict__ part,
+                                             int khA, int& c) {
   DecodeShared* sh = d.sh;
-  const int H = a.H, I = a.I;
-  const int nsub = I / 4, ng = I / 64;
-  constexpr int S = DEC_SB;
-  const uint32_t lo_b = S * nsub, hi_b = S * (nsub / 4), sc_b = S * ng * 2;
-  const uint32_t stage_b = lo_b + hi_b + sc_b;
+  const int H = a.H, I = a.I, nsub = I / 4, ng = I / 64;
+  constexpr int S = down_rows_per_stage(KH);
+  const uint32_t lo_b = S * nsub, hi_b = S * (nsub / 4);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  dec_prologue(a, a.w2_cb, d);
-  const long total = (long)sh->nunits * H;
-
-  if (warp == DEC_NW) {   // ---------------- producer: weights do not depend on the gate/up grid
-    if (lane == 0) {
-      const uint64_t pol = l2_evict_first();
-      ChunkIter it(total, H, S);
-      int u, h0, n, c = 0;
-      while (it.next(u, h0, n)) {
-        const int slot = c % DEC_STAGES;
-        if (c >= DEC_STAGES && !mbar_wait(&sh->empty[slot], ((c / DEC_STAGES) - 1) & 1)) { sh->abort = 1; break; }
-        const long r = (long)sh->unit_e[u] * H + h0;
-        if (c == 0) PROBE(1, 8);
-        uint8_t* st = d.stages + slot * stage_b;
-        mbar_arrive_expect_tx(&sh->full[slot], (uint32_t)n * (nsub + nsub / 4 + ng * 2));
-        bulk_g2s_stream(st, a.w2_lo + r * nsub, n * nsub, &sh->full[slot], pol);
-        bulk_g2s_stream(st + lo_b, a.w2_hi + r * (nsub / 4), n * (nsub / 4), &sh->full[slot], pol);
-        bulk_g2s_stream(st + lo_b + hi_b, a.w2_sc + r * ng, n * ng * 2, &sh->full[slot], pol);
-#ifdef VQ2_DEC_PROBE
-        if (c == 0) { mbar_wait(&sh->full[0], 0); PROBE(1, 9); }
-#endif
-        ++c;
-      }
-      for (int q = max(0, c - DEC_STAGES); q < c; ++q) mbar_wait(&sh->full[q % DEC_STAGES], (q / DEC_STAGES) & 1);
-    }
-    return;
-  }
-
-  if (threadIdx.x == 0) PROBE(1, 0);
-  fill_codebook(d.cbs, sh);
-  if (threadIdx.x == 0) PROBE(1, 1);
-  pdl_wait();   // the gate/up partials and the zeroed output come from the previous grid
-  if (threadIdx.x == 0) PROBE(1, 2);
   const int h = warp % KH, rsub = warp / KH, rstep = DEC_NW / KH;
   const int g = h * 32 + lane;
   const bool gv = g < ng;
@@ -599,7 +607,7 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
   uint32_t xr[1][32];
   float wsc = 0.f;
   int tok = -1, ucur = -1;
-  ChunkIter it(total, H, S);
+  ChunkIter it((long)sh->nunits * H, H, S);
   // Units of this CTA's row range: when all of their activations fit the staging buffer they are
   // staged together before the loop (a range that crosses a unit boundary then pays one staging).
   const int ub = it.u, nu = it.left > 0 ? (it.row0 + it.left - 1) / H + 1 : 0;
@@ -612,9 +620,10 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
       const int k = i4 / q4, j4 = i4 - k * q4;
       const int m = sh->unit_m[ub + k0 + k][0];
       const float* p = part + (size_t)m * khA * 2 * I + 4 * j4;
-      float4 G = *(const float4*)p, U = *(const float4*)(p + I);
+      // L2 loads (__ldcg): the partials were written by other SMs in the previous grid
+      float4 G = __ldcg((const float4*)p), U = __ldcg((const float4*)(p + I));
       if (khA > 1) {
-        const float4 g2 = *(const float4*)(p + 2 * I), u2 = *(const float4*)(p + 3 * I);
+        const float4 g2 = __ldcg((const float4*)(p + 2 * I)), u2 = __ldcg((const float4*)(p + 3 * I));
         G.x += g2.x; G.y += g2.y; G.z += g2.z; G.w += g2.w;
         U.x += u2.x; U.y += u2.y; U.z += u2.z; U.w += u2.w;
       }
@@ -630,7 +639,7 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
     stage_activation([&](int i) { return scr[i]; }, cnt * ng, sh);
   };
   if (all_at_once && nu > 0) stage_units(0, nu);
-  int u, h0, n, c = 0;
+  int u, h0, n;
   while (it.next(u, h0, n)) {
     const int slot = c % DEC_STAGES;
     if (u != ucur) {
@@ -644,9 +653,9 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
       wsc = sh->unit_w[u] * (gv ? sh->ginv[gi] : 0.f);
       if (threadIdx.x == 0 && c == 0) PROBE(1, 5);
     }
-    if (!mbar_wait(&sh->full[slot], (c / DEC_STAGES) & 1)) break;
+    if (!mbar_wait(&sh->full[slot], (c / DEC_STAGES) & 1)) { ++c; break; }
     if (threadIdx.x == 0 && c == 0) PROBE(1, 3);
-    const uint8_t* st = d.stages + slot * stage_b;
+    const uint8_t* st = d.stages + slot * DEC_STAGE_BYTES;
     if (S / rstep >= 8) {
       for (int rr0 = rsub; rr0 < n; rr0 += 8 * rstep)
         down_rows<8>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, tok, H, h0, a.out);
@@ -665,6 +674,55 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
     if (lane == 0) mbar_arrive(&sh->empty[slot]);
     ++c;
   }
+}
+
+// ------------------------------------------------------------------ kernel A: gate/up partials
+template <int KH>
+__global__ void __launch_bounds__(DEC_THREADS, 1)
+decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const DecSmem d = dec_smem(smem);
+  if (threadIdx.x == 0) PROBE(0, 0);
+  pdl_launch_dependents();
+  dec_prologue(a, a.w13_cb, d);
+  int c = 0;
+  if (threadIdx.x >> 5 == DEC_NW) {   // producer warp
+    if ((threadIdx.x & 31) == 0) {
+      gateup_produce(a, d, l2_evict_first(), c);
+      produce_drain(d, c);
+    }
+    return;
+  }
+  GateupPre pre;
+  gateup_pre(a, d, pre);
+  if (threadIdx.x == 0) PROBE(0, 1);
+  fill_codebook(d.cbs, d.sh);      // ends with a consumer barrier
+  if (threadIdx.x == 0) PROBE(0, 2);
+  gateup_consume<KH>(a, d, part, pre, c);
+  if (threadIdx.x == 0) PROBE(0, 4);
+}
+
+// ------------------------------------------------------------------ kernel B: down + combine
+template <int KH>
+__global__ void __launch_bounds__(DEC_THREADS, 1)
+decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const DecSmem d = dec_smem(smem);
+  dec_prologue(a, a.w2_cb, d);
+  int c = 0;
+  if (threadIdx.x >> 5 == DEC_NW) {   // producer warp: the weights do not depend on the gate/up grid
+    if ((threadIdx.x & 31) == 0) {
+      down_produce<KH>(a, d, l2_evict_first(), c);
+      produce_drain(d, c);
+    }
+    return;
+  }
+  if (threadIdx.x == 0) PROBE(1, 0);
+  fill_codebook(d.cbs, d.sh);
+  if (threadIdx.x == 0) PROBE(1, 1);
+  pdl_wait();   // the gate/up partials and the zeroed output come from the previous grid
+  if (threadIdx.x == 0) PROBE(1, 2);
+  down_consume<KH>(a, d, part, khA, c);
   if (threadIdx.x == 0) PROBE(1, 4);
 }
 
@@ -714,40 +772,35 @@ extern "C" int vq2_decode(const vq2_moe_args* a, void* ws, size_t ws_bytes, void
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VQ2_ERR_NO_DEVICE;
   DecodeLaunchCache& lc = g_dec_cache[dev];
-  // smem sized for the largest supported rows (H, I <= 4096)
-  const size_t smA = decode_smem_bytes((size_t)DEC_SA * 2 * (4096 / 4 + 4096 / 16 + 4096 / 32));
-  const size_t smB = decode_smem_bytes((size_t)DEC_SB * (4096 / 4 + 4096 / 16 + 4096 / 32) / 2);
+  const size_t sm = decode_smem_bytes(DEC_STAGE_BYTES);   // every kernel: H, I <= 4096
   if (!lc.attr_set) {
     if (cudaDeviceGetAttribute(&lc.nsm, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return VQ2_ERR_CUDA;
     bool ok = true;
-    ok &= cudaFuncSetAttribute(decode_gateup_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smA) == cudaSuccess;
-    ok &= cudaFuncSetAttribute(decode_gateup_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smA) == cudaSuccess;
-    ok &= cudaFuncSetAttribute(decode_down_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smB) == cudaSuccess;
-    ok &= cudaFuncSetAttribute(decode_down_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smB) == cudaSuccess;
+    const void* kernels[] = {(const void*)decode_gateup_kernel<1>, (const void*)decode_gateup_kernel<2>,
+                             (const void*)decode_down_kernel<1>,   (const void*)decode_down_kernel<2>};
+    for (const void* k : kernels)
+      ok &= cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm) == cudaSuccess;
     if (!ok) return VQ2_ERR_CUDA;
     lc.attr_set = true;
   }
-  const int khA = khA_of(a->H), khB = (a->I / 64 + 31) / 32;
-  void (*ka)(vq2_moe_args, float*) = khA == 1 ? decode_gateup_kernel<1> : decode_gateup_kernel<2>;
-  void (*kb)(vq2_moe_args, const float*, int) = khB == 1 ? decode_down_kernel<1> : decode_down_kernel<2>;
-
+  const int khA = khA_of(a->H), khB = khA_of(a->I);
   vq2_moe_args args = *a;
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(lc.nsm);
   cfg.blockDim = dim3(DEC_THREADS);
-  cfg.dynamicSmemBytes = smA;
+  cfg.dynamicSmemBytes = sm;
   cfg.stream = (cudaStream_t)stream;
+  void (*ka)(vq2_moe_args, float*) = khA == 1 ? decode_gateup_kernel<1> : decode_gateup_kernel<2>;
+  void (*kb)(vq2_moe_args, const float*, int) = khB == 1 ? decode_down_kernel<1> : decode_down_kernel<2>;
   if (cudaLaunchKernelEx(&cfg, ka, args, part) != cudaSuccess) return VQ2_ERR_CUDA;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.dynamicSmemBytes = smB;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
   if (cudaLaunchKernelEx(&cfg, kb, args, (const float*)part, khA) != cudaSuccess) return VQ2_ERR_CUDA;
   return VQ2_OK;
 }
-
 static_assert(offsetof(vq2::DecodeShared, xs) % 16 == 0, "xs must be 16-byte aligned");
 static_assert(offsetof(vq2::DecodeShared, scratch) % 16 == 0, "bulk-copy destination must be 16-byte aligned");
 static_assert(offsetof(vq2::DecodeShared, ekey) % 16 == 0, "ekey is read as int4");

@@ -74,3 +74,26 @@ def test_max_pairs_and_expert_base(big_layer):
     assert torch_ref.rel_l2(out, ref) < TOL
     none = _moe()(x, ids * 0 + 255, tw, *synth.layer_args(sub), expert_base=64)
     assert torch.count_nonzero(none) == 0
+
+
+@pytest.mark.parametrize("H,I", [(1024, 4096), (4096, 4096), (2048, 1024)])
+def test_shapes_k_slices(H, I):
+    """One and two K-slices on either side (I = 4096 runs 16-row down stages)."""
+    from vq2_vllm import synth
+    L = synth.make_layer(16, H, I, seed=11, device="cuda")
+    x = synth.make_tokens(3, H, seed=12, device="cuda")
+    ids, tw = synth.route_softmax_topk(x, 16, 8, w_std=0.02, seed=13)
+    out = _moe()(x, ids, tw, *synth.layer_args(L))
+    assert torch_ref.rel_l2(out, torch_ref.moe_ref(x, ids, tw, L)) < TOL
+
+
+def test_many_calls_back_to_back(big_layer):
+    """Back-to-back calls on one stream (the chained kernel pair, queued ahead of the GPU)."""
+    from vq2_vllm import synth
+    x = synth.make_tokens(2, 4096, seed=21, device="cuda")
+    ids, tw = synth.route_softmax_topk(x, 256, 8, w_std=0.02, seed=22)
+    ref = torch_ref.moe_ref(x, ids, tw, big_layer)
+    outs = [_moe()(x, ids, tw, *synth.layer_args(big_layer)) for _ in range(50)]
+    torch.cuda.synchronize()
+    for o in outs[::7]:
+        assert torch_ref.rel_l2(o, ref) < TOL
