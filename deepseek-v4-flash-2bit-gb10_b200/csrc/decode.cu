@@ -191,11 +191,6 @@ __device__ __forceinline__ void fill_codebook(uint8_t* cbs, DecodeShared* sh) {
 // R independent 64-group dot products for NT tokens: for each row r, sum over the group's 16
 // sub-vectors of <codebook[id_s], x_s>, accumulated in two half2 chains, returned in fp32.
 // lo[r]: the 16 index low bytes; hw[r]: the 4 hi bytes; x[t]: 32 half2 regs of the rotated group.
-__device__ __forceinline__ uint2 lds64(uint32_t addr) {
-  uint2 v;
-  asm("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(addr));
-  return v;
-}
 
 template <int R, int NT>
 __device__ __forceinline__ void multi_dot(const uint4* lo, const uint32_t* hw, const uint8_t* cbl_ptr,

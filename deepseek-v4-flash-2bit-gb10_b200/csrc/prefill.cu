@@ -172,7 +172,7 @@ __device__ __forceinline__ uint32_t sw128_off(int r, int kc) {
 // f16: 4 sub-vectors -> 16 f16 values C[id] * sc. lo: the sub-vectors' low bytes (little-endian
 // in lo.x, lo.y); hw: their hi bits (2 per sub-vector from bit 0). cbl: this lane's codebook copy.
 template <int PREC>
-__device__ __forceinline__ void decode_b_quarter(const uint8_t* cbl, uint2 lo, uint32_t hw, float scf, uint8_t* tile,
+__device__ __forceinline__ void decode_b_quarter(uint32_t cbl, uint2 lo, uint32_t hw, float scf, uint32_t tile,
                                                  int r, int h) {
   if (PREC == VQ2_PREC_FP8) {
 #pragma unroll
@@ -183,13 +183,13 @@ __device__ __forceinline__ void decode_b_quarter(const uint8_t* cbl, uint2 lo, u
 #pragma unroll
       for (int j = 0; j < 4; ++j) {
         const uint32_t id = (j & 2) ? (ids[j & 1] >> 16) : (ids[j & 1] & 0xFFFFu);
-        const uint2 c = *(const uint2*)(cbl + (id << 6));
+        const uint2 c = lds64(cbl + (id << 6));
         const float2 a = __half22float2(*(const __half2*)&c.x), b = __half22float2(*(const __half2*)&c.y);
         const __nv_fp8x2_storage_t p0 = __nv_cvt_float2_to_fp8x2(make_float2(a.x * scf, a.y * scf), __NV_SATFINITE, __NV_E4M3);
         const __nv_fp8x2_storage_t p1 = __nv_cvt_float2_to_fp8x2(make_float2(b.x * scf, b.y * scf), __NV_SATFINITE, __NV_E4M3);
         packed[j] = (uint32_t)p0 | ((uint32_t)p1 << 16);
       }
-      *(uint4*)(tile + sw128_off(r, 2 * h + q)) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+      sts128_v(tile + sw128_off(r, 2 * h + q), make_uint4(packed[0], packed[1], packed[2], packed[3]));
     }
   } else {
     const __half2 s2 = __float2half2_rn(scf);
@@ -202,12 +202,12 @@ __device__ __forceinline__ void decode_b_quarter(const uint8_t* cbl, uint2 lo, u
       for (int jj = 0; jj < 2; ++jj) {
         const int j = 2 * q + jj;
         const uint32_t id = (j & 2) ? (ids[j & 1] >> 16) : (ids[j & 1] & 0xFFFFu);
-        const uint2 c = *(const uint2*)(cbl + (id << 6));
+        const uint2 c = lds64(cbl + (id << 6));
         const __half2 v0 = __hmul2(*(const __half2*)&c.x, s2), v1 = __hmul2(*(const __half2*)&c.y, s2);
         w[2 * jj] = *(const uint32_t*)&v0;
         w[2 * jj + 1] = *(const uint32_t*)&v1;
       }
-      *(uint4*)(tile + sw128_off(r, 2 * h + q)) = make_uint4(w[0], w[1], w[2], w[3]);
+      sts128_v(tile + sw128_off(r, 2 * h + q), make_uint4(w[0], w[1], w[2], w[3]));
     }
   }
 }
@@ -261,11 +261,13 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
   if (!a.val[(size_t)b0 * PF_BM]) return;            // blocks past the last expert hold no pair
   const bool v1 = b0 + 1 < nblk && a.val[(size_t)(b0 + 1) * PF_BM];
   const int e0 = a.be[b0], e1 = v1 ? a.be[b0 + 1] : -1;
-  PfPass pass[2];
+  // at most two passes, kept in registers (a run-time-indexed array would live in local memory)
+  PfPass pass0, pass1 = {b0 + 1, 1, e1, 1};
   int npass;
-  if (v1 && e1 == e0) { pass[0] = {b0, 2, e0, 0}; npass = 1; }
-  else if (v1) { pass[0] = {b0, 1, e0, 0}; pass[1] = {b0 + 1, 1, e1, 1}; npass = 2; }
-  else { pass[0] = {b0, 1, e0, 0}; npass = 1; }
+  if (v1 && e1 == e0) { pass0 = {b0, 2, e0, 0}; npass = 1; }
+  else if (v1) { pass0 = {b0, 1, e0, 0}; npass = 2; }
+  else { pass0 = {b0, 1, e0, 0}; npass = 1; }
+  auto pass_of = [&](int pi) { return pi == 0 ? pass0 : pass1; };
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int elem = PREC == VQ2_PREC_FP8 ? 1 : 2;
@@ -321,7 +323,7 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
     if (lane == 0) {
       int gc = 0;
       for (int pi = 0; pi < npass; ++pi) {
-        const PfPass P = pass[pi];
+        const PfPass P = pass_of(pi);
         for (int c = 0; c < nchunks; ++c, ++gc) {
           const int slot = gc % PF_STAGES;
           if (gc >= PF_STAGES && !mbar_wait(&sh->empty[slot], ((gc / PF_STAGES) - 1) & 1)) { pi = npass; break; }
@@ -337,7 +339,7 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
     constexpr int LOB = 128 / elem / 4;               // lo bytes per row per stage (32 fp8, 16 f16)
     int gc = 0;
     for (int pi = 0; pi < npass; ++pi) {
-      const PfPass P = pass[pi];
+      const PfPass P = pass_of(pi);
       const uint8_t* hi_r[8];
       const uint8_t* sc_r[8];
 #pragma unroll
@@ -379,7 +381,7 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
       int gc = 0;
       bool ok = true;
       for (int pi = 0; pi < npass && ok; ++pi) {
-        const PfPass P = pass[pi];
+        const PfPass P = pass_of(pi);
         for (int c = 0; c < nchunks; ++c, ++gc) {
           const int slot = gc % PF_STAGES, bslot = gc % PF_BSTAGES;
           if (!mbar_wait(&sh->full_a[slot], (gc / PF_STAGES) & 1)) { ok = false; break; }
@@ -408,27 +410,29 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
     // ---------------- weight decoders (512 threads: row r, half h of the 128-byte row)
     // the two half-row threads of a row are adjacent lanes: index-plane reads are contiguous
     const int dt = threadIdx.x - 96, r = dt >> 1, h = dt & 1;
-    const uint8_t* cbl = cbs + (lane & (PF_CB_COPIES - 1)) * 8;
+    const uint32_t cbl = smem_u32(cbs + (lane & (PF_CB_COPIES - 1)) * 8);   // shared-window address
     int gc = 0;
     bool ok = true;
     for (int pi = 0; pi < npass; ++pi) {
-      const PfPass P = pass[pi];
+      const PfPass P = pass_of(pi);
       for (int c = 0; c < nchunks && ok; ++c, ++gc) {
         const int slot = gc % PF_ISTAGES, bslot = gc % PF_BSTAGES;
         if (!mbar_wait(&sh->full_i[slot], (gc / PF_ISTAGES) & 1)) { ok = false; break; }
         if (gc >= PF_BSTAGES && !mbar_wait(&sh->empty_b[bslot], ((gc / PF_BSTAGES) - 1) & 1)) { ok = false; break; }
-        const uint8_t* ip = I_t(slot);
-        uint8_t* bt = B_t(bslot);
+        const uint32_t ip = smem_u32(I_t(slot));
+        const uint32_t bt = smem_u32(B_t(bslot));
         if (PREC == VQ2_PREC_FP8) {                   // 16 sub-vectors = one 64-group; lo rows 32 B apart
-          const uint4 lo = *(const uint4*)(ip + r * 32 + h * 16);
-          const uint32_t hw = *(const uint32_t*)(ip + PF_IDX_HI + r * 8 + h * 4);
-          const float scf = __half2float(*(const __half*)(ip + PF_IDX_SC + r * 4 + h * 2));
+          const uint4 lo = lds128_v(ip + r * 32 + h * 16);
+          const uint32_t hw = lds32_v(ip + PF_IDX_HI + r * 8 + h * 4);
+          const uint32_t sbits = lds16_v(ip + PF_IDX_SC + r * 4 + h * 2);
+          const float scf = __half2float(__ushort_as_half((unsigned short)sbits));
           decode_b_quarter<PREC>(cbl, make_uint2(lo.x, lo.y), hw & 0xFFFFu, scf, bt, r, 2 * h);
           decode_b_quarter<PREC>(cbl, make_uint2(lo.z, lo.w), hw >> 16, scf, bt, r, 2 * h + 1);
         } else {                                      // 8 sub-vectors; lo rows 16 B apart
-          const uint2 lo = *(const uint2*)(ip + r * 16 + h * 8);
-          const uint32_t hw = *(const uint16_t*)(ip + PF_IDX_HI + r * 8 + h * 2);
-          const float scf = __half2float(*(const __half*)(ip + PF_IDX_SC + r * 4 + (c & 1) * 2));
+          const uint2 lo = lds64_v(ip + r * 16 + h * 8);
+          const uint32_t hw = lds16_v(ip + PF_IDX_HI + r * 8 + h * 2);
+          const uint32_t sbits = lds16_v(ip + PF_IDX_SC + r * 4 + (c & 1) * 2);
+          const float scf = __half2float(__ushort_as_half((unsigned short)sbits));
           decode_b_quarter<PREC>(cbl, make_uint2(lo.x, 0u), hw & 0xFFu, scf, bt, r, 2 * h);
           decode_b_quarter<PREC>(cbl, make_uint2(lo.y, 0u), hw >> 8, scf, bt, r, 2 * h + 1);
         }
