@@ -280,7 +280,7 @@ def run_ours(args, rank, world):
                          "frac": achieved / hbm,
                          # dram read+write of one layer call (both decode kernels), from the ncu
                          # capture summarised in profiles/decode_config1_b1.txt (8 distinct experts)
-                         "traffic": 69.7e6, "traffic_unit": "bytes per layer call",
+                         "traffic": 69.97e6, "traffic_unit": "bytes per layer call",
                          "kernel": "decode layer call (gate/up + down kernels, CUDA events around both)",
                          "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src,
                          "bytes": "index planes of distinct experts + x + out per layer call",
