@@ -13,6 +13,9 @@ partitioned over the ranks, NCCL all-to-all dispatch and combine — timed as th
 
 --impl reference: the reference's CPU path (fp32 dequant + matmul, restated in
 oracle/torch_ref.py) on the host cores, on the same metric; rank 0 only.
+
+--ref-gpu: the reference's own GPU kernels (an unmodified install in baseline/_ref; its prefill
+extension built for sm_100a by baseline/build_ref_ext.py) timed beside ours on the same inputs.
 """
 from __future__ import annotations
 
@@ -294,6 +297,104 @@ def run_ours(args, rank, world):
     print(json.dumps(line), flush=True)
 
 
+def run_ref_gpu(args):
+    """--ref-gpu: the reference's own GPU path on this B200 beside ours, same layers and inputs:
+    decode (its Triton kernels, vq2_moe_fused_10b) at config 1, N=1 and N=3, eager and CUDA-graph
+    replayed; prefill (its vq2_grouped.cu fp8 path, vq2_moe_grouped_wmma) at config 2. Reports
+    both timings and the relative L2 distance between the two outputs. One JSON line."""
+    from vq2_vllm import synth
+    from vq2_vllm.kernels.ds4_vq2_cuda import vq2_moe_grouped_wmma as ours_pf
+    from vq2_vllm.kernels.vq2_kernel import vq2_moe_fused_10b as ours_dec
+    from oracle import torch_ref
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    try:
+        from baseline.ref_modules import RefModules
+        refs = RefModules()
+    except Exception as ex:      # reference absent or not importable: say why, exit cleanly
+        print(json.dumps({"impl": "reference-gpu", "unavailable": f"{type(ex).__name__}: {ex}"}), flush=True)
+        return
+    ref_dec = refs.mods["vq2_kernel"].vq2_moe_fused_10b
+    ref_pf = refs.mods["ds4_vq2_cuda"].vq2_moe_grouped_wmma
+    nlayers = 4
+    layers = [synth.make_layer(E, H, I, seed=1000 * l, device=dev) for l in range(nlayers)]
+    stream = torch.cuda.current_stream()
+
+    def timed(fn, steps, graph):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        if graph:
+            gs = []
+            for j in range(nlayers):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g):
+                    fn(j)
+                gs.append(g)
+            torch.cuda.synchronize()
+            run = lambda i: gs[i % nlayers].replay()
+        else:
+            run = fn
+        for i in range(3):
+            run(i)
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        torch.cuda._sleep(5_000_000)
+        s.record(stream)
+        for i in range(steps):
+            run(i)
+        e.record(stream)
+        e.synchronize()
+        return s.elapsed_time(e) / steps
+
+    out = {"impl": "reference-gpu", "metric": METRIC, "n_gpus": 1, "steps": args.steps,
+           "config": {"workload": "config1 decode (N=1, 3) and config2 prefill, reference GPU path vs ours",
+                      "H": H, "I": I, "E": E, "topk": K, "l2": f"{nlayers} layers cycled"},
+           "reference": "baseline/_ref (unmodified install); prefill extension built for sm_100a by "
+                        "baseline/build_ref_ext.py", "decode": {}}
+    for N in (1, 3):
+        x = synth.make_tokens(N, H, seed=400 + N, device=dev)
+        ids, tw = make_routing(x, 500 + N)
+        res = {}
+        for name, fn in (("ours", ours_dec), ("reference", ref_dec)):
+            call = lambda i, fn=fn: fn(x, ids, tw, *synth.layer_args(layers[i % nlayers]))
+            with refs:
+                res[name] = {"eager_us_per_call": 1e3 * timed(call, args.steps, False)}
+                try:
+                    res[name]["graph_us_per_call"] = 1e3 * timed(call, args.steps, True)
+                except Exception as ex:
+                    res[name]["graph_us_per_call"] = None
+                    res[name]["graph_error"] = f"{type(ex).__name__}: {ex}"[:200]
+        with refs:
+            a = ours_dec(x, ids, tw, *synth.layer_args(layers[0]))
+            b = ref_dec(x, ids, tw, *synth.layer_args(layers[0]))
+            d = torch_ref.moe_ref(x, ids, tw, layers[0])
+        res["rel_l2_ours_vs_reference"] = torch_ref.rel_l2(a, b)
+        res["rel_l2_ours_vs_fp32"] = torch_ref.rel_l2(a, d)
+        res["rel_l2_reference_vs_fp32"] = torch_ref.rel_l2(b, d)
+        out["decode"][f"N={N}"] = res
+    if refs.has_prefill:
+        Np = 8192
+        x = synth.make_tokens(Np, H, seed=300, device=dev)
+        ids, tw = synth.route_zipf(Np, E, K, s=1.1, seed=301, device=dev)
+        flops = 2.0 * Np * K * H * 2 * I + 2.0 * Np * K * I * H
+        pf = {}
+        reps = max(3, min(args.steps, 10))
+        for name, fn in (("ours", lambda i: ours_pf(x, ids, tw, *synth.layer_args(layers[i % nlayers]), precision="fp8")),
+                         ("reference", lambda i: ref_pf(x, ids, tw, *synth.layer_args(layers[i % nlayers])))):
+            with refs:
+                ms = timed(fn, reps, False)
+            pf[name] = {"fp8_ms_per_call": ms, "tok_per_s": Np / (ms * 1e-3), "tflops": flops / (ms * 1e-3) / 1e12}
+        with refs:
+            a = ours_pf(x, ids, tw, *synth.layer_args(layers[0]), precision="fp8")
+            b = ref_pf(x, ids, tw, *synth.layer_args(layers[0]))
+        pf["rel_l2_ours_vs_reference"] = torch_ref.rel_l2(a, b)
+        out["prefill"] = pf
+    else:
+        out["prefill"] = {"unavailable": "reference extension not built for sm_100a (baseline/build_ref_ext.py)"}
+    print(json.dumps(out), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -302,7 +403,11 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu", action="store_true", help="skip the CPU baseline leg")
     ap.add_argument("--soak", type=float, default=0.6, help="untimed seconds before the timed decode steps")
+    ap.add_argument("--ref-gpu", action="store_true",
+                    help="time the reference's own GPU path (baseline/_ref) beside ours; one JSON line")
     args = ap.parse_args()
+    if args.ref_gpu:
+        return run_ref_gpu(args)
     rank = int(os.environ.get("RANK", 0))
     world = int(os.environ.get("WORLD_SIZE", 1))
     if args.impl == "reference":
