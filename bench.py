@@ -126,6 +126,54 @@ def cpu_reference_us_per_token(threads, tokens=1, reps=1):
     return statistics.median(ts) * 1e6 / tokens, f"{tokens} token(s), top-8 over 8 resident experts, H=4096 I=2048"
 
 
+def cpu_reference_prefill_tok_per_s(threads, tokens=256):
+    """The reference's CPU path on a bounded prefill sample: `tokens` tokens, each routed top-8
+    over 8 resident experts of the config-1 shape, i.e. `tokens` pairs per expert (256 is the
+    config-2 mean, 65,536 pairs over 256 experts); scaled to config 2 (8192 tokens, 256 experts)."""
+    from oracle import torch_ref
+    from vq2_vllm import synth
+    torch.set_num_threads(threads)
+    layer = _cpu_layer()
+    x = synth.make_tokens(tokens, H, seed=2)
+    ids = torch.arange(8, dtype=torch.int32).repeat(tokens, 1)
+    w = torch.full((tokens, K), 1.0 / K)
+    t0 = time.perf_counter()
+    torch_ref.moe_ref(x, ids, w, layer)
+    t_sample = time.perf_counter() - t0
+    t_layer = t_sample * E / 8
+    return 8192 / t_layer, (f"{tokens} tokens x top-8 over 8 resident experts ({tokens} pairs per expert), "
+                            f"{t_sample:.2f} s, scaled by 256/8 experts to config 2")
+
+
+def time_decode_graph(layers, xs, routes, steps, stream):
+    """The same decode steps replayed from CUDA graphs (one graph per (layer, input) pair of the
+    cycle), as a serving engine captures decode."""
+    from vq2_vllm.kernels.vq2_kernel import vq2_moe_fused_10b
+    from vq2_vllm import synth
+    nL, nX = len(layers), len(xs)
+    ncyc = nL * nX // __import__("math").gcd(nL, nX)
+    graphs = []
+    for i in range(ncyc):
+        vq2_moe_fused_10b(xs[i % nX], *routes[i % len(routes)], *synth.layer_args(layers[i % nL]))
+    torch.cuda.synchronize()
+    for i in range(ncyc):
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            vq2_moe_fused_10b(xs[i % nX], *routes[i % len(routes)], *synth.layer_args(layers[i % nL]))
+        graphs.append(g)
+    for i in range(ncyc):
+        graphs[i].replay()
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+    torch.cuda._sleep(5_000_000)
+    s.record(stream)
+    for i in range(steps):
+        graphs[i % ncyc].replay()
+    e.record(stream)
+    e.synchronize()
+    return s.elapsed_time(e) / steps
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -230,6 +278,8 @@ def run_ours(args, rank, world):
         with Clocks(dev.index) as ck:
             ms = time_decode(layers, xs, routes, args.steps, max(args.warmup, 3), stream, soak_s=args.soak)
         res[B] = (ms, distinct, ck.summary())
+        if B == 1:
+            ms_graph = time_decode_graph(layers, xs, routes, args.steps, stream)
     ms1, u1, clocks = res[1]
     us_tok = ms1 * 1e3 / 1
     idx_bytes = u1 * IDX_BYTES_PER_EXPERT + 1 * H * 2 + 1 * H * 4
@@ -267,8 +317,10 @@ def run_ours(args, rank, world):
     prefill = time_prefill(layers, dev, args)
 
     cpu_v, cpu_sample = (None, None)
+    cpu_pf, cpu_pf_sample = (None, None)
     if not args.no_cpu:
         cpu_v, cpu_sample = cpu_reference_us_per_token(os.cpu_count() or 1)
+        cpu_pf, cpu_pf_sample = cpu_reference_prefill_tok_per_s(os.cpu_count() or 1)
     ms3, u3, _ = res[3]
     line = {"metric": METRIC, "value": us_tok, "unit": "us/token", "n_gpus": 1, "steps": args.steps,
             "warmup": max(args.warmup, 3), "ms_per_step": ms1, "higher_is_better": False, "scaling": "weak",
@@ -277,6 +329,8 @@ def run_ours(args, rank, world):
             "config": {"workload": "config1 decode batch 1 (batch 3 in decode_b3)", "H": H, "I": I, "E": E,
                        "topk": K, "batch": 1, "l2": f"{nlayers} layers cycled per step (8.8 GB > L2)",
                        "distinct_experts_per_step": u1},
+            "decode_graph": {"us_per_token": ms_graph * 1e3,
+                             "how": "the same batch-1 steps replayed from CUDA graphs"},
             "decode_b3": {"us_per_token": ms3 * 1e3 / 3, "us_per_layer_call": ms3 * 1e3, "distinct_experts": u3,
                           "idx_act_GBps": (u3 * IDX_BYTES_PER_EXPERT + 3 * H * 6) / (ms3 * 1e-3) / 1e9},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
@@ -290,6 +344,8 @@ def run_ours(args, rank, world):
                          "achieved_incl_scales": all_bytes / (ms1 * 1e-3) / 1e9},
             "cpu_baseline": {"value": cpu_v, "unit": "us/token", "cores": os.cpu_count(), "kind": "port",
                              "sample": cpu_sample},
+            "cpu_baseline_prefill": {"value": cpu_pf, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                                     "sample": cpu_pf_sample},
             "e2e": {"value": e2e_ms * 1e3, "unit": "us/token", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "prefill": prefill,
             "gpu_launches": 2 * args.steps,

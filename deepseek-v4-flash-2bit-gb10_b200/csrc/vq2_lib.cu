@@ -4,3 +4,4 @@
 #include "align.cu"
 #include "decode.cu"
 #include "prefill.cu"
+#include "ep_p2p.cu"

@@ -45,6 +45,17 @@ _SIGS = {
                                           ctypes.c_void_p, ctypes.c_void_p]),
     "vq2_hadamard_rows": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
                                          ctypes.c_long, ctypes.c_int, ctypes.c_void_p]),
+    "vq2_ep_alloc": (ctypes.c_int, [ctypes.c_size_t, ctypes.POINTER(ctypes.c_void_p)]),
+    "vq2_ep_free": (ctypes.c_int, [ctypes.c_void_p]),
+    "vq2_ipc_get_handle": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p]),
+    "vq2_ipc_open": (ctypes.c_int, [ctypes.c_void_p, ctypes.POINTER(ctypes.c_void_p)]),
+    "vq2_ipc_close": (ctypes.c_int, [ctypes.c_void_p]),
+    "vq2_ep_dispatch": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                       ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                       ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_void_p]),
+    "vq2_ep_combine": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
+                                      ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
+                                      ctypes.c_void_p, ctypes.c_void_p]),
     "vq2_device_status": (ctypes.c_int, [ctypes.c_int]),
     "vq2_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "vq2_version": (ctypes.c_int, []),

@@ -116,6 +116,136 @@ def ep_moe_gather(x, topk_ids, topk_w, expert_fn, E: int, group=None):
     return out
 
 
+EP_CTAS = 8          # VQ2_EP_CTAS of the C ABI: flags per source rank
+
+
+class _DevBuf:
+    """A raw device allocation exposed to torch (no ownership) through __cuda_array_interface__."""
+
+    def __init__(self, ptr: int, nbytes: int):
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+
+
+def _up256(v: int) -> int:
+    return (v + 255) & ~255
+
+
+class P2PExchange:
+    """Token exchange of decode-sized expert-parallel steps over NVLink peer memory (the C ABI's
+    vq2_ep_dispatch / vq2_ep_combine). Each rank allocates one exchange region, shares it through a
+    CUDA IPC handle (exchanged with all_gather_object) and maps every peer's region; a step is one
+    dispatch kernel (rows pushed to every rank, a flag per source) and one combine kernel (partial
+    outputs pushed to the owning rank, summed there in source order). Every rank must call the
+    same sequence with the same N (<= n_max). No host synchronisation: a step can be captured in
+    a CUDA graph."""
+
+    def __init__(self, n_max: int, H: int, k: int, x_dtype=torch.bfloat16, group=None):
+        import ctypes
+        from . import _lib
+        self._lib = _lib
+        L = _lib.lib()
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.n_max, self.H, self.k, self.x_dtype = n_max, H, k, x_dtype
+        self.row_x = H * torch.tensor([], dtype=x_dtype).element_size()
+        if self.row_x % 16:
+            raise ValueError("vq2 ep: token rows must be a multiple of 16 bytes")
+        W = self.world
+        o = 0
+        self.off_x = o; o = _up256(o + W * n_max * self.row_x)
+        self.off_ids = o; o = _up256(o + W * n_max * k * 4)
+        self.off_w = o; o = _up256(o + W * n_max * k * 4)
+        self.off_comb = o; o = _up256(o + W * n_max * H * 4)
+        self.off_dflag = o; o = _up256(o + W * EP_CTAS * 4)
+        self.off_cflag = o; o = _up256(o + W * EP_CTAS * 4)
+        self.off_epoch = o; o = _up256(o + 4)
+        self.nbytes = o
+        dev = torch.device("cuda", torch.cuda.current_device())
+        p = ctypes.c_void_p()
+        _lib.check(L.vq2_ep_alloc(self.nbytes, ctypes.byref(p)), "vq2_ep_alloc")
+        self.base = p.value
+        self.region = torch.as_tensor(_DevBuf(self.base, self.nbytes), device=dev)
+        h = (ctypes.c_char * 64)()
+        _lib.check(L.vq2_ipc_get_handle(self.base, h), "vq2_ipc_get_handle")
+        handles = [None] * W
+        dist.all_gather_object(handles, bytes(h), group=group)
+        self._opened = []
+        rows = []
+        for r in range(W):
+            if r == self.rank:
+                b = self.base
+            else:
+                q = ctypes.c_void_p()
+                _lib.check(L.vq2_ipc_open(ctypes.create_string_buffer(handles[r], 64), ctypes.byref(q)), "vq2_ipc_open")
+                b = q.value
+                self._opened.append(b)
+            rows.append([b + self.off_x, b + self.off_ids, b + self.off_w, b + self.off_comb,
+                         b + self.off_dflag, b + self.off_cflag])
+        self.peers = torch.tensor(rows, dtype=torch.int64, device=dev)
+        torch.cuda.synchronize()
+        dist.barrier(group=group)            # every region is zeroed and mapped before any push
+
+    def gathered(self, N: int):
+        """Views of the gathered rows in source-rank order: x [W*N, H], ids i32 [W*N, k], w f32 [W*N, k]."""
+        W, r = self.world, self.region
+        xa = r[self.off_x:self.off_x + W * N * self.row_x].view(self.x_dtype).view(W * N, self.H)
+        ia = r[self.off_ids:self.off_ids + W * N * self.k * 4].view(torch.int32).view(W * N, self.k)
+        wa = r[self.off_w:self.off_w + W * N * self.k * 4].view(torch.float32).view(W * N, self.k)
+        return xa, ia, wa
+
+    @staticmethod
+    def _aligned(t):
+        t = t.contiguous()
+        return t if t.data_ptr() % 16 == 0 else t.clone()
+
+    def dispatch(self, x, topk_ids, topk_w):
+        N = x.shape[0]
+        if N > self.n_max or x.dtype != self.x_dtype or x.shape[1] != self.H or topk_ids.shape[1] != self.k:
+            raise ValueError("vq2 ep: step does not fit the exchange region")
+        x = self._aligned(x)
+        if topk_ids.dtype not in (torch.int32, torch.int64):
+            topk_ids = topk_ids.to(torch.int32)
+        ids = self._aligned(topk_ids)               # i64 ids are narrowed by the dispatch kernel
+        w = self._aligned(topk_w.float())
+        self._lib.check(self._lib.lib().vq2_ep_dispatch(
+            x.data_ptr(), ids.data_ptr(), 1 if ids.dtype == torch.int64 else 0, w.data_ptr(), N, self.row_x, self.k,
+            self.peers.data_ptr(), self.world,
+            self.rank, self.base, self.off_dflag, self.off_epoch, self._lib.stream_ptr()), "vq2_ep_dispatch")
+        return self.gathered(N)
+
+    def combine(self, part, N: int):
+        part = self._aligned(part.float())
+        out = torch.empty(N, self.H, dtype=torch.float32, device=part.device)
+        self._lib.check(self._lib.lib().vq2_ep_combine(
+            part.data_ptr(), N, self.H, self.peers.data_ptr(), self.world, self.rank, self.base, self.off_comb,
+            self.off_cflag, self.off_epoch, out.data_ptr(), self._lib.stream_ptr()), "vq2_ep_combine")
+        return out
+
+    def close(self):
+        torch.cuda.synchronize()
+        L = self._lib.lib()
+        for b in self._opened:
+            L.vq2_ipc_close(b)
+        self._opened = []
+        if self.base:
+            L.vq2_ep_free(self.base)
+            self.base = 0
+
+
+def ep_moe_p2p(x, topk_ids, topk_w, expert_fn, E: int, exch: P2PExchange):
+    """ep_moe_gather over NVLink peer memory: the gathered rows land in the exchange region (no
+    packing copies), this rank's experts run on them, and the partial outputs return to their
+    owners through the same region."""
+    world, rank = exch.world, exch.rank
+    if E % world:
+        raise ValueError(f"vq2 ep: {E} experts do not split evenly over {world} ranks")
+    per = E // world
+    N = x.shape[0]
+    xa, ia, wa = exch.dispatch(x, topk_ids, topk_w)
+    part = expert_fn(xa, ia, wa, rank * per, per)
+    return exch.combine(part, N)
+
+
 def local_layer(layer: dict, rank: int, world: int) -> dict:
     """This rank's slice of a full layer dict (experts [rank*E/W, (rank+1)*E/W))."""
     E = layer["w13_lo"].shape[0]
@@ -157,13 +287,36 @@ def bench_ep(args, rank, world, metric):
     fns = [cuda_expert_fn(L) for L in layers]
 
     graphs_used = {}
+    use_p2p = os.environ.get("VQ2_EP_P2P", "1") != "0"
+    exchanges = {}
+    idx_bytes_per_expert = 3 * H * I // 4 + 3 * H * I // 16      # lo + hi planes, gate/up/down
 
-    def run(per_rank, steps, warmup):
+    def local_distinct(per_rank):
+        """Mean over the 8 input sets of the distinct experts this rank serves per step (every
+        rank's routing is rebuilt from its seed, so no communication is needed)."""
+        tot = 0
+        for j in range(8):
+            ids = torch.cat([synth.route_uniform(per_rank, E, K, seed=500 + 97 * r + j, device=dev)[0]
+                             for r in range(world)]).long()
+            mine = ids[(ids >= rank * per) & (ids < (rank + 1) * per)]
+            tot += torch.unique(mine).numel()
+        return tot / 8
+
+    def run(per_rank, steps, warmup, collective_only=False):
         xs = [synth.make_tokens(per_rank, H, seed=50 + 97 * rank + j, device=dev) for j in range(8)]
         rs = [synth.route_uniform(per_rank, E, K, seed=500 + 97 * rank + j, device=dev) for j in range(8)]
         gather = per_rank * world <= 512
         moe = ep_moe_gather if gather else ep_moe
-        step = lambda i: moe(xs[i % 8], rs[i % 8][0], rs[i % 8][1], fns[i % nlayers], E)
+        if gather and use_p2p:               # NVLink peer-memory exchange (one region per size)
+            if per_rank not in exchanges:
+                exchanges[per_rank] = P2PExchange(per_rank, H, K)
+            exch = exchanges[per_rank]
+            moe = lambda x, ids, w, fn, E_: ep_moe_p2p(x, ids, w, fn, E_, exch)
+        if collective_only:      # the same exchange with an expert function that does no work
+            zero = lambda x, ids, w, base, El: torch.zeros(x.shape[0], H, device=x.device)
+            step = lambda i: moe(xs[i % 8], rs[i % 8][0], rs[i % 8][1], zero, E)
+        else:
+            step = lambda i: moe(xs[i % 8], rs[i % 8][0], rs[i % 8][1], fns[i % nlayers], E)
         for i in range(warmup):
             step(i)
         torch.cuda.synchronize()
@@ -171,6 +324,7 @@ def bench_ep(args, rank, world, metric):
             # the gather-mode step has no host read: replay it from CUDA graphs, one per input set
             try:
                 gs = []
+                torch.cuda.synchronize()
                 for j in range(8):
                     g = torch.cuda.CUDAGraph()
                     with torch.cuda.graph(g):
@@ -179,9 +333,11 @@ def bench_ep(args, rank, world, metric):
                 torch.cuda.synchronize()
                 dist.barrier()
                 step = lambda i: gs[i % 8].replay()
-                graphs_used[per_rank] = True
+                if not collective_only:
+                    graphs_used[per_rank] = True
             except Exception as ex:            # fall back to eager launches
-                graphs_used[per_rank] = f"eager ({type(ex).__name__})"
+                if not collective_only:
+                    graphs_used[per_rank] = f"eager ({type(ex).__name__})"
                 torch.cuda.synchronize()
         torch.cuda.synchronize()
         dist.barrier()
@@ -197,12 +353,25 @@ def bench_ep(args, rank, world, metric):
         dist.barrier()
         return ms.item()
 
+    def detail(per_rank, ms):
+        """Per-GPU HBM rate on the index bytes of this rank's distinct experts (mean over ranks)
+        and the exchange alone."""
+        u = torch.tensor([local_distinct(per_rank)], device=dev)
+        dist.all_reduce(u)
+        u = u.item() / world
+        coll = run(per_rank, max(3, args.steps // 4), 3, collective_only=True)
+        return {"local_distinct_experts_per_rank": u,
+                "local_idx_GBps_per_gpu": u * idx_bytes_per_expert / (ms * 1e-3) / 1e9,
+                "exchange_only_us": coll * 1e3}
+
     ms1 = run(1, args.steps, max(args.warmup, 3))
+    d1 = detail(1, ms1)
     extra = {}
     for total in (64, 256):
         if total % world == 0:
             m = run(total // world, max(3, args.steps // 4), 3)
-            extra[f"config3_{total}_tokens"] = {"ms_per_step": m, "us_per_token": m * 1e3 / total}
+            extra[f"config3_{total}_tokens"] = {"ms_per_step": m, "us_per_token": m * 1e3 / total,
+                                                **detail(total // world, m)}
     if rank == 0:
         line = {"metric": metric, "value": ms1 * 1e3 / world, "unit": "us/token", "n_gpus": world,
                 "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms1,
@@ -212,7 +381,13 @@ def bench_ep(args, rank, world, metric):
                 "config": {"workload": "expert-parallel decode, 1 token per rank per step",
                            "H": H, "I": I, "E": E, "topk": K, "experts_per_rank": per,
                            "parallelism": f"ep{world}", "l2": f"{nlayers} layers cycled"},
-                "ep": extra, "cuda_graphs": {str(k): v for k, v in graphs_used.items()},
+                "ep": {"one_token_per_rank": d1, **extra,
+                       "exchange": "nvlink peer memory (vq2_ep_dispatch / vq2_ep_combine)" if use_p2p
+                       else "nccl all_gather + reduce_scatter"},
+                "cuda_graphs": {str(k): v for k, v in graphs_used.items()},
                 "gpu_launches": 2 * args.steps}
         print(json.dumps(line), flush=True)
+    for ex in exchanges.values():
+        ex.close()
+    dist.barrier()
     dist.destroy_process_group()

@@ -109,6 +109,38 @@ int vq2_quant_fp8_rows(const float* x, int rows, int cols, uint8_t* out, float* 
 int vq2_hadamard_rows(const void* x, int in_dtype, void* y, int out_dtype, long rows, int cols, void* stream);
 
 /* Error word written by bounded device waits (0 = none). Synchronises the device. */
+/* ---- expert-parallel token exchange over NVLink peer memory (no counterpart in the reference,
+   which runs on one device). One exchange region per rank, allocated by vq2_ep_alloc (zeroed) and
+   shared through CUDA IPC handles; regions are laid out identically on every rank:
+     X    [world][N][row_x]   token rows as pushed by each source rank (bytes, 16-byte multiple)
+     IDS  [world][N][k] i32   their expert ids
+     WT   [world][N][k] f32   their routing weights
+     COMB [world][N][H] f32   partial outputs pushed back by each rank, for this rank's tokens
+     DFLAG[world][VQ2_EP_CTAS] u32, CFLAG[world][VQ2_EP_CTAS] u32   per-(source, slice) step flags
+     EPOCH u32   this rank's step
+   `peers` is a device array [world][6] of u64 addresses (X, IDS, WT, COMB, DFLAG, CFLAG) of every
+   rank's region, this rank's included. Every rank calls dispatch / combine once per step with the
+   same N. Waits are bounded: a peer that never arrives makes vq2_device_status report
+   VQ2_ERR_TIMEOUT, and the call returns with the data it has. */
+#define VQ2_EP_CTAS 8   /* at most this many slices (CTAs, flags) per destination: one per 32 KB */
+int vq2_ep_alloc(size_t bytes, void** dev_ptr_out);
+int vq2_ep_free(void* dev_ptr);
+int vq2_ipc_get_handle(const void* dev_ptr, void* handle_out /* 64 bytes */);
+int vq2_ipc_open(const void* handle /* 64 bytes */, void** dev_ptr_out);
+int vq2_ipc_close(void* dev_ptr);
+/* Push this rank's N rows (x: N x row_x bytes; ids N x k of VQ2_ID_I32 / VQ2_ID_I64, stored as
+   i32; w f32 N x k) into slot `rank` of every rank's X/IDS/WT, signal, and wait until every rank's
+   rows have arrived here. */
+int vq2_ep_dispatch(const void* x, const void* ids, int ids_dtype, const float* w, int N, int row_x, int k,
+                    const uint64_t* peers, int world, int rank, void* my_region, size_t off_dflag,
+                    size_t off_epoch, void* stream);
+/* part: f32 [world*N][H], rows [d*N, (d+1)*N) belong to rank d's tokens. Push them into slot
+   `rank` of rank d's COMB, signal, wait for every rank's rows, and write out[n][h] = sum over
+   source ranks of COMB[src][n][h] (f32 [N][H]). */
+int vq2_ep_combine(const float* part, int N, int H, const uint64_t* peers, int world, int rank,
+                   void* my_region, size_t off_comb, size_t off_cflag, size_t off_epoch, float* out,
+                   void* stream);
+
 int vq2_device_status(int reset);
 const char* vq2_strerror(int code);
 int vq2_version(void);

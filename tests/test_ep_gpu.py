@@ -1,5 +1,7 @@
-"""Expert-parallel decode and prefill over NCCL on 2 GPUs (skipped with fewer), against the fp32
-oracle of the same full layer. NVLS is off (NCCL_NVLS_ENABLE=0) in the child ranks."""
+"""Expert-parallel decode and prefill on 2 GPUs (skipped with fewer) against the fp32 oracle of the
+same full layer: NCCL gather and all-to-all modes, and the NVLink peer-memory exchange (several
+consecutive steps through one region, with different token counts). NVLS is off
+(NCCL_NVLS_ENABLE=0) in the child ranks."""
 import os
 import socket
 
@@ -38,11 +40,21 @@ def _worker(rank, world, port, q):
         local = {k: v.clone() for k, v in ep.local_layer(layer, rank, world).items()}
         fn = ep.cuda_expert_fn(local)
         res = []
-        for N, mode in ((4, "gather"), (4, "a2a"), (300, "a2a")):
-            x = synth.make_tokens(N, H, seed=10 + rank, device=dev)
-            ids, w = synth.route_uniform(N, E, 8, seed=20 + rank, device=dev)
-            out = (ep.ep_moe_gather if mode == "gather" else ep.ep_moe)(x, ids, w, fn, E)
-            res.append(torch_ref.rel_l2(out, torch_ref.moe_ref(x, ids, w, layer)))
+        exch = ep.P2PExchange(4, H, 8)
+        for N, mode in ((4, "gather"), (4, "a2a"), (300, "a2a"), (4, "p2p"), (1, "p2p"), (3, "p2p")):
+            for rep in range(2 if mode == "p2p" else 1):       # p2p: consecutive steps reuse the region
+                x = synth.make_tokens(N, H, seed=10 + rank + rep, device=dev)
+                ids, w = synth.route_uniform(N, E, 8, seed=20 + rank + rep, device=dev)
+                if mode == "p2p":
+                    out = ep.ep_moe_p2p(x, ids, w, fn, E, exch)
+                else:
+                    out = (ep.ep_moe_gather if mode == "gather" else ep.ep_moe)(x, ids, w, fn, E)
+                res.append(torch_ref.rel_l2(out, torch_ref.moe_ref(x, ids, w, layer)))
+        from vq2_vllm import _lib
+        status = _lib.lib().vq2_device_status(1)
+        exch.close()
+        if status != 0:
+            raise RuntimeError(f"device status {status}")
         q.put((rank, "ok", max(res)))
         dist.destroy_process_group()
     except Exception as ex:
