@@ -130,6 +130,10 @@ def _up256(v: int) -> int:
     return (v + 255) & ~255
 
 
+class P2PUnavailable(RuntimeError):
+    """Peer mapping failed on some rank; every rank raises it together."""
+
+
 class P2PExchange:
     """Token exchange of decode-sized expert-parallel steps over NVLink peer memory (the C ABI's
     vq2_ep_dispatch / vq2_ep_combine). Each rank allocates one exchange region, shares it through a
@@ -171,16 +175,25 @@ class P2PExchange:
         dist.all_gather_object(handles, bytes(h), group=group)
         self._opened = []
         rows = []
+        ok = 1
         for r in range(W):
             if r == self.rank:
                 b = self.base
             else:
                 q = ctypes.c_void_p()
-                _lib.check(L.vq2_ipc_open(ctypes.create_string_buffer(handles[r], 64), ctypes.byref(q)), "vq2_ipc_open")
-                b = q.value
-                self._opened.append(b)
+                if L.vq2_ipc_open(ctypes.create_string_buffer(handles[r], 64), ctypes.byref(q)) != 0:
+                    ok, b = 0, 0
+                else:
+                    b = q.value
+                    self._opened.append(b)
             rows.append([b + self.off_x, b + self.off_ids, b + self.off_w, b + self.off_comb,
                          b + self.off_dflag, b + self.off_cflag])
+        # every rank learns whether every rank mapped every peer (so all fall back together)
+        flag = torch.tensor([ok], dtype=torch.int32, device=dev)
+        dist.all_reduce(flag, op=dist.ReduceOp.MIN, group=group)
+        if flag.item() == 0:
+            self.close()
+            raise P2PUnavailable("vq2 ep: a rank could not map a peer's exchange region (CUDA IPC)")
         self.peers = torch.tensor(rows, dtype=torch.int64, device=dev)
         torch.cuda.synchronize()
         dist.barrier(group=group)            # every region is zeroed and mapped before any push
@@ -309,9 +322,13 @@ def bench_ep(args, rank, world, metric):
         moe = ep_moe_gather if gather else ep_moe
         if gather and use_p2p:               # NVLink peer-memory exchange (one region per size)
             if per_rank not in exchanges:
-                exchanges[per_rank] = P2PExchange(per_rank, H, K)
+                try:
+                    exchanges[per_rank] = P2PExchange(per_rank, H, K)
+                except P2PUnavailable:
+                    exchanges[per_rank] = None      # all ranks fall back to NCCL together
             exch = exchanges[per_rank]
-            moe = lambda x, ids, w, fn, E_: ep_moe_p2p(x, ids, w, fn, E_, exch)
+            if exch is not None:
+                moe = lambda x, ids, w, fn, E_: ep_moe_p2p(x, ids, w, fn, E_, exch)
         if collective_only:      # the same exchange with an expert function that does no work
             zero = lambda x, ids, w, base, El: torch.zeros(x.shape[0], H, device=x.device)
             step = lambda i: moe(xs[i % 8], rs[i % 8][0], rs[i % 8][1], zero, E)
@@ -382,12 +399,14 @@ def bench_ep(args, rank, world, metric):
                            "H": H, "I": I, "E": E, "topk": K, "experts_per_rank": per,
                            "parallelism": f"ep{world}", "l2": f"{nlayers} layers cycled"},
                 "ep": {"one_token_per_rank": d1, **extra,
-                       "exchange": "nvlink peer memory (vq2_ep_dispatch / vq2_ep_combine)" if use_p2p
+                       "exchange": "nvlink peer memory (vq2_ep_dispatch / vq2_ep_combine)"
+                       if use_p2p and all(v is not None for v in exchanges.values())
                        else "nccl all_gather + reduce_scatter"},
                 "cuda_graphs": {str(k): v for k, v in graphs_used.items()},
                 "gpu_launches": 2 * args.steps}
         print(json.dumps(line), flush=True)
     for ex in exchanges.values():
-        ex.close()
+        if ex is not None:
+            ex.close()
     dist.barrier()
     dist.destroy_process_group()
