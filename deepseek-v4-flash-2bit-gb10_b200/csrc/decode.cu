@@ -363,8 +363,9 @@ __device__ __forceinline__ DecSmem dec_smem(uint8_t* smem) {
   return d;
 }
 
-// Barrier init, codebook bulk copy, expert plan (all threads; ends with __syncthreads).
-__device__ __forceinline__ void dec_prologue(const vq2_moe_args& a, const uint16_t* cb, DecSmem d) {
+// Barrier init and codebook bulk copy (thread 0; the codebook is a constant weight, so this may
+// run before the grid-dependency wait).
+__device__ __forceinline__ void dec_init(const uint16_t* cb, DecSmem d) {
   if (threadIdx.x == 0) {
     for (int s = 0; s < DEC_STAGES; ++s) { mbar_init(&d.sh->full[s], 1); mbar_init(&d.sh->empty[s], DEC_NW); }
     mbar_init(&d.sh->cbbar, 1);
@@ -373,6 +374,10 @@ __device__ __forceinline__ void dec_prologue(const vq2_moe_args& a, const uint16
     mbar_arrive_expect_tx(&d.sh->cbbar, 1024 * 4 * 2);
     bulk_g2s(d.sh->scratch, cb, 1024 * 4 * 2, &d.sh->cbbar);
   }
+}
+// Barrier init, codebook bulk copy, expert plan (all threads; ends with __syncthreads).
+__device__ __forceinline__ void dec_prologue(const vq2_moe_args& a, const uint16_t* cb, DecSmem d) {
+  dec_init(cb, d);
   build_plan(a.topk_ids, a.ids_dtype, a.topk_w, a.N * a.topk, a.E, a.expert_base, d.sh);
 }
 
@@ -678,8 +683,16 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
   extern __shared__ __align__(128) uint8_t smem[];
   const DecSmem d = dec_smem(smem);
   if (threadIdx.x == 0) PROBE(0, 0);
+  // Launched with programmatic dependent launch: the CTA becomes resident and issues the
+  // codebook copy (a constant weight) while the previous kernel drains. Everything after
+  // pdl_wait() reads the call's inputs or writes the workspace and output, which the previous
+  // kernel may still be using. (Replicating the codebook before the wait was measured slower:
+  // it then no longer hides the activation loads below.)
+  dec_init(a.w13_cb, d);
+  pdl_wait();
+  // dependents (the down kernel) may launch now: everything this grid waited for is complete
   pdl_launch_dependents();
-  dec_prologue(a, a.w13_cb, d);
+  build_plan(a.topk_ids, a.ids_dtype, a.topk_w, a.N * a.topk, a.E, a.expert_base, d.sh);
   int c = 0;
   if (threadIdx.x >> 5 == DEC_NW) {   // producer warp
     if ((threadIdx.x & 31) == 0) {
@@ -691,7 +704,7 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
   GateupPre pre;
   gateup_pre(a, d, pre);
   if (threadIdx.x == 0) PROBE(0, 1);
-  fill_codebook(d.cbs, d.sh);      // ends with a consumer barrier
+  fill_codebook(d.cbs, d.sh);         // overlaps the activation loads of gateup_pre
   if (threadIdx.x == 0) PROBE(0, 2);
   gateup_consume<KH>(a, d, part, pre, c);
   if (threadIdx.x == 0) PROBE(0, 4);
@@ -703,6 +716,9 @@ __global__ void __launch_bounds__(DEC_THREADS, 1)
 decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
   extern __shared__ __align__(128) uint8_t smem[];
   const DecSmem d = dec_smem(smem);
+  // the next call's gate/up kernel may launch now: before its own grid-dependency wait it only
+  // initialises barriers and copies its codebook into its shared memory
+  pdl_launch_dependents();
   dec_prologue(a, a.w2_cb, d);
   int c = 0;
   if (threadIdx.x >> 5 == DEC_NW) {   // producer warp: the weights do not depend on the gate/up grid
@@ -787,12 +803,14 @@ extern "C" int vq2_decode(const vq2_moe_args* a, void* ws, size_t ws_bytes, void
   cfg.stream = (cudaStream_t)stream;
   void (*ka)(vq2_moe_args, float*) = khA == 1 ? decode_gateup_kernel<1> : decode_gateup_kernel<2>;
   void (*kb)(vq2_moe_args, const float*, int) = khB == 1 ? decode_down_kernel<1> : decode_down_kernel<2>;
-  if (cudaLaunchKernelEx(&cfg, ka, args, part) != cudaSuccess) return VQ2_ERR_CUDA;
+  // both kernels use programmatic dependent launch (each waits for its predecessor with
+  // griddepcontrol.wait before touching anything the predecessor may produce or still read)
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, ka, args, part) != cudaSuccess) return VQ2_ERR_CUDA;
   if (cudaLaunchKernelEx(&cfg, kb, args, (const float*)part, khA) != cudaSuccess) return VQ2_ERR_CUDA;
   return VQ2_OK;
 }

@@ -360,7 +360,8 @@ def bench_ep(args, rank, world, metric):
         dist.barrier()
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(True), torch.cuda.Event(True)
-        s.record()
+        torch.cuda._sleep(5_000_000)          # every rank queues its steps ahead of its GPU, so the
+        s.record()                            # timed region sees device time, not launch gaps
         for i in range(steps):
             step(i)
         e.record()
