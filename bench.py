@@ -174,6 +174,37 @@ def time_decode_graph(layers, xs, routes, steps, stream):
     return s.elapsed_time(e) / steps
 
 
+def time_router(dev, reps=200):
+    """The fused router (top-k of softmax(x @ W_r), config-1 shapes, batch 1) against the same
+    formula as torch ops, both replayed from CUDA graphs; us per call."""
+    from vq2_vllm.kernels.router import router_topk
+    g = torch.Generator(device=dev).manual_seed(900)
+    x = torch.randn(1, H, generator=g, device=dev).bfloat16()
+    wr = (torch.randn(H, E, generator=g, device=dev) * 0.02).bfloat16()
+
+    def torch_route():
+        p = torch.softmax(x.float() @ wr.float(), -1)
+        return torch.topk(p, K, -1)
+
+    res = {}
+    for name, f in (("ours_us", lambda: router_topk(x, wr, K)), ("torch_ops_us", torch_route)):
+        for _ in range(5):
+            f()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            f()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        torch.cuda._sleep(3_000_000)
+        s.record()
+        for _ in range(reps):
+            gr.replay()
+        e.record()
+        e.synchronize()
+        res[name] = s.elapsed_time(e) * 1e3 / reps
+    return res
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -315,6 +346,7 @@ def run_ours(args, rank, world):
     d2h = H * 4
 
     prefill = time_prefill(layers, dev, args)
+    router = time_router(dev)
 
     cpu_v, cpu_sample = (None, None)
     cpu_pf, cpu_pf_sample = (None, None)
@@ -329,6 +361,7 @@ def run_ours(args, rank, world):
             "config": {"workload": "config1 decode batch 1 (batch 3 in decode_b3)", "H": H, "I": I, "E": E,
                        "topk": K, "batch": 1, "l2": f"{nlayers} layers cycled per step (8.8 GB > L2)",
                        "distinct_experts_per_step": u1},
+            "router": {**router, "workload": "top-8 of softmax(x @ W_r), x [1, 4096], W_r [4096, 256], graph replay"},
             "decode_graph": {"us_per_token": ms_graph * 1e3,
                              "how": "the same batch-1 steps replayed from CUDA graphs"},
             "decode_b3": {"us_per_token": ms3 * 1e3 / 3, "us_per_layer_call": ms3 * 1e3, "distinct_experts": u3,

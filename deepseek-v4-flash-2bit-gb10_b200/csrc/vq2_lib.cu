@@ -5,3 +5,4 @@
 #include "decode.cu"
 #include "prefill.cu"
 #include "ep_p2p.cu"
+#include "router.cu"

@@ -56,6 +56,10 @@ _SIGS = {
     "vq2_ep_combine": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
                                       ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
                                       ctypes.c_void_p, ctypes.c_void_p]),
+    "vq2_router_workspace_size": (ctypes.c_size_t, [ctypes.c_int] * 3),
+    "vq2_router_topk": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                       ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                       ctypes.c_size_t, ctypes.c_void_p]),
     "vq2_device_status": (ctypes.c_int, [ctypes.c_int]),
     "vq2_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "vq2_version": (ctypes.c_int, []),

@@ -141,6 +141,14 @@ int vq2_ep_combine(const float* part, int N, int H, const uint64_t* peers, int w
                    void* my_region, size_t off_comb, size_t off_cflag, size_t off_epoch, float* out,
                    void* stream);
 
+/* ---- router (upstream of the MoE method): topk_w, topk_ids = top-k(softmax(x . W_r)) per token,
+   weights = the selected probabilities (not renormalised); ids by probability descending, lower
+   index first on ties. x: N x H of x_dtype; w_r: bf16 [H][E] (row-major, E contiguous); N <= 64,
+   H % 64 == 0, E <= 1024, k <= min(E, 64). fp32 logits summed in a fixed order (deterministic). */
+size_t vq2_router_workspace_size(int N, int H, int E);
+int vq2_router_topk(const void* x, int x_dtype, const void* w_r, int N, int H, int E, int k,
+                    int32_t* topk_ids, float* topk_w, void* workspace, size_t ws_bytes, void* stream);
+
 int vq2_device_status(int reset);
 const char* vq2_strerror(int code);
 int vq2_version(void);
