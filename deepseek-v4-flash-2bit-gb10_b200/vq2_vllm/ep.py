@@ -266,6 +266,19 @@ def local_layer(layer: dict, rank: int, world: int) -> dict:
     return {k: (v[rank * per:(rank + 1) * per] if v.dim() == 3 else v) for k, v in layer.items()}
 
 
+def load_local_layer(path: str, rank: int, world: int, device="cpu") -> dict:
+    """This rank's experts of one ``experts_fused_layer_{L}.safetensors`` file, read as slices of
+    the file (the other ranks' experts are never read)."""
+    from safetensors import safe_open
+    from .plugin import read_fused_layer
+    with safe_open(path, "pt") as f:
+        E = f.get_slice("w13_lo").get_shape()[0]
+    if E % world:
+        raise ValueError(f"vq2 ep: {E} experts do not split evenly over {world} ranks")
+    per = E // world
+    return read_fused_layer(path, device=device, expert_range=(rank * per, (rank + 1) * per))
+
+
 def cuda_expert_fn(local: dict):
     """expert_fn running the B200 kernels on a rank's local expert slice (decode for small
     batches, the tcgen05 grouped GEMM above the decode pair limit)."""

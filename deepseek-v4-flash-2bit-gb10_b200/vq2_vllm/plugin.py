@@ -67,17 +67,34 @@ def apply_moe(layer, x, topk_weights, topk_ids, group=64):
     return out.to(x.dtype)
 
 
-def load_fused_layer_file(layer, layer_index: int, directory: str | None = None) -> bool:
+def read_fused_layer(path: str, device="cpu", expert_range=None) -> dict:
+    """The 8 tensors of one ``experts_fused_layer_{L}.safetensors`` file (reference layout,
+    vq2_vllm/__init__.py:233-235). ``expert_range=(lo, hi)`` reads only experts [lo, hi) of the
+    per-expert tensors (slices of the file, so a rank of an expert-parallel group reads only its
+    share); the codebooks are read whole."""
+    from safetensors import safe_open
+    out = {}
+    with safe_open(path, "pt", device=str(device)) as f:
+        for name in PARAMS:
+            if expert_range is not None and not name.endswith("cb"):
+                lo, hi = expert_range
+                out[name] = f.get_slice(name)[lo:hi]
+            else:
+                out[name] = f.get_tensor(name)
+    return out
+
+
+def load_fused_layer_file(layer, layer_index: int, directory: str | None = None, expert_range=None) -> bool:
     """Fast load of ``experts_fused_layer_{L}.safetensors`` (the 8 tensors, directly onto the
-    parameters' device) when present (reference vq2_vllm/__init__.py:220-235)."""
+    parameters' device) when present (reference vq2_vllm/__init__.py:220-235). With
+    ``expert_range`` only those experts are read (the layer then holds E = hi - lo experts)."""
     d = directory or os.environ.get("VQ2_EXPERTS_DIR", "models/DeepSeek-V4-Flash-2bit")
     path = f"{d}/experts_fused_layer_{layer_index}.safetensors"
     if not os.path.exists(path):
         return False
-    from safetensors import safe_open
-    f = safe_open(path, "pt", device=str(layer.w13_lo.device))
+    t = read_fused_layer(path, device=layer.w13_lo.device, expert_range=expert_range)
     for name in PARAMS:
-        getattr(layer, name).data.copy_(f.get_tensor(name))
+        getattr(layer, name).data.copy_(t[name])
     return True
 
 

@@ -62,3 +62,23 @@ def test_apply_dispatch_matches_oracle(N):
     assert out.dtype == x.dtype
     ref = torch_ref.moe_ref(x, ids, w, L) if N < 256 else torch_ref.moe_prefill_fp8_ref(x, ids, w, L)
     assert torch_ref.rel_l2(out.float(), ref) < 3e-2
+
+
+def test_fused_layer_file_sharded_read(tmp_path):
+    """An expert-parallel rank reads only its experts of a fused layer file (slices), identical to
+    slicing the whole layer."""
+    from safetensors.torch import save_file
+    from vq2_vllm import ep, synth
+    from vq2_vllm.plugin import read_fused_layer
+    layer = synth.make_layer(8, 256, 128, seed=3)
+    path = str(tmp_path / "experts_fused_layer_0.safetensors")
+    save_file({k: v.contiguous() for k, v in layer.items()}, path)
+    whole = read_fused_layer(path)
+    for k in layer:
+        assert torch.equal(whole[k], layer[k])
+    for rank in range(4):
+        mine = ep.load_local_layer(path, rank, 4)
+        ref = ep.local_layer(layer, rank, 4)
+        for k in layer:
+            assert torch.equal(mine[k], ref[k]), (rank, k)
+        assert mine["w13_lo"].shape[0] == 2 and mine["w13_cb"].shape == (1024, 4)
