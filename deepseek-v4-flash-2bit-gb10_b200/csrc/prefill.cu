@@ -11,16 +11,17 @@
 //   vb_quant   inter -> Hadamard -> per-slot quantised activation (+ inv)
 //   down       per (block, 128 output rows): D = vb . Wd^T; epilogue out[tok] += D * w * inv_vb
 //
-// GEMM CTA (one per SM, 320 threads): warp 0 allocates TMEM and loads the activation tile (rows in
-// slot order, 128-byte swizzled K-major) and the weight tile's lo index plane with 2-D TMA copies,
-// the small hi / scale planes with cp.async; warp 1 lane 0 issues tcgen05.mma
-// (M=128, N=128, K=32 fp8 / K=16 f16 per instruction) into a 128-column fp32 TMEM accumulator;
-// warps 2..9 decode the VQ weight tile (10-bit index -> fp16 codebook vector x fp16 group scale
-// -> e4m3 / f16) straight into the swizzled B tile, then run the epilogue out of TMEM.
-// A 5-stage ring of (A tile, staged index planes), filled by warp 0, and a 2-stage
-// ring of B tiles, filled by the decoders from the staged planes, are synchronised with mbarriers;
-// tcgen05.commit frees stages of both rings. The codebook (8 copies, lane l reads copy l mod 8) arrives
-// by one bulk copy.
+// GEMM CTA (608 threads; one 128-token block pair and one 256-row weight tile): warp 0 loads the
+// activation tiles of the pass's blocks (rows in slot order, 128-byte swizzled K-major) with 2-D
+// TMA into a 2-stage ring; warp 1 loads the weight tile's index planes (the lo plane by 2-D TMA,
+// the small hi / scale planes with cp.async signalling the same mbarrier) into a 3-stage ring;
+// warp 2 lane 0 issues tcgen05.mma (M=128 tokens, N=256 = 128 gate + 128 up rows or 256 down rows,
+// K=32 fp8 / K=16 f16 per instruction) into fp32 TMEM accumulators, one per block (512 columns
+// for two blocks of the same expert, so every decoded weight tile feeds two MMAs); warps 3..18
+// decode the weight tile (10-bit index -> fp16 codebook vector x fp16 group scale -> e4m3 / f16)
+// straight into the swizzled B tile of a 2-stage ring and then run the epilogue out of TMEM.
+// tcgen05.commit frees the ring stages; the codebook (8 copies, lane l reads copy l mod 8)
+// arrives by one bulk copy and is replicated in shared memory.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_fp8.h>
