@@ -6,10 +6,10 @@
 //   align      pairs grouped by expert, each expert padded to 128 slots (csrc/align.cu)
 //   act_quant  x -> Hadamard -> per-token quantised activation (fp8 e4m3 with s = 448/amax, as the
 //              reference's quant_fp8_rows; or fp16 with a power-of-two range scale)
-//   gateup     per (128-slot block, 64 gate + 64 matching up rows): D = A . B^T in TMEM, epilogue
+//   gateup     per (128-slot block, 128 gate + 128 matching up rows): D = A . B^T in TMEM, epilogue
 //              inter = silu(g * inv_x) * (u * inv_x)   (reference vq2_grouped.cu:255-264 fused)
 //   vb_quant   inter -> Hadamard -> per-slot quantised activation (+ inv)
-//   down       per (block, 128 output rows): D = vb . Wd^T; epilogue out[tok] += D * w * inv_vb
+//   down       per (block, 256 output rows): D = vb . Wd^T; epilogue out[tok] += D * w * inv_vb
 //
 // GEMM CTA (608 threads; one 128-token block pair and one 256-row weight tile): warp 0 loads the
 // activation tiles of the pass's blocks (rows in slot order, 128-byte swizzled K-major) with 2-D
