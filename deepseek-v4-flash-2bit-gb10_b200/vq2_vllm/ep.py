@@ -403,6 +403,7 @@ def bench_ep(args, rank, world, metric):
             m = run(total // world, max(3, args.steps // 4), 3)
             extra[f"config3_{total}_tokens"] = {"ms_per_step": m, "us_per_token": m * 1e3 / total,
                                                 **detail(total // world, m)}
+    p2p_used = use_p2p and all(v is not None for v in exchanges.values())
     if rank == 0:
         line = {"metric": metric, "value": ms1 * 1e3 / world, "unit": "us/token", "n_gpus": world,
                 "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms1,
@@ -413,11 +414,12 @@ def bench_ep(args, rank, world, metric):
                            "H": H, "I": I, "E": E, "topk": K, "experts_per_rank": per,
                            "parallelism": f"ep{world}", "l2": f"{nlayers} layers cycled"},
                 "ep": {"one_token_per_rank": d1, **extra,
-                       "exchange": "nvlink peer memory (vq2_ep_dispatch / vq2_ep_combine)"
-                       if use_p2p and all(v is not None for v in exchanges.values())
+                       "exchange": "nvlink peer memory (vq2_ep_dispatch / vq2_ep_combine)" if p2p_used
                        else "nccl all_gather + reduce_scatter"},
                 "cuda_graphs": {str(k): v for k, v in graphs_used.items()},
-                "gpu_launches": 2 * args.steps}
+                # this package's kernels per timed step: the two decode kernels, plus dispatch and
+                # combine with the peer-memory exchange (NCCL kernels are not counted)
+                "gpu_launches": (4 if p2p_used else 2) * args.steps}
         print(json.dumps(line), flush=True)
     for ex in exchanges.values():
         if ex is not None:
