@@ -296,7 +296,7 @@ def run_ours(args, rank, world):
     torch.cuda.set_device(dev)
     if world > 1:
         from vq2_vllm import ep
-        return ep.bench_ep(args, rank, world, METRIC)
+        return ep.bench_ep(args, rank, world, METRIC, Clocks, peaks)
     hbm, _, src = peaks()
     stream = torch.cuda.current_stream()
     nlayers = 4

@@ -292,10 +292,11 @@ def cuda_expert_fn(local: dict):
 
 
 # ----------------------------------------------------------------------------- benchmark (N > 1)
-def bench_ep(args, rank, world, metric):
+def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
     """Weak-scaling expert-parallel decode: every rank contributes `per_rank` decode tokens per
     step (1 = the config-1 batch per rank); the 256 experts are split over the ranks. Device time
-    with CUDA events, the max over ranks."""
+    with CUDA events, the max over ranks. `clocks_cls` samples the GPU clocks during the timed
+    steps (rank 0's GPU); `peaks_fn` gives the measured HBM peak for the roofline figure."""
     import json
     import os
     import time
@@ -395,8 +396,46 @@ def bench_ep(args, rank, world, metric):
                 "local_idx_GBps_per_gpu": u * idx_bytes_per_expert / (ms * 1e-3) / 1e9,
                 "exchange_only_us": coll * 1e3}
 
-    ms1 = run(1, args.steps, max(args.warmup, 3))
+    if clocks_cls is not None and rank == 0:
+        with clocks_cls(dev.index) as ck:
+            ms1 = run(1, args.steps, max(args.warmup, 3))
+        clocks = ck.summary()
+    else:
+        ms1 = run(1, args.steps, max(args.warmup, 3))
+        clocks = None
     d1 = detail(1, ms1)
+
+    # e2e: the public call (ep_moe_p2p / ep_moe_gather) with this rank's token row, ids and
+    # weights copied in from pinned host memory and its output copied back, every step
+    xh = [synth.make_tokens(1, H, seed=50 + 97 * rank + j).pin_memory() for j in range(8)]
+    rh = [tuple(t.cpu().pin_memory() for t in synth.route_uniform(1, E, K, seed=500 + 97 * rank + j, device=dev))
+          for j in range(8)]
+    outh = torch.empty(1, H, dtype=torch.float32).pin_memory()
+    exch1 = exchanges.get(1)
+
+    def e2e_step(i):
+        x = xh[i % 8].to(dev, non_blocking=True)
+        ids = rh[i % 8][0].to(dev, non_blocking=True)
+        w = rh[i % 8][1].to(dev, non_blocking=True)
+        if exch1 is not None:
+            out = ep_moe_p2p(x, ids, w, fns[i % nlayers], E, exch1)
+        else:
+            out = ep_moe_gather(x, ids, w, fns[i % nlayers], E)
+        outh.copy_(out, non_blocking=True)
+
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    dist.barrier()
+    s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+    s.record()
+    for i in range(args.steps):
+        e2e_step(i)
+    e.record()
+    e.synchronize()
+    e2e_ms = torch.tensor([s.elapsed_time(e) / args.steps], device=dev)
+    dist.all_reduce(e2e_ms, op=dist.ReduceOp.MAX)
+    e2e_ms = e2e_ms.item()
     extra = {}
     for total in (64, 256):
         if total % world == 0:
@@ -404,6 +443,8 @@ def bench_ep(args, rank, world, metric):
             extra[f"config3_{total}_tokens"] = {"ms_per_step": m, "us_per_token": m * 1e3 / total,
                                                 **detail(total // world, m)}
     p2p_used = use_p2p and all(v is not None for v in exchanges.values())
+    hbm, src = (peaks_fn()[0], peaks_fn()[2]) if peaks_fn is not None else (None, None)
+    achieved = d1["local_idx_GBps_per_gpu"]
     if rank == 0:
         line = {"metric": metric, "value": ms1 * 1e3 / world, "unit": "us/token", "n_gpus": world,
                 "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": ms1,
@@ -413,6 +454,13 @@ def bench_ep(args, rank, world, metric):
                 "config": {"workload": "expert-parallel decode, 1 token per rank per step",
                            "H": H, "I": I, "E": E, "topk": K, "experts_per_rank": per,
                            "parallelism": f"ep{world}", "l2": f"{nlayers} layers cycled"},
+                "e2e": {"value": e2e_ms * 1e3 / world, "unit": "us/token", "h2d_bytes_per_step": H * 2 + K * 8 + K * 4,
+                        "d2h_bytes_per_step": H * 4, "per": "rank (every rank copies its own token in and out)"},
+                "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                             "frac": (achieved / hbm) if hbm else None, "traffic": None,
+                             "kernel": "decode layer step per GPU (index bytes of its distinct local experts)",
+                             "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src},
+                "clocks": clocks,
                 "ep": {"one_token_per_rank": d1, **extra,
                        "exchange": "nvlink peer memory (vq2_ep_dispatch / vq2_ep_combine)" if p2p_used
                        else "nccl all_gather + reduce_scatter"},
