@@ -155,15 +155,10 @@ class P2PExchange:
         if self.row_x % 16:
             raise ValueError("vq2 ep: token rows must be a multiple of 16 bytes")
         W = self.world
-        o = 0
-        self.off_x = o; o = _up256(o + W * n_max * self.row_x)
-        self.off_ids = o; o = _up256(o + W * n_max * k * 4)
-        self.off_w = o; o = _up256(o + W * n_max * k * 4)
-        self.off_comb = o; o = _up256(o + W * n_max * H * 4)
-        self.off_dflag = o; o = _up256(o + W * EP_CTAS * 4)
-        self.off_cflag = o; o = _up256(o + W * EP_CTAS * 4)
-        self.off_epoch = o; o = _up256(o + 4)
-        self.nbytes = o
+        lay = self.layout(W, n_max, H, k, self.row_x)
+        self.off_x, self.off_ids, self.off_w, self.off_comb = lay["x"], lay["ids"], lay["w"], lay["comb"]
+        self.off_dflag, self.off_cflag, self.off_epoch = lay["dflag"], lay["cflag"], lay["epoch"]
+        self.nbytes = lay["bytes"]
         dev = torch.device("cuda", torch.cuda.current_device())
         p = ctypes.c_void_p()
         _lib.check(L.vq2_ep_alloc(self.nbytes, ctypes.byref(p)), "vq2_ep_alloc")
@@ -197,6 +192,20 @@ class P2PExchange:
         self.peers = torch.tensor(rows, dtype=torch.int64, device=dev)
         torch.cuda.synchronize()
         dist.barrier(group=group)            # every region is zeroed and mapped before any push
+
+    @staticmethod
+    def layout(world: int, n_max: int, H: int, k: int, row_x: int) -> dict:
+        """Byte offsets of the exchange region's fields (the layout of include/vq2_b200.h), each
+        256-byte aligned, and the region size."""
+        sizes = (("x", world * n_max * row_x), ("ids", world * n_max * k * 4), ("w", world * n_max * k * 4),
+                 ("comb", world * n_max * H * 4), ("dflag", world * EP_CTAS * 4), ("cflag", world * EP_CTAS * 4),
+                 ("epoch", 4))
+        out, o = {}, 0
+        for name, size in sizes:
+            out[name] = o
+            o = _up256(o + size)
+        out["bytes"] = o
+        return out
 
     def gathered(self, N: int):
         """Views of the gathered rows in source-rank order: x [W*N, H], ids i32 [W*N, k], w f32 [W*N, k]."""

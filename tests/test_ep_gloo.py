@@ -92,3 +92,19 @@ def test_failed_rank_surfaces_as_error_on_the_others():
     res = _run(2, fail_rank=1)
     assert res[1][1] == "error" and "injected" in res[1][2]
     assert res[0][1] == "error"
+
+
+def test_exchange_region_layout():
+    """Every field of the peer-exchange region is 256-byte aligned, in order, and sized for the
+    step's largest token count (the kernels rely on 16-byte alignment of every slot)."""
+    from vq2_vllm import ep
+    for world in (1, 2, 8):
+        for n_max in (1, 4, 32):
+            lay = ep.P2PExchange.layout(world, n_max, 4096, 8, 4096 * 2)
+            names = ["x", "ids", "w", "comb", "dflag", "cflag", "epoch"]
+            offs = [lay[n] for n in names] + [lay["bytes"]]
+            assert all(o % 256 == 0 for o in offs)
+            assert offs == sorted(offs)
+            assert lay["ids"] - lay["x"] >= world * n_max * 8192
+            assert lay["dflag"] - lay["comb"] >= world * n_max * 4096 * 4
+            assert lay["cflag"] - lay["dflag"] >= world * ep.EP_CTAS * 4

@@ -19,14 +19,8 @@ def test_dispatch_wait_times_out_and_context_survives():
     L.vq2_device_status(1)                        # clear
     H, k, N, W = 256, 8, 1, 2
     row_x = H * 2
-    # region layout of ep.P2PExchange for world 2, n_max 1
-    up = ep._up256
-    o = 0
-    off = {}
-    for name, size in (("x", W * N * row_x), ("ids", W * N * k * 4), ("w", W * N * k * 4), ("comb", W * N * H * 4),
-                       ("dflag", W * ep.EP_CTAS * 4), ("cflag", W * ep.EP_CTAS * 4), ("epoch", 4)):
-        off[name] = o
-        o = up(o + size)
+    off = ep.P2PExchange.layout(W, N, H, k, row_x)
+    o = off["bytes"]
     p = ctypes.c_void_p()
     _lib.check(L.vq2_ep_alloc(o, ctypes.byref(p)), "vq2_ep_alloc")
     base = p.value
