@@ -4,21 +4,22 @@
 // Two persistent kernels, one CTA per SM, chained with programmatic dependent launch:
 //   gateup: part[m, s] = (<W_gate,e[i], Hx_n>, <W_up,e[i], Hx_n>) over K-slice s (fp32 scratch)
 //   down:   out[n, h] += w_m * <W_down,e[h], H·(silu(sum_s gate) * sum_s up)>  (fp32 red.add)
-// for every (token n, slot j) pair m routed to expert e. Pairs are grouped by expert so each
-// expert's index planes stream from HBM once per group of up to DEC_TT tokens.
+// for every (token n, slot j) pair m routed to expert e. Every CTA builds the same plan: one unit
+// per pair, units ordered by expert (a pair's rank among the pairs ordered by (expert, pair)); the
+// flattened (unit, row) space is split evenly over the CTAs.
 //
 // Per CTA: a producer warp streams contiguous row chunks (lo / hi / scale planes) into a ring
-// of shared-memory stages with 1-D bulk async copies (TMA engine) and mbarriers; consumer warps
-// decode them. Lane l of a warp owns one 64-wide group of a row (a warp covers a 32-group
-// K-slice; rows wider than 2048 are split over KH warps): one 16-byte lo load, one 4-byte hi load
-// and one fp16 scale per group. A warp decodes several rows at once (independent chains) and
-// reduces their partial sums together with a halving shuffle reduction. The 1024x4 fp16 codebook
-// is replicated 16x in shared memory so that lane l reads only from bank pair (l mod 16): a
-// half-warp's 8-byte gathers are conflict-free. The Hadamard rotation of the activation is an
-// in-register 64-point FWHT per lane. Activations are held as fp16, scaled by a power of two
-// chosen from the slice max and the codebook max so that no half2 partial can overflow; a
-// group's 16 codebook-vector x activation products accumulate in packed half2 FMAs, and groups
-// combine in fp32 with their scale.
+// of shared-memory stages with 1-D bulk async copies (TMA engine, L2 evict-first) and mbarriers;
+// 16 consumer warps decode them. Lane l of a warp owns one 64-wide group of a row (a warp covers a
+// 32-group K-slice; rows wider than 2048 are split over KH warps): one 16-byte lo load, one 4-byte
+// hi load and one fp16 scale per group. A warp decodes one or more rows per pass (independent
+// chains) and reduces their partial sums together with a halving shuffle reduction. The 1024x4
+// fp16 codebook is replicated 16x in shared memory so that lane l reads only from bank pair
+// (l mod 16): a half-warp's 8-byte gathers are conflict-free. The activation of a unit is staged
+// once per CTA: each 64-group is rotated by a warp-shuffle FWHT (the Hadamard), scaled by a power
+// of two chosen from the group max and the codebook max so that no half2 partial can overflow,
+// and stored as half2 in conflict-free padded rows; a group's 16 codebook-vector x activation
+// products accumulate in packed half2 FMAs, and groups combine in fp32 with their scales.
 #include <cstddef>
 #include "vq2_common.cuh"
 
