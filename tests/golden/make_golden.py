@@ -1,8 +1,9 @@
 """Generate the golden fixtures by running the REFERENCE's own Python code on the CPU.
 
-Run in a container that has the reference checkout (default ``/root/reference``, override with
-``VQ2_REFERENCE``); the fixtures it writes (``tests/golden/*.npz``) are committed so the tests
-never need the reference at run time.
+Run where a checkout of the reference is available and name it:
+``python tests/golden/make_golden.py <reference checkout>`` (or set ``VQ2_REFERENCE``); the
+fixtures it writes (``tests/golden/*.npz``) are committed so the tests never need the reference at
+run time.
 
 The reference modules are imported from ``vq2_vllm/kernels`` with two shims:
   * ``vq2_kernel.py:129`` allocates a 384 MB flush buffer on "cuda" at import; that one
@@ -24,7 +25,9 @@ import torch
 os.environ["TRITON_INTERPRET"] = "1"
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.dirname(os.path.dirname(HERE))
-REF = os.environ.get("VQ2_REFERENCE", "/root/reference")
+REF = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("VQ2_REFERENCE", "")
+if not os.path.isdir(os.path.join(REF, "vq2_vllm", "kernels")):
+    sys.exit("usage: make_golden.py <reference checkout> (or VQ2_REFERENCE=<checkout>)")
 sys.path.insert(0, os.path.join(REF, "vq2_vllm", "kernels"))
 sys.path.insert(0, os.path.join(REPO, "deepseek-v4-flash-2bit-gb10_b200"))
 
