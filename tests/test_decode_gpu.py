@@ -97,3 +97,20 @@ def test_many_calls_back_to_back(big_layer):
     torch.cuda.synchronize()
     for o in outs[::7]:
         assert torch_ref.rel_l2(o, ref) < TOL
+
+
+def test_properties_full_size(big_layer):
+    """Size-independent properties at the full config-1 layer: the output is linear in the
+    routing weights and invariant to the order of a token's top-k slots."""
+    from vq2_vllm import synth
+    N = 3
+    x = synth.make_tokens(N, 4096, seed=61, device="cuda")
+    ids, w1 = synth.route_softmax_topk(x, 256, 8, w_std=0.02, seed=62)
+    w2 = torch.rand(N, 8, device="cuda", generator=torch.Generator(device="cuda").manual_seed(63))
+    f = lambda i, w: _moe()(x, i, w, *synth.layer_args(big_layer))
+    lhs = f(ids, 0.7 * w1 - 1.3 * w2)
+    rhs = 0.7 * f(ids, w1) - 1.3 * f(ids, w2)
+    assert torch_ref.rel_l2(lhs, rhs) < 1e-5
+    perm = torch.stack([torch.randperm(8, generator=torch.Generator().manual_seed(64 + n)) for n in range(N)]).cuda()
+    got = f(ids.gather(1, perm), w1.gather(1, perm))
+    assert torch_ref.rel_l2(got, f(ids, w1)) < 1e-5

@@ -74,3 +74,16 @@ def test_decode_entry_routes_large_batches_to_grouped(small):
     ids, tw = synth.route_zipf(N, 8, 2, seed=12, device="cuda")
     out = vq2_moe_fused_10b(x, ids, tw, *synth.layer_args(small))
     assert torch_ref.rel_l2(out, torch_ref.moe_ref(x, ids, tw, small)) < TOL
+
+
+def test_prefill_fp8_linear_in_routing_weights():
+    """The fp8 prefill output is linear in the routing weights (they scale the down epilogue)."""
+    from oracle import torch_ref
+    from vq2_vllm import synth
+    from vq2_vllm.kernels.ds4_vq2_cuda import vq2_moe_grouped_wmma
+    L = synth.make_layer(16, 4096, 2048, seed=71, device="cuda")
+    x = synth.make_tokens(300, 4096, seed=72, device="cuda")
+    ids, w1 = synth.route_zipf(300, 16, 8, seed=73, device="cuda")
+    w2 = torch.rand_like(w1)
+    f = lambda w: vq2_moe_grouped_wmma(x, ids, w, *synth.layer_args(L), precision="fp8")
+    assert torch_ref.rel_l2(f(2.0 * w1 + 0.5 * w2), 2.0 * f(w1) + 0.5 * f(w2)) < 1e-5
