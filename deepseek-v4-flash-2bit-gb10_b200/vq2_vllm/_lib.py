@@ -99,10 +99,14 @@ def ptr(t):
     return None if t is None else t.data_ptr()
 
 
-def require_cuda(*ts):
+def require_cuda(*ts, device: int = -1):
+    """Every tensor is a CUDA tensor (there is no CPU path) and, with ``device`` >= 0, on that
+    device (a tensor on another GPU would hand the kernels a foreign pointer)."""
     for t in ts:
         if not t.is_cuda:
             raise RuntimeError("vq2: all tensors must be CUDA tensors (no CPU path)")
+        if device >= 0 and t.get_device() != device:
+            raise RuntimeError(f"vq2: tensors on cuda:{t.get_device()} and cuda:{device}; all must share one device")
 
 
 _WS = {}

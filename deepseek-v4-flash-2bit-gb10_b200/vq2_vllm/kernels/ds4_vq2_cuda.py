@@ -33,6 +33,10 @@ def vq2_moe_grouped_wmma(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sd
         raise ValueError("vq2: only group=64 is supported")
     if precision is None:
         precision = "fp8" if os.environ.get("VQ2_FP8_PREFILL", "1") == "1" else "f16"
+    if x.is_cuda and x.get_device() != torch.cuda.current_device():   # the library launches on the current device
+        with torch.cuda.device(x.device):
+            return vq2_moe_grouped_wmma(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, group=group,
+                                        expert_base=expert_base, precision=precision)
     t = _prep(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn)
     N = x.shape[0]
     out = torch.empty(N, x.shape[1], device=x.device, dtype=torch.float32)

@@ -17,7 +17,7 @@ _WS = {}
 def router_topk(x: torch.Tensor, w_r: torch.Tensor, k: int):
     """x [N, H] (bf16 / fp16 / fp32), w_r [H, E] bf16 -> (topk_ids int32 [N, k], topk_w fp32 [N, k]).
     Ids by probability descending (lower index first on ties)."""
-    _lib.require_cuda(x, w_r)
+    _lib.require_cuda(x, w_r, device=x.get_device() if x.is_cuda else -1)
     if w_r.dtype != torch.bfloat16 or w_r.dim() != 2 or x.dim() != 2 or x.shape[1] != w_r.shape[0]:
         raise ValueError("vq2 router: x [N, H] and bf16 w_r [H, E] expected")
     x = x.contiguous()

@@ -77,7 +77,7 @@ def _prep(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn):
     for i, (t, d) in enumerate(zip(ws, want)):
         if not _ok(t, d):
             ws[i] = t.to(d).contiguous()
-    _lib.require_cuda(topk_ids, topk_w, *ws)
+    _lib.require_cuda(topk_ids, topk_w, *ws, device=x.get_device())
     return [x, topk_ids, topk_w] + ws
 
 
@@ -88,6 +88,9 @@ def vq2_moe_fused_10b(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, 
     parallelism). Batches above the decode kernel's pair limit go to the grouped GEMM path."""
     if group != 64:
         raise ValueError("vq2: only group=64 is supported")
+    if x.is_cuda and x.get_device() != torch.cuda.current_device():   # the library launches on the current device
+        with torch.cuda.device(x.device):
+            return vq2_moe_fused_10b(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, group, expert_base)
     N = x.shape[0]
     k = topk_ids.shape[1]
     if N * k > _lib.DECODE_MAX_PAIRS:
