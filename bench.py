@@ -205,6 +205,59 @@ def time_router(dev, reps=200):
     return res
 
 
+def time_pack(dev):
+    """The VQ packer (offline) on 8 experts of the config-1 gate/up tensor (8 x 4096 x 4096 bf16,
+    33.5M sub-vectors): the whole mirrored pack_vq2_experts_10b call (sample draw, k-means on
+    200k samples for 12 iterations, assignment with planes, scales and dq) and the assignment
+    kernel alone, beside the reference's assignment step as torch ops (torch.cdist + argmin over
+    1M-row chunks, vq2_kernel.py:59-62) on the same normalised sub-vectors. ms, device events."""
+    from vq2_vllm import _lib
+    from vq2_vllm.kernels.vq2_pack import pack_vq2_experts_10b
+    g = torch.Generator(device=dev).manual_seed(77)
+    W3 = (torch.randn(8, 2 * I, H, generator=g, device=dev) * 0.02).bfloat16()
+    rows, D = 8 * 2 * I, H
+    nvec = rows * D // 4
+
+    def ev(f, reps=2):
+        f()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        s.record()
+        for _ in range(reps):
+            f()
+        e.record()
+        e.synchronize()
+        return s.elapsed_time(e) / reps
+
+    res = {}
+    out = {}
+    res["pack_call_ms"] = ev(lambda: out.update(r=pack_vq2_experts_10b(W3, iters=12)))
+    C = out["r"][0]
+    lo = torch.empty(nvec, dtype=torch.uint8, device=dev)
+    hi = torch.empty(nvec // 4, dtype=torch.uint8, device=dev)
+    sc = torch.empty(rows * D // 64, dtype=torch.float32, device=dev)
+    L = _lib.lib()
+    res["assign_kernel_ms"] = ev(lambda: _lib.check(L.vq2_pack_assign(
+        W3.data_ptr(), 0, rows, D, C.data_ptr(), C.shape[0], lo.data_ptr(), hi.data_ptr(), None, sc.data_ptr(), None,
+        _lib.stream_ptr(dev)), "vq2_pack_assign"))
+    from vq2_vllm.kernels.vq2_kernel import _hadamard
+    Hm = _hadamard(64).to(dev)
+    wn = W3.view(-1, 64).float() @ Hm
+    wn = (wn / wn.abs().amax(1, keepdim=True).clamp_min(1e-8)).view(-1, 4)
+    idx = torch.empty(nvec, dtype=torch.long, device=dev)
+
+    def ref_assign():
+        for i in range(0, nvec, 1 << 20):
+            idx[i:i + (1 << 20)] = torch.cdist(wn[i:i + (1 << 20)], C).argmin(1)
+    res["reference_ops_assign_ms"] = ev(ref_assign, reps=1)
+    res["same_ids_as_reference_ops"] = float((idx == (lo.long() | ((hi.long().repeat_interleave(4) >> (
+        (torch.arange(nvec, device=dev) & 3) * 2)) & 3) << 8)).float().mean().item())
+    res["Gsubvectors_per_s_assign"] = nvec / (res["assign_kernel_ms"] * 1e-3) / 1e9
+    del W3, wn, idx, out
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -347,6 +400,10 @@ def run_ours(args, rank, world):
 
     prefill = time_prefill(layers, dev, args)
     router = time_router(dev)
+    try:
+        pack = time_pack(dev)
+    except Exception as ex:  # an offline-tool figure must not cost the headline line
+        pack = {"error": f"{type(ex).__name__}: {ex}"[:300]}
 
     cpu_v, cpu_sample = (None, None)
     cpu_pf, cpu_pf_sample = (None, None)
@@ -362,6 +419,7 @@ def run_ours(args, rank, world):
                        "topk": K, "batch": 1, "l2": f"{nlayers} layers cycled per step (8.8 GB > L2)",
                        "distinct_experts_per_step": u1},
             "router": {**router, "workload": "top-8 of softmax(x @ W_r), x [1, 4096], W_r [4096, 256], graph replay"},
+            "pack": {**pack, "workload": "VQ packer on 8 experts of the gate/up tensor, 8 x 4096 x 4096 bf16"},
             "decode_graph": {"us_per_token": ms_graph * 1e3,
                              "how": "the same batch-1 steps replayed from CUDA graphs"},
             "decode_b3": {"us_per_token": ms3 * 1e3 / 3, "us_per_layer_call": ms3 * 1e3, "distinct_experts": u3,

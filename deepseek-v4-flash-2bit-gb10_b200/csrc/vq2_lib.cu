@@ -6,3 +6,4 @@
 #include "prefill.cu"
 #include "ep_p2p.cu"
 #include "router.cu"
+#include "pack.cu"

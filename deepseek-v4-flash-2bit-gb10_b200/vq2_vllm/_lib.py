@@ -60,6 +60,14 @@ _SIGS = {
     "vq2_router_topk": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                        ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                        ctypes.c_size_t, ctypes.c_void_p]),
+    "vq2_pack_gather": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_int, ctypes.c_void_p,
+                                       ctypes.c_longlong, ctypes.c_void_p, ctypes.c_void_p]),
+    "vq2_kmeans_workspace_size": (ctypes.c_size_t, [ctypes.c_int]),
+    "vq2_kmeans": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_longlong, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                  ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "vq2_pack_assign": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_int, ctypes.c_void_p,
+                                       ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                       ctypes.c_void_p, ctypes.c_void_p]),
     "vq2_device_status": (ctypes.c_int, [ctypes.c_int]),
     "vq2_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "vq2_version": (ctypes.c_int, []),

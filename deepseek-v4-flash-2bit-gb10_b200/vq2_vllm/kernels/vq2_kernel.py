@@ -108,3 +108,8 @@ def vq2_moe_fused_10b(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, 
     if rc:
         _lib.check(rc, "vq2_moe_fused_10b")
     return out
+
+
+# The packer lives beside the decode entry in the reference module (vq2_kernel.py:37-72, :160-167,
+# :501-505); its implementation here is kernels/vq2_pack.py.
+from .vq2_pack import pack_vq2, pack_vq2_experts, pack_vq2_experts_10b  # noqa: E402,F401

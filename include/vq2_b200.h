@@ -149,6 +149,28 @@ size_t vq2_router_workspace_size(int N, int H, int E);
 int vq2_router_topk(const void* x, int x_dtype, const void* w_r, int N, int H, int E, int k,
                     int32_t* topk_ids, float* topk_w, void* workspace, size_t ws_bytes, void* stream);
 
+/* ---- VQ packer (offline quantisation into the format above; not on the serving path). Replaces
+   the k-means packer vq2_kernel.pack_vq2 (reference vq2_vllm/kernels/vq2_kernel.py:37-72). W is
+   [rows][D] of VQ2_DT_* (columns zero-padded to ng = ceil(D/64) groups); sub-vectors are numbered
+   flat over rows x groups x 16 (sub-vector v: group v>>4, columns 4*(v&15)..+3 of the rotated
+   group). Rotation is the group Hadamard (fp32 butterfly), scale s = max(|group|, 1e-8), values
+   normalised by s; distances ((d0^2+d1^2)+d2^2)+d3^2 with each operation rounded separately, lowest
+   index on ties; k <= 1024. */
+/* out f32 [n][4] (16-byte aligned): the normalised sub-vectors vec_idx[0..n). */
+int vq2_pack_gather(const void* W, int w_dtype, long long rows, int D, const long long* vec_idx, long long n,
+                    float* out, void* stream);
+/* `iters` Lloyd iterations over samp f32 [n][4] starting from C f32 [k][4] (updated in place): each
+   centroid with members becomes their mean (members summed as int64 fixed point, value x 2^40
+   rounded to nearest even; mean = (double)sum * 2^-40 / count rounded to f32); empty ones stay. */
+size_t vq2_kmeans_workspace_size(int k);
+int vq2_kmeans(const float* samp, long long n, float* C, int k, int iters, void* workspace, size_t ws_bytes,
+               void* stream);
+/* Nearest centroid of every sub-vector of W. Outputs (each optional except scale):
+   lo u8 [rows*ng*16] and hi u8 [rows*ng*4] (the 10-bit planes, both or neither, lo 4-byte aligned),
+   idx i16 [rows*ng*16] (8-byte aligned), scale f32 [rows*ng], dq f32 [rows][D] = (C[id] * s) @ H64. */
+int vq2_pack_assign(const void* W, int w_dtype, long long rows, int D, const float* C, int k, uint8_t* lo,
+                    uint8_t* hi, int16_t* idx, float* scale, float* dq, void* stream);
+
 int vq2_device_status(int reset);
 const char* vq2_strerror(int code);
 int vq2_version(void);

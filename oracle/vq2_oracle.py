@@ -211,3 +211,88 @@ def rel_l2(a, b) -> float:
     a = np.asarray(a, dtype=np.float64)
     b = np.asarray(b, dtype=np.float64)
     return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+# ----------------------------------------------------------------------------- VQ packer
+# Restates the k-means packer of the reference, vq2_kernel.pack_vq2
+# (vq2_vllm/kernels/vq2_kernel.py:37-72), with every fp32 operation in the order the B200 kernels
+# use, so results compare bit for bit: the group rotation is the 64-point butterfly (strides
+# 32, 16, ..., 1, then x 1/8) rather than a matmul; distances are ((d0^2+d1^2)+d2^2)+d3^2; member
+# sums are int64 fixed point (x 2^40, rounded to nearest even), means (double)sum * 2^-40 / count.
+PACK_FIX = 2.0 ** 40
+
+
+def fwht64_f32(x: np.ndarray) -> np.ndarray:
+    """Rows of 64 fp32 values -> x @ H64 by the butterfly (pair i with i + len, len = 32 .. 1:
+    (lo + hi, lo - hi)), then x 1/8; each step rounded to fp32 (vq2_kernel.py:46 rotates with
+    W @ H, the same transform)."""
+    x = np.asarray(x, np.float32).reshape(-1, 64).copy()
+    n = x.shape[0]
+    ln = 32
+    while ln >= 1:
+        r = x.reshape(n, 64 // (2 * ln), 2, ln)
+        lo, hi = r[:, :, 0, :].copy(), r[:, :, 1, :].copy()
+        r[:, :, 0, :] = lo + hi
+        r[:, :, 1, :] = lo - hi
+        x = r.reshape(n, 64)
+        ln //= 2
+    return (x * np.float32(0.125)).astype(np.float32)
+
+
+def pack_rotate(W: np.ndarray):
+    """W [rows, D] -> (Wn [rows*ng, 64] normalised rotated groups, scale f32 [rows*ng]);
+    zero-padded to a group multiple; s = max(|group|, 1e-8) (vq2_kernel.py:41-49)."""
+    W = np.asarray(W, np.float32)
+    rows, D = W.shape
+    pad = (-D) % GROUP
+    if pad:
+        W = np.concatenate([W, np.zeros((rows, pad), np.float32)], 1)
+    g = fwht64_f32(W.reshape(-1, GROUP))
+    s = np.maximum(np.abs(g).max(1), np.float32(1e-8)).astype(np.float32)
+    return (g / s[:, None]).astype(np.float32), s
+
+
+def pack_dist(x: np.ndarray, C: np.ndarray) -> np.ndarray:
+    """[n, 4] x [k, 4] -> [n, k] squared distances in the kernels' fp32 order."""
+    d = (x[:, None, :] - C[None, :, :]).astype(np.float32)
+    q = (d * d).astype(np.float32)
+    return ((q[..., 0] + q[..., 1]) + q[..., 2]) + q[..., 3]
+
+
+def pack_nearest(x: np.ndarray, C: np.ndarray, chunk: int = 4096) -> np.ndarray:
+    """Nearest centroid, lowest index on ties (vq2_kernel.py:54 and :62, argmin of distances)."""
+    out = np.empty(x.shape[0], np.int64)
+    for i in range(0, x.shape[0], chunk):
+        out[i:i + chunk] = pack_dist(x[i:i + chunk], C).argmin(1)
+    return out
+
+
+def pack_kmeans(samp: np.ndarray, C: np.ndarray, iters: int) -> np.ndarray:
+    """Lloyd iterations: assign, then each centroid with members = their mean, others kept
+    (vq2_kernel.py:53-58)."""
+    C = np.asarray(C, np.float32).copy()
+    k = C.shape[0]
+    q = np.rint(samp.astype(np.float64) * PACK_FIX).astype(np.int64)
+    for _ in range(iters):
+        a = pack_nearest(samp, C)
+        sums = np.zeros((k, 4), np.int64)
+        np.add.at(sums, a, q)
+        cnt = np.bincount(a, minlength=k)
+        nz = cnt > 0
+        C[nz] = ((sums[nz].astype(np.float64) * 2.0 ** -40) / cnt[nz, None]).astype(np.float32)
+    return C
+
+
+def pack_from_sample(W: np.ndarray, si: np.ndarray, init: np.ndarray, iters: int):
+    """The whole packer for a given sample (sub-vector indices si, initial codebook = sample rows
+    init): returns (C, idx [rows, nsub], scale [rows, ng], dq [rows, D]) (vq2_kernel.py:37-65)."""
+    rows, D = np.asarray(W).shape
+    wn, s = pack_rotate(W)
+    vec = wn.reshape(-1, VDIM)
+    samp = vec[np.asarray(si)]
+    C = pack_kmeans(samp, samp[np.asarray(init)], iters)
+    idx = pack_nearest(vec, C)
+    recon = (C[idx].reshape(-1, GROUP) * s[:, None]).astype(np.float32)
+    ng = wn.shape[0] // rows
+    dq = fwht64_f32(recon).reshape(rows, ng * GROUP)[:, :D]
+    return C, idx.reshape(rows, -1), s.reshape(rows, ng), dq

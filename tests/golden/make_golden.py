@@ -15,6 +15,11 @@ Fixtures:
   config0.npz   the tiny config-0 layer + routing + reference outputs (decode Triton path,
                 fp32 dequant+matmul MoE, Hadamard, moe_align (torch + fast), fp8 row quant)
   align.npz     moe_align outputs of the reference for several (N, k, E, BM) cases
+  pack.npz      the reference's k-means packer (pack_vq2_experts_10b, pack_vq2 with padding and
+                k <= 256) on small weights, with the sample it drew (its own torch.manual_seed(0)
+                draw, repeated here on the same CPU generator)
+
+Extra arguments after the checkout name the fixtures to write (config0, align, pack); default all.
 """
 import os
 import sys
@@ -91,7 +96,39 @@ def ref_dense_moe(x, ids, w, layer):
     return out
 
 
+def draw_sample(nvec, k):
+    """The reference's sample draw (vq2_kernel.py:50-52) on the CPU generator."""
+    torch.manual_seed(0)
+    si = torch.randint(0, nvec, (min(nvec, 200000),))
+    return si, torch.randperm(si.shape[0])[:k]
+
+
+def main_pack():
+    g = torch.Generator().manual_seed(11)
+    W3 = torch.randn(2, 48, 256, generator=g) * 0.02
+    W3[:, :, 5] *= 8.0                                    # an outlier column, as trained weights have
+    C, lo, hi, sc, dq = rk.pack_vq2_experts_10b(W3, k=1024, iters=12)
+    si, init = draw_sample(2 * 48 * 4 * 16, 1024)
+    W2 = torch.randn(40, 200, generator=g).to(torch.bfloat16)
+    C2, idx2, sc2, dq2, inn2, pad2 = rk.pack_vq2(W2, k=256, iters=6)
+    si2, init2 = draw_sample(40 * 4 * 16, 256)
+    print(f"pack: 10b case rel-L2 {((dq - W3).norm() / W3.norm()).item():.3f}, padded case "
+          f"{((dq2 - W2.float()).norm() / W2.float().norm()).item():.3f} (inn {inn2}, pad {pad2}, idx {idx2.dtype})")
+    np.savez_compressed(
+        os.path.join(HERE, "pack.npz"),
+        a_W=W3.numpy(), a_C=C.numpy(), a_lo=lo.numpy(), a_hi=hi.numpy(), a_sc=sc.numpy(), a_dq=dq.numpy(),
+        a_si=si.numpy(), a_init=init.numpy(), a_meta=np.array([1024, 12]),
+        b_W_bf16_bits=W2.view(torch.int16).numpy(), b_C=C2.numpy(), b_idx=idx2.numpy(), b_sc=sc2.numpy(),
+        b_dq=dq2.numpy(), b_si=si2.numpy(), b_init=init2.numpy(), b_meta=np.array([256, 6, inn2, pad2]))
+    print("wrote", os.path.join(HERE, "pack.npz"))
+
+
 def main():
+    which = set(sys.argv[2:]) or {"config0", "align", "pack"}
+    if "pack" in which:
+        main_pack()
+    if not which & {"config0", "align"}:
+        return
     E, H, I, N, K = 8, 512, 256, 4, 2
     layer = synth.make_layer(E, H, I, seed=0)
     x = synth.make_tokens(N, H, seed=1)

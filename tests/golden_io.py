@@ -26,3 +26,13 @@ def load_align():
     n = len([k for k in z if k.endswith("_ids")])
     return [(z[f"c{i}_ids"], int(z[f"c{i}_meta"][0]), int(z[f"c{i}_meta"][1]), int(z[f"c{i}_meta"][2]),
              z[f"c{i}_st"], z[f"c{i}_ss"], z[f"c{i}_val"], z[f"c{i}_be"]) for i in range(n)]
+
+
+def load_pack():
+    """The reference packer's fixtures: case a (pack_vq2_experts_10b, fp32 W [2, 48, 256], k=1024,
+    12 iterations) and case b (pack_vq2, bf16 W [40, 200] padded to 256, k=256, 6 iterations),
+    each with the sample the reference drew (si) and its initial-codebook positions (init)."""
+    z = dict(np.load(os.path.join(GOLDEN, "pack.npz")))
+    bits = z["b_W_bf16_bits"].astype(np.uint16).astype(np.uint32) << 16
+    z["b_W"] = bits.view(np.float32)
+    return z

@@ -43,3 +43,23 @@ def test_cpu_tensors_are_rejected():
         moe_align(ids, 4, 64)
     with pytest.raises(RuntimeError, match="no CPU path"):
         router_topk(x, torch.zeros(128, 4, dtype=torch.bfloat16), 2)
+
+
+def test_packer_rejects_bad_arguments_without_a_gpu():
+    """The packer's argument checks run on the host before any launch: the mirror raises on
+    unsupported formats and CPU tensors, the C ABI returns its error codes."""
+    from vq2_vllm import _lib
+    from vq2_vllm.kernels.vq2_kernel import pack_vq2
+    with pytest.raises(ValueError):
+        pack_vq2(torch.zeros(4, 64), k=2048)
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        pack_vq2(torch.zeros(4, 64), k=64)
+    L = _lib.lib()
+    fake = 1 << 20                                   # never dereferenced: every call below fails its checks
+    assert L.vq2_pack_assign(fake, 0, 4, 64, fake, 2000, None, None, None, fake, None, None) == 2   # k > 1024
+    assert L.vq2_pack_assign(fake, 0, 4, 64, fake + 4, 16, None, None, None, fake, None, None) == 3  # C unaligned
+    assert L.vq2_pack_assign(fake, 0, 4, 64, fake, 16, fake, None, None, fake, None, None) == 1   # lo without hi
+    assert L.vq2_pack_assign(fake, 7, 4, 64, fake, 16, None, None, None, fake, None, None) == 4   # dtype
+    assert L.vq2_kmeans(fake, 10, fake, 16, 3, None, 0, None) == 5                                # workspace
+    assert L.vq2_pack_gather(fake, 0, 4, 64, fake, 5, fake + 8, None) == 3                       # out unaligned
+    assert L.vq2_kmeans_workspace_size(1025) == 0

@@ -92,3 +92,30 @@ def test_torch_fp8_prefill_matches_numpy_oracle():
                                       torch.from_numpy(z["topk_w"]), tl)
     b = O.moe_prefill_fp8_ref(x, z["topk_ids"], z["topk_w"], _w(layer, "w13"), _w(layer, "w2"))
     assert O.rel_l2(a.numpy(), b) < 2e-3
+
+
+def test_packer_matches_reference():
+    """The oracle's packer restatement (exact-order butterfly rotation, fixed-point centroid sums)
+    against the reference's pack_vq2_experts_10b / pack_vq2 run on the same weights and sample:
+    identical assignments; codebook, scales and reconstruction equal to fp32 rounding."""
+    from golden_io import load_pack
+    z = load_pack()
+    W = z["a_W"].reshape(-1, 256)
+    C, idx, s, dq = O.pack_from_sample(W, z["a_si"], z["a_init"], int(z["a_meta"][1]))
+    assert np.array_equal(idx, O.unpack10(z["a_lo"], z["a_hi"]).reshape(idx.shape))
+    assert np.abs(C - z["a_C"]).max() <= 2e-6
+    assert np.abs(s - z["a_sc"].reshape(s.shape)).max() <= 2e-6 * np.abs(s).max()
+    assert O.rel_l2(dq, z["a_dq"].reshape(W.shape)) <= 1e-5
+    k, it, inn, pad = (int(v) for v in z["b_meta"])
+    C2, idx2, s2, dq2 = O.pack_from_sample(z["b_W"], z["b_si"], z["b_init"], it)
+    assert (inn, pad) == (200, 56) and C2.shape == (k, 4) and dq2.shape == (40, 200)
+    assert np.array_equal(idx2, z["b_idx"].astype(np.int64))
+    assert np.abs(C2 - z["b_C"]).max() <= 2e-6
+    assert np.abs(s2 - z["b_sc"]).max() <= 2e-6 * np.abs(s2).max()
+    assert O.rel_l2(dq2, z["b_dq"]) <= 1e-5
+
+
+def test_packer_butterfly_is_the_hadamard():
+    x = np.random.default_rng(0).standard_normal((9, 64)).astype(np.float32)
+    assert np.allclose(O.fwht64_f32(x), x @ O.hadamard(64), atol=2e-6)
+    assert np.allclose(O.fwht64_f32(O.fwht64_f32(x)), x, atol=2e-6)
