@@ -258,6 +258,44 @@ def time_pack(dev):
     return res
 
 
+def time_shared(dev, hbm):
+    """The config-1 shared expert (bf16 gate/up [4096, 4096], down [4096, 2048]) for batch 1 and
+    3: four copies of its weights (201 MB > L2) cycled, CUDA events around 40 calls; beside it the
+    same layer as torch bf16 ops (two cuBLAS GEMMs and silu * mul), cycled the same way."""
+    from vq2_vllm.kernels.shared_expert import shared_expert_fused
+    Is = I
+    g = torch.Generator(device=dev).manual_seed(31)
+    ws = [((torch.randn(2 * Is, H, generator=g, device=dev) * 0.02).bfloat16(),
+           (torch.randn(H, Is, generator=g, device=dev) * 0.02).bfloat16()) for _ in range(4)]
+    nbytes = (2 * Is * H + H * Is) * 2
+
+    def torch_ops(x, w13, w2):
+        h = torch.nn.functional.linear(x, w13)
+        return torch.nn.functional.linear(torch.nn.functional.silu(h[:, :Is]) * h[:, Is:], w2)
+
+    res = {"bytes_per_call": nbytes}
+    for N in (1, 3):
+        x = torch.randn(N, H, generator=g, device=dev).bfloat16()
+        for name, f in (("ours", lambda a, b: shared_expert_fused(x, a, b)), ("torch_ops", lambda a, b: torch_ops(x, a, b))):
+            for i in range(8):
+                f(*ws[i % 4])
+            torch.cuda.synchronize()
+            s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+            s.record()
+            for i in range(40):
+                f(*ws[i % 4])
+            e.record()
+            e.synchronize()
+            us = s.elapsed_time(e) * 1e3 / 40
+            res[f"{name}_us_b{N}"] = us
+            if name == "ours":
+                res[f"ours_GBps_b{N}"] = nbytes / (us * 1e-6) / 1e9
+                res[f"ours_frac_hbm_b{N}"] = nbytes / (us * 1e-6) / 1e9 / hbm
+    del ws
+    torch.cuda.empty_cache()
+    return res
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return
@@ -401,6 +439,10 @@ def run_ours(args, rank, world):
     prefill = time_prefill(layers, dev, args)
     router = time_router(dev)
     try:
+        shared = time_shared(dev, hbm)
+    except Exception as ex:  # a figure beside the path must not cost the headline line
+        shared = {"error": f"{type(ex).__name__}: {ex}"[:300]}
+    try:
         pack = time_pack(dev)
     except Exception as ex:  # an offline-tool figure must not cost the headline line
         pack = {"error": f"{type(ex).__name__}: {ex}"[:300]}
@@ -419,6 +461,7 @@ def run_ours(args, rank, world):
                        "topk": K, "batch": 1, "l2": f"{nlayers} layers cycled per step (8.8 GB > L2)",
                        "distinct_experts_per_step": u1},
             "router": {**router, "workload": "top-8 of softmax(x @ W_r), x [1, 4096], W_r [4096, 256], graph replay"},
+            "shared_expert": {**shared, "workload": "config1 shared expert, bf16 gate/up [4096, 4096] + down [4096, 2048], 4 weight copies cycled (> L2)"},
             "pack": {**pack, "workload": "VQ packer on 8 experts of the gate/up tensor, 8 x 4096 x 4096 bf16"},
             "decode_graph": {"us_per_token": ms_graph * 1e3,
                              "how": "the same batch-1 steps replayed from CUDA graphs"},

@@ -16,9 +16,10 @@
 //            additions does not matter; mean = (double)sum * 2^-40 / count, rounded to fp32.
 //   assign   each warp takes 8 consecutive groups (128 sub-vectors, flat over rows x groups):
 //            rotates and normalises them into shared memory, every lane finds the nearest
-//            centroid of 4 consecutive sub-vectors, and writes the lo plane (one word), the hi
-//            byte, the int16 ids, the group scales and, when asked, dq (C[id] * s through the
-//            same butterfly, which is its own inverse up to the 1/8 normalisation).
+//            centroid of 4 consecutive sub-vectors (two per packed f32x2 instruction), and
+//            writes the lo plane (one word), the hi byte, the int16 ids, the group scales and,
+//            when asked, dq (C[id] * s through the same butterfly, which is its own inverse up
+//            to the 1/8 normalisation).
 // Distances are ((d0^2 + d1^2) + d2^2) + d3^2 with d = x - c, each operation rounded separately
 // (no contraction); the lowest index wins a tie. The reference uses torch.cdist, whose rounding
 // differs, so near-ties can resolve differently there.
@@ -130,15 +131,55 @@ __global__ void kmeans_update_kernel(float* __restrict__ C, int k, unsigned long
   cnt[c] = 0u;
 }
 
+// Two sub-vectors per packed fp32x2 instruction (Blackwell add/sub/mul.rn.f32x2: each half
+// rounded to nearest on its own, so the result equals the scalar sequence bit for bit).
+__device__ __forceinline__ unsigned long long f2pack(float lo, float hi) {
+  unsigned long long d;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(d) : "f"(lo), "f"(hi));
+  return d;
+}
+__device__ __forceinline__ void f2unpack(unsigned long long v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ unsigned long long f2sub(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("sub.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ unsigned long long f2mul(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ unsigned long long f2add(unsigned long long a, unsigned long long b) {
+  unsigned long long d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+
+// Shared memory of the assign kernel: the codebook with every component doubled, centroid c as
+// {x, x, y, y}, {z, z, w, w} (so one 16-byte load gives two packed operands), then the per-warp
+// staging of 8 rotated groups and their scales.
+constexpr size_t PK_ASSIGN_SMEM = (size_t)PK_MAX_K * 32 + (size_t)(PK_THREADS / 32) * PK_GROUPS_PER_WARP * 64 * 4 +
+                                  (size_t)(PK_THREADS / 32) * PK_GROUPS_PER_WARP * 4;
+
 __global__ void __launch_bounds__(PK_THREADS) pack_assign_kernel(const void* __restrict__ W, int dt, int D, int ng,
                                                                  long long ngroups, const float4* __restrict__ C,
                                                                  int k, uint8_t* __restrict__ lo,
                                                                  uint8_t* __restrict__ hi, int16_t* __restrict__ idx,
                                                                  float* __restrict__ scale, float* __restrict__ dq) {
-  __shared__ float4 cs[PK_MAX_K];
-  __shared__ __align__(16) float stage[PK_THREADS / 32][PK_GROUPS_PER_WARP * 64];
-  __shared__ float gsc[PK_THREADS / 32][PK_GROUPS_PER_WARP];
-  pk_load_codebook(cs, C, k);
+  extern __shared__ __align__(16) unsigned char pk_smem[];
+  ulonglong2* cs2 = reinterpret_cast<ulonglong2*>(pk_smem);                       // [k][2]
+  float (*stage)[PK_GROUPS_PER_WARP * 64] =
+      reinterpret_cast<float (*)[PK_GROUPS_PER_WARP * 64]>(pk_smem + (size_t)PK_MAX_K * 32);
+  float (*gsc)[PK_GROUPS_PER_WARP] = reinterpret_cast<float (*)[PK_GROUPS_PER_WARP]>(
+      pk_smem + (size_t)PK_MAX_K * 32 + (size_t)(PK_THREADS / 32) * PK_GROUPS_PER_WARP * 64 * 4);
+  for (int c = threadIdx.x; c < k; c += blockDim.x) {
+    const float4 v = C[c];
+    cs2[2 * c] = make_ulonglong2(f2pack(v.x, v.x), f2pack(v.y, v.y));
+    cs2[2 * c + 1] = make_ulonglong2(f2pack(v.z, v.z), f2pack(v.w, v.w));
+  }
+  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   float* st = stage[warp];
   const long long ntiles = (ngroups + PK_GROUPS_PER_WARP - 1) / PK_GROUPS_PER_WARP;
@@ -154,19 +195,35 @@ __global__ void __launch_bounds__(PK_THREADS) pack_assign_kernel(const void* __r
       if (lane == 0) gsc[warp][q] = s;
     }
     __syncwarp();
-    // lane owns sub-vectors 4*lane .. 4*lane+3 of the tile: floats 16*lane .. 16*lane+15
+    // lane owns sub-vectors 4*lane .. 4*lane+3 of the tile: floats 16*lane .. 16*lane+15;
+    // packed as pairs (0, 1) and (2, 3), one 64-bit register per component
     float4 x[4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) x[i] = *reinterpret_cast<const float4*>(st + 16 * lane + 4 * i);
+    unsigned long long X[2][4];
+#pragma unroll
+    for (int p = 0; p < 2; ++p) {
+      X[p][0] = f2pack(x[2 * p].x, x[2 * p + 1].x);
+      X[p][1] = f2pack(x[2 * p].y, x[2 * p + 1].y);
+      X[p][2] = f2pack(x[2 * p].z, x[2 * p + 1].z);
+      X[p][3] = f2pack(x[2 * p].w, x[2 * p + 1].w);
+    }
     float best[4] = {INFINITY, INFINITY, INFINITY, INFINITY};
     int bi[4] = {0, 0, 0, 0};
 #pragma unroll 4
     for (int c = 0; c < k; ++c) {
-      const float4 cv = cs[c];
+      const ulonglong2 A = cs2[2 * c], B = cs2[2 * c + 1];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float d = pk_dist(x[i], cv);
-        if (d < best[i]) { best[i] = d; bi[i] = c; }
+      for (int p = 0; p < 2; ++p) {
+        const unsigned long long d0 = f2sub(X[p][0], A.x), d1 = f2sub(X[p][1], A.y);
+        const unsigned long long d2 = f2sub(X[p][2], B.x), d3 = f2sub(X[p][3], B.y);
+        unsigned long long sacc = f2add(f2mul(d0, d0), f2mul(d1, d1));
+        sacc = f2add(sacc, f2mul(d2, d2));
+        sacc = f2add(sacc, f2mul(d3, d3));
+        float s0, s1;
+        f2unpack(sacc, s0, s1);
+        if (s0 < best[2 * p]) { best[2 * p] = s0; bi[2 * p] = c; }
+        if (s1 < best[2 * p + 1]) { best[2 * p + 1] = s1; bi[2 * p + 1] = c; }
       }
     }
     const int q = lane >> 2;                       // this lane's group within the tile
@@ -190,7 +247,7 @@ __global__ void __launch_bounds__(PK_THREADS) pack_assign_kernel(const void* __r
       __syncwarp();
 #pragma unroll
       for (int i = 0; i < 4; ++i) {
-        const float4 cv = cs[bi[i]];
+        const float4 cv = C[bi[i]];
         *reinterpret_cast<float4*>(st + 16 * lane + 4 * i) =
             make_float4(__fmul_rn(cv.x, s), __fmul_rn(cv.y, s), __fmul_rn(cv.z, s), __fmul_rn(cv.w, s));
       }
@@ -276,7 +333,10 @@ extern "C" int vq2_pack_assign(const void* W, int w_dtype, long long rows, int D
   const int ng = (D + 63) / 64;
   const long long ngroups = rows * ng;
   const long long tiles = (ngroups + PK_GROUPS_PER_WARP - 1) / PK_GROUPS_PER_WARP;
-  pack_assign_kernel<<<pk_grid(tiles), PK_THREADS, 0, (cudaStream_t)stream>>>(W, w_dtype, D, ng, ngroups,
+  if (cudaFuncSetAttribute(pack_assign_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PK_ASSIGN_SMEM) !=
+      cudaSuccess)
+    return VQ2_ERR_CUDA;
+  pack_assign_kernel<<<pk_grid(tiles), PK_THREADS, PK_ASSIGN_SMEM, (cudaStream_t)stream>>>(W, w_dtype, D, ng, ngroups,
                                                                               (const float4*)C, k, lo, hi, idx,
                                                                               scale, dq);
   return cudaGetLastError() == cudaSuccess ? VQ2_OK : VQ2_ERR_CUDA;

@@ -1,0 +1,232 @@
+// K6 — shared expert of the decode step: a dense bf16 SiLU-gated MLP beside the routed experts
+//   out[n] (+)= W2 . (silu(Wg . x[n]) * (Wu . x[n]))
+// with w13 = [Wg; Wu] bf16 [2*Is][H] and w2 bf16 [H][Is]. In the model this plugin serves, vLLM
+// runs the shared expert beside the MoE method (the method's `apply` receives and ignores it,
+// reference vq2_vllm/__init__.py:197-198); this is the same layer as two HBM-streaming GEMV
+// kernels chained by programmatic dependent launch, so a decode step can add it onto the routed
+// output on the same stream without a host round trip:
+//   gateup  issues the first weight chunks of its rows, waits for its predecessor (x and `out`
+//           may come from it), releases the dependent launch, stages x; every warp takes (gate
+//           row r, up row r) pairs: 16-byte non-caching loads of both rows, 8 chunks (8 KB) in
+//           flight per warp, fp32 dot products against x staged in shared memory as fp32, warp
+//           reduction, inter[n][r] = silu(g) * u in fp32.
+//   down    starts while gateup runs: each warp loads the first chunks of its two W2 rows into
+//           registers BEFORE waiting for gateup, then stages inter in shared memory and finishes
+//           its rows; out[n][h] = (accumulate ? out[n][h] : 0) + sum.
+// Both kernels stream their weights once: 2*Is*H*2 + H*Is*2 bytes per call (50.3 MB at H=4096,
+// Is=2048), which is the HBM roofline of the layer.
+#include "vq2_common.cuh"
+
+namespace vq2 {
+
+constexpr int SE_THREADS = 256;
+constexpr int SE_WARPS = SE_THREADS / 32;
+constexpr int SE_MAX_N = 8;
+constexpr int SE_BATCH = 8;            // 16-byte chunks per row in flight per lane
+constexpr int SE_CTAS_PER_SM = 2;
+
+__device__ __forceinline__ uint4 ld_stream16(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "l"(p));
+  return v;
+}
+
+// acc += <8 bf16 weights in w, 8 fp32 values at xs>
+__device__ __forceinline__ float dot8_bf16(uint4 w, const float* xs, float acc) {
+  const float4 a = *reinterpret_cast<const float4*>(xs);
+  const float4 b = *reinterpret_cast<const float4*>(xs + 4);
+  const uint32_t u[4] = {w.x, w.y, w.z, w.w};
+  const float xv[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    acc = fmaf(__uint_as_float(u[i] << 16), xv[2 * i], acc);
+    acc = fmaf(__uint_as_float(u[i] & 0xFFFF0000u), xv[2 * i + 1], acc);
+  }
+  return acc;
+}
+
+__global__ void __launch_bounds__(SE_THREADS, SE_CTAS_PER_SM) shared_gateup_kernel(
+    const void* __restrict__ x, int x_dtype, const __nv_bfloat16* __restrict__ w13, int N, int H, int Is,
+    float* __restrict__ inter) {
+  extern __shared__ __align__(16) float xs[];          // [N][H]
+  const int lane = threadIdx.x & 31;
+  const int nch = H / 256;                             // 16-byte chunks per lane per row
+  const long long nw = (long long)gridDim.x * SE_WARPS;
+  long long r = (long long)blockIdx.x * SE_WARPS + (threadIdx.x >> 5);
+  uint4 wg[SE_BATCH], wu[SE_BATCH];
+  // the weights depend on nothing earlier in the stream: fetch the first chunks of this warp's
+  // first row pair before waiting for the predecessor and staging x
+  if (r < Is) {
+    const char* rg = reinterpret_cast<const char*>(w13 + (size_t)r * H) + lane * 16;
+    const char* ru = reinterpret_cast<const char*>(w13 + (size_t)(r + Is) * H) + lane * 16;
+#pragma unroll
+    for (int c = 0; c < SE_BATCH; ++c) {
+      if (c < nch) {
+        wg[c] = ld_stream16(rg + (size_t)c * 512);
+        wu[c] = ld_stream16(ru + (size_t)c * 512);
+      }
+    }
+  }
+  pdl_wait();
+  pdl_launch_dependents();
+  for (int i = threadIdx.x; i < N * H; i += SE_THREADS) xs[i] = load_act(x, x_dtype, i);
+  __syncthreads();
+  bool first = true;
+  for (; r < Is; r += nw) {
+    const char* rg = reinterpret_cast<const char*>(w13 + (size_t)r * H) + lane * 16;
+    const char* ru = reinterpret_cast<const char*>(w13 + (size_t)(r + Is) * H) + lane * 16;
+    float g[SE_MAX_N], u[SE_MAX_N];
+#pragma unroll
+    for (int n = 0; n < SE_MAX_N; ++n) g[n] = u[n] = 0.f;
+    for (int c0 = 0; c0 < nch; c0 += SE_BATCH) {
+      if (!(first && c0 == 0)) {
+#pragma unroll
+        for (int c = 0; c < SE_BATCH; ++c) {
+          if (c0 + c < nch) {
+            wg[c] = ld_stream16(rg + (size_t)(c0 + c) * 512);
+            wu[c] = ld_stream16(ru + (size_t)(c0 + c) * 512);
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < SE_BATCH; ++c) {
+        if (c0 + c < nch) {
+          const int col = (c0 + c) * 256 + lane * 8;
+#pragma unroll
+          for (int n = 0; n < SE_MAX_N; ++n) {
+            if (n < N) {
+              g[n] = dot8_bf16(wg[c], xs + n * H + col, g[n]);
+              u[n] = dot8_bf16(wu[c], xs + n * H + col, u[n]);
+            }
+          }
+        }
+      }
+    }
+    first = false;
+#pragma unroll
+    for (int n = 0; n < SE_MAX_N; ++n) {
+      if (n < N) {
+        const float gs = warp_sum(g[n]), us = warp_sum(u[n]);
+        if (lane == 0) inter[(size_t)n * Is + r] = gs / (1.f + __expf(-gs)) * us;
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(SE_THREADS, SE_CTAS_PER_SM) shared_down_kernel(
+    const float* __restrict__ inter, const __nv_bfloat16* __restrict__ w2, int N, int H, int Is,
+    float* __restrict__ out, int accumulate) {
+  extern __shared__ __align__(16) float is_[];         // [N][Is]
+  const int lane = threadIdx.x & 31;
+  const int nch = Is / 256;
+  const long long nunits = H / 2;                      // two W2 rows per warp unit
+  const long long nw = (long long)gridDim.x * SE_WARPS;
+  long long unit = (long long)blockIdx.x * SE_WARPS + (threadIdx.x >> 5);
+  uint4 wa[SE_BATCH], wb[SE_BATCH];
+  // prefetch the first chunks of this warp's first rows while the gate/up kernel still runs
+  if (unit < nunits) {
+    const char* ra = reinterpret_cast<const char*>(w2 + (size_t)(2 * unit) * Is) + lane * 16;
+#pragma unroll
+    for (int c = 0; c < SE_BATCH; ++c) {
+      if (c < nch) {
+        wa[c] = ld_stream16(ra + (size_t)c * 512);
+        wb[c] = ld_stream16(ra + (size_t)Is * 2 + (size_t)c * 512);
+      }
+    }
+  }
+  pdl_wait();
+  for (int i = threadIdx.x; i < N * Is; i += SE_THREADS) is_[i] = inter[i];
+  __syncthreads();
+  bool first = true;
+  for (; unit < nunits; unit += nw) {
+    const char* ra = reinterpret_cast<const char*>(w2 + (size_t)(2 * unit) * Is) + lane * 16;
+    float a[SE_MAX_N], b[SE_MAX_N];
+#pragma unroll
+    for (int n = 0; n < SE_MAX_N; ++n) a[n] = b[n] = 0.f;
+    for (int c0 = 0; c0 < nch; c0 += SE_BATCH) {
+      if (!(first && c0 == 0)) {
+#pragma unroll
+        for (int c = 0; c < SE_BATCH; ++c) {
+          if (c0 + c < nch) {
+            wa[c] = ld_stream16(ra + (size_t)(c0 + c) * 512);
+            wb[c] = ld_stream16(ra + (size_t)Is * 2 + (size_t)(c0 + c) * 512);
+          }
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < SE_BATCH; ++c) {
+        if (c0 + c < nch) {
+          const int col = (c0 + c) * 256 + lane * 8;
+#pragma unroll
+          for (int n = 0; n < SE_MAX_N; ++n) {
+            if (n < N) {
+              a[n] = dot8_bf16(wa[c], is_ + n * Is + col, a[n]);
+              b[n] = dot8_bf16(wb[c], is_ + n * Is + col, b[n]);
+            }
+          }
+        }
+      }
+    }
+    first = false;
+#pragma unroll
+    for (int n = 0; n < SE_MAX_N; ++n) {
+      if (n < N) {
+        const float as = warp_sum(a[n]), bs = warp_sum(b[n]);
+        if (lane == 0) {
+          float* o = out + (size_t)n * H + 2 * unit;
+          o[0] = accumulate ? o[0] + as : as;
+          o[1] = accumulate ? o[1] + bs : bs;
+        }
+      }
+    }
+  }
+}
+
+inline int se_grid(long long warps) {
+  const long long b = (warps + SE_WARPS - 1) / SE_WARPS;
+  return (int)std::min<long long>(std::max<long long>(b, 1), 148LL * SE_CTAS_PER_SM);
+}
+
+}  // namespace vq2
+
+using namespace vq2;
+
+extern "C" size_t vq2_shared_expert_workspace_size(int N, int Is) {
+  if (N <= 0 || Is <= 0) return 0;
+  return (size_t)N * Is * sizeof(float) + 256;
+}
+
+extern "C" int vq2_shared_expert(const void* x, int x_dtype, const void* w13, const void* w2, int N, int H, int Is,
+                                 float* out, int accumulate, void* ws, size_t ws_bytes, void* stream) {
+  if (!x || !w13 || !w2 || !out) return VQ2_ERR_NULL;
+  if (N <= 0 || N > SE_MAX_N || H <= 0 || Is <= 0 || H % 256 || Is % 256 || H % 2) return VQ2_ERR_SHAPE;
+  const size_t sm_gu = (size_t)N * H * sizeof(float), sm_dn = (size_t)N * Is * sizeof(float);
+  if (sm_gu > 200 * 1024 || sm_dn > 200 * 1024) return VQ2_ERR_SHAPE;
+  if (x_dtype < 0 || x_dtype > 2) return VQ2_ERR_DTYPE;
+  if ((uintptr_t)w13 % 16 || (uintptr_t)w2 % 16) return VQ2_ERR_ALIGN;
+  if (!ws || ws_bytes < vq2_shared_expert_workspace_size(N, Is)) return VQ2_ERR_WORKSPACE;
+  float* inter = (float*)(((uintptr_t)ws + 255) & ~(uintptr_t)255);
+  if (cudaFuncSetAttribute(shared_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu) != cudaSuccess ||
+      cudaFuncSetAttribute(shared_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_dn) != cudaSuccess)
+    return VQ2_ERR_CUDA;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.blockDim = dim3(SE_THREADS);
+  cfg.stream = (cudaStream_t)stream;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cfg.gridDim = dim3(se_grid(Is));
+  cfg.dynamicSmemBytes = sm_gu;
+  if (cudaLaunchKernelEx(&cfg, shared_gateup_kernel, x, x_dtype, (const __nv_bfloat16*)w13, N, H, Is, inter) !=
+      cudaSuccess)
+    return VQ2_ERR_CUDA;
+  cfg.gridDim = dim3(se_grid(H / 2));
+  cfg.dynamicSmemBytes = sm_dn;
+  if (cudaLaunchKernelEx(&cfg, shared_down_kernel, (const float*)inter, (const __nv_bfloat16*)w2, N, H, Is, out,
+                         accumulate) != cudaSuccess)
+    return VQ2_ERR_CUDA;
+  return VQ2_OK;
+}

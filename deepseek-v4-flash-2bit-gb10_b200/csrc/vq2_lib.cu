@@ -7,3 +7,4 @@
 #include "ep_p2p.cu"
 #include "router.cu"
 #include "pack.cu"
+#include "shared.cu"

@@ -68,6 +68,10 @@ _SIGS = {
     "vq2_pack_assign": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_longlong, ctypes.c_int, ctypes.c_void_p,
                                        ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                        ctypes.c_void_p, ctypes.c_void_p]),
+    "vq2_shared_expert_workspace_size": (ctypes.c_size_t, [ctypes.c_int, ctypes.c_int]),
+    "vq2_shared_expert": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                         ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
+                                         ctypes.c_size_t, ctypes.c_void_p]),
     "vq2_device_status": (ctypes.c_int, [ctypes.c_int]),
     "vq2_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "vq2_version": (ctypes.c_int, []),

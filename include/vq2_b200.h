@@ -171,6 +171,17 @@ int vq2_kmeans(const float* samp, long long n, float* C, int k, int iters, void*
 int vq2_pack_assign(const void* W, int w_dtype, long long rows, int D, const float* C, int k, uint8_t* lo,
                     uint8_t* hi, int16_t* idx, float* scale, float* dq, void* stream);
 
+/* ---- shared expert of the decode step (no counterpart in the reference plugin, whose `apply`
+   leaves it to vLLM): out[n] (+)= W2 . (silu(Wg . x[n]) * (Wu . x[n])), dense bf16 weights
+   w13 = [Wg; Wu] [2*Is][H] and w2 [H][Is] (row-major, 16-byte aligned), fp32 accumulation and
+   fp32 intermediate. out f32 [N][H]: overwritten, or added to with accumulate = 1. N <= 8,
+   H and Is multiples of 256, N*H*4 and N*Is*4 <= 200 KB. Two launches chained by programmatic
+   dependent launch; the first waits for the stream's previous work, so `out` may be the routed
+   experts' output of the same stream. */
+size_t vq2_shared_expert_workspace_size(int N, int Is);
+int vq2_shared_expert(const void* x, int x_dtype, const void* w13, const void* w2, int N, int H, int Is, float* out,
+                      int accumulate, void* workspace, size_t ws_bytes, void* stream);
+
 int vq2_device_status(int reset);
 const char* vq2_strerror(int code);
 int vq2_version(void);

@@ -63,3 +63,18 @@ def test_packer_rejects_bad_arguments_without_a_gpu():
     assert L.vq2_kmeans(fake, 10, fake, 16, 3, None, 0, None) == 5                                # workspace
     assert L.vq2_pack_gather(fake, 0, 4, 64, fake, 5, fake + 8, None) == 3                       # out unaligned
     assert L.vq2_kmeans_workspace_size(1025) == 0
+
+
+def test_shared_expert_rejects_bad_arguments_without_a_gpu():
+    from vq2_vllm import _lib
+    from vq2_vllm.kernels.shared_expert import shared_expert_fused
+    with pytest.raises(RuntimeError, match="no CPU path"):
+        shared_expert_fused(torch.zeros(1, 256), torch.zeros(512, 256, dtype=torch.bfloat16),
+                            torch.zeros(256, 256, dtype=torch.bfloat16))
+    L = _lib.lib()
+    fake = 1 << 20
+    assert L.vq2_shared_expert(fake, 0, fake, fake, 9, 256, 256, fake, 0, fake, 1 << 20, None) == 2     # N > 8
+    assert L.vq2_shared_expert(fake, 0, fake, fake, 1, 320, 256, fake, 0, fake, 1 << 20, None) == 2     # H % 256
+    assert L.vq2_shared_expert(fake, 0, fake + 2, fake, 1, 256, 256, fake, 0, fake, 1 << 20, None) == 3  # alignment
+    assert L.vq2_shared_expert(fake, 0, fake, fake, 1, 256, 256, fake, 0, None, 0, None) == 5           # workspace
+    assert L.vq2_shared_expert(None, 0, fake, fake, 1, 256, 256, fake, 0, fake, 1 << 20, None) == 1     # null
