@@ -260,8 +260,9 @@ def time_pack(dev):
 
 def time_shared(dev, hbm):
     """The config-1 shared expert (bf16 gate/up [4096, 4096], down [4096, 2048]) for batch 1 and
-    3: four copies of its weights (201 MB > L2) cycled, CUDA events around 40 calls; beside it the
-    same layer as torch bf16 ops (two cuBLAS GEMMs and silu * mul), cycled the same way."""
+    3: four copies of its weights (201 MB > L2) cycled, one call per copy captured in a CUDA
+    graph, replayed 10 times between CUDA events (us per call); beside it the same layer as torch
+    bf16 ops (two cuBLAS GEMMs and silu * mul), captured and replayed the same way."""
     from vq2_vllm.kernels.shared_expert import shared_expert_fused
     Is = I
     g = torch.Generator(device=dev).manual_seed(31)
@@ -273,24 +274,34 @@ def time_shared(dev, hbm):
         h = torch.nn.functional.linear(x, w13)
         return torch.nn.functional.linear(torch.nn.functional.silu(h[:, :Is]) * h[:, Is:], w2)
 
-    res = {"bytes_per_call": nbytes}
+    res = {"bytes_per_call": nbytes, "how": "CUDA graph of 4 calls (one per weight copy), 10 replays"}
     for N in (1, 3):
         x = torch.randn(N, H, generator=g, device=dev).bfloat16()
         for name, f in (("ours", lambda a, b: shared_expert_fused(x, a, b)), ("torch_ops", lambda a, b: torch_ops(x, a, b))):
-            for i in range(8):
-                f(*ws[i % 4])
+            s = torch.cuda.Stream()
+            s.wait_stream(torch.cuda.current_stream())
+            with torch.cuda.stream(s):
+                for i in range(8):
+                    f(*ws[i % 4])
+            torch.cuda.current_stream().wait_stream(s)
+            gr = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(gr):
+                for i in range(4):
+                    f(*ws[i])
+            gr.replay()
             torch.cuda.synchronize()
-            s, e = torch.cuda.Event(True), torch.cuda.Event(True)
-            s.record()
-            for i in range(40):
-                f(*ws[i % 4])
-            e.record()
-            e.synchronize()
-            us = s.elapsed_time(e) * 1e3 / 40
+            st, en = torch.cuda.Event(True), torch.cuda.Event(True)
+            st.record()
+            for _ in range(10):
+                gr.replay()
+            en.record()
+            en.synchronize()
+            us = st.elapsed_time(en) * 1e3 / 40
             res[f"{name}_us_b{N}"] = us
             if name == "ours":
                 res[f"ours_GBps_b{N}"] = nbytes / (us * 1e-6) / 1e9
                 res[f"ours_frac_hbm_b{N}"] = nbytes / (us * 1e-6) / 1e9 / hbm
+            del gr
     del ws
     torch.cuda.empty_cache()
     return res

@@ -46,6 +46,33 @@ __device__ __forceinline__ float dot8_bf16(uint4 w, const float* xs, float acc) 
   return acc;
 }
 
+// dst[0 .. n) = fp32 of src (VQ2_DT_*), 16-byte loads; n a multiple of 8, src 16-byte aligned
+__device__ __forceinline__ void stage_f32(float* dst, const void* src, int dt, int n) {
+  if (dt == VQ2_DT_F32) {
+    for (int i = threadIdx.x * 4; i < n; i += SE_THREADS * 4)
+      *reinterpret_cast<float4*>(dst + i) = *reinterpret_cast<const float4*>(static_cast<const float*>(src) + i);
+    return;
+  }
+  for (int i = threadIdx.x * 8; i < n; i += SE_THREADS * 8) {
+    const uint4 v = *reinterpret_cast<const uint4*>(static_cast<const uint16_t*>(src) + i);
+    const uint32_t u[4] = {v.x, v.y, v.z, v.w};
+    float f[8];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (dt == VQ2_DT_BF16) {
+        f[2 * j] = __uint_as_float(u[j] << 16);
+        f[2 * j + 1] = __uint_as_float(u[j] & 0xFFFF0000u);
+      } else {
+        const float2 h = __half22float2(*reinterpret_cast<const __half2*>(&u[j]));
+        f[2 * j] = h.x;
+        f[2 * j + 1] = h.y;
+      }
+    }
+    *reinterpret_cast<float4*>(dst + i) = make_float4(f[0], f[1], f[2], f[3]);
+    *reinterpret_cast<float4*>(dst + i + 4) = make_float4(f[4], f[5], f[6], f[7]);
+  }
+}
+
 __global__ void __launch_bounds__(SE_THREADS, SE_CTAS_PER_SM) shared_gateup_kernel(
     const void* __restrict__ x, int x_dtype, const __nv_bfloat16* __restrict__ w13, int N, int H, int Is,
     float* __restrict__ inter) {
@@ -70,7 +97,7 @@ __global__ void __launch_bounds__(SE_THREADS, SE_CTAS_PER_SM) shared_gateup_kern
   }
   pdl_wait();
   pdl_launch_dependents();
-  for (int i = threadIdx.x; i < N * H; i += SE_THREADS) xs[i] = load_act(x, x_dtype, i);
+  stage_f32(xs, x, x_dtype, N * H);
   __syncthreads();
   bool first = true;
   for (; r < Is; r += nw) {
@@ -136,7 +163,7 @@ __global__ void __launch_bounds__(SE_THREADS, SE_CTAS_PER_SM) shared_down_kernel
     }
   }
   pdl_wait();
-  for (int i = threadIdx.x; i < N * Is; i += SE_THREADS) is_[i] = inter[i];
+  stage_f32(is_, inter, VQ2_DT_F32, N * Is);
   __syncthreads();
   bool first = true;
   for (; unit < nunits; unit += nw) {
@@ -204,7 +231,7 @@ extern "C" int vq2_shared_expert(const void* x, int x_dtype, const void* w13, co
   const size_t sm_gu = (size_t)N * H * sizeof(float), sm_dn = (size_t)N * Is * sizeof(float);
   if (sm_gu > 200 * 1024 || sm_dn > 200 * 1024) return VQ2_ERR_SHAPE;
   if (x_dtype < 0 || x_dtype > 2) return VQ2_ERR_DTYPE;
-  if ((uintptr_t)w13 % 16 || (uintptr_t)w2 % 16) return VQ2_ERR_ALIGN;
+  if ((uintptr_t)w13 % 16 || (uintptr_t)w2 % 16 || (uintptr_t)x % 16) return VQ2_ERR_ALIGN;
   if (!ws || ws_bytes < vq2_shared_expert_workspace_size(N, Is)) return VQ2_ERR_WORKSPACE;
   float* inter = (float*)(((uintptr_t)ws + 255) & ~(uintptr_t)255);
   if (cudaFuncSetAttribute(shared_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu) != cudaSuccess ||
