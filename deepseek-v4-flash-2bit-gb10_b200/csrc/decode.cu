@@ -73,21 +73,6 @@ struct DecodeShared {
   alignas(16) int ekey[VQ2_DECODE_MAX_PAIRS];
 };
 
-#ifdef VQ2_DEC_PROBE
-// Development probe (off in the product build): per-CTA global-timer stamps of the phases.
-__device__ unsigned long long g_probe[2][1024][16];
-__device__ __forceinline__ unsigned long long gtime() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-// slot 15: globaltimer anchor, slot 14: clock64 at the anchor; other slots: clock64
-#define PROBE(k, i) do { \
-    if ((i) == 0) { g_probe[k][blockIdx.x][14] = clock64(); g_probe[k][blockIdx.x][15] = gtime(); } \
-    g_probe[k][blockIdx.x][i] = clock64(); } while (0)
-#else
-#define PROBE(k, i) do {} while (0)
-#endif
 
 // ------------------------------------------------------------------ plan: group pairs by expert
 // Unit u = one (local expert, pair) with units ordered by expert and, within an expert, by pair
@@ -569,10 +554,8 @@ __device__ __forceinline__ void gateup_consume(const vq2_moe_args& a, const DecS
         load_xs(sh, g, gv, xr[0]);
         inv = gv ? sh->ginv[g] : 0.f;
       }
-      if (threadIdx.x == 0 && c == 0) PROBE(0, 5);
     }
     if (!mbar_wait(&sh->full[slot], (c / DEC_STAGES) & 1)) { ++c; break; }
-    if (threadIdx.x == 0 && c == 0) PROBE(0, 3);
     const uint8_t* st = d.stages + slot * DEC_STAGE_BYTES;
     if (S / rstep >= 4) {
       for (int rr0 = rsub; rr0 < n; rr0 += 4 * rstep)
@@ -652,10 +635,8 @@ __device__ __forceinline__ void down_consume(const vq2_moe_args& a, const DecSme
       else stage_units(u - ub, 1);
       load_xs(sh, gi, gv, xr[0]);
       wsc = sh->unit_w[u] * (gv ? sh->ginv[gi] : 0.f);
-      if (threadIdx.x == 0 && c == 0) PROBE(1, 5);
     }
     if (!mbar_wait(&sh->full[slot], (c / DEC_STAGES) & 1)) { ++c; break; }
-    if (threadIdx.x == 0 && c == 0) PROBE(1, 3);
     const uint8_t* st = d.stages + slot * DEC_STAGE_BYTES;
     if (S / rstep >= 8) {
       for (int rr0 = rsub; rr0 < n; rr0 += 8 * rstep)
@@ -683,7 +664,6 @@ __global__ void __launch_bounds__(DEC_THREADS, 1)
 decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
   extern __shared__ __align__(128) uint8_t smem[];
   const DecSmem d = dec_smem(smem);
-  if (threadIdx.x == 0) PROBE(0, 0);
   // Launched with programmatic dependent launch: the CTA becomes resident and issues the
   // codebook copy (a constant weight) while the previous kernel drains. Everything after
   // pdl_wait() reads the call's inputs or writes the workspace and output, which the previous
@@ -704,11 +684,8 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
   }
   GateupPre pre;
   gateup_pre(a, d, pre);
-  if (threadIdx.x == 0) PROBE(0, 1);
   fill_codebook(d.cbs, d.sh);         // overlaps the activation loads of gateup_pre
-  if (threadIdx.x == 0) PROBE(0, 2);
   gateup_consume<KH>(a, d, part, pre, c);
-  if (threadIdx.x == 0) PROBE(0, 4);
 }
 
 // ------------------------------------------------------------------ kernel B: down + combine
@@ -729,13 +706,9 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
     }
     return;
   }
-  if (threadIdx.x == 0) PROBE(1, 0);
   fill_codebook(d.cbs, d.sh);
-  if (threadIdx.x == 0) PROBE(1, 1);
   pdl_wait();   // the gate/up partials and the zeroed output come from the previous grid
-  if (threadIdx.x == 0) PROBE(1, 2);
   down_consume<KH>(a, d, part, khA, c);
-  if (threadIdx.x == 0) PROBE(1, 4);
 }
 
 static size_t decode_smem_bytes(size_t stage_bytes) {
@@ -754,11 +727,6 @@ static DecodeLaunchCache g_dec_cache[64];
 
 using namespace vq2;
 
-#ifdef VQ2_DEC_PROBE
-extern "C" int vq2_probe_read(void* host) {
-  return (int)cudaMemcpyFromSymbol(host, g_probe, sizeof(g_probe));
-}
-#endif
 
 static int khA_of(int H) { return (H / 64 + 31) / 32; }
 

@@ -31,6 +31,7 @@ constexpr int PK_MAX_K = 1024;
 constexpr int PK_THREADS = 256;
 constexpr int PK_GROUPS_PER_WARP = 8;              // 128 sub-vectors, 4 per lane
 constexpr float PK_FIX = 1099511627776.0f;         // 2^40
+constexpr long long PK_MAX_SAMPLES = 1LL << 23;    // k-means sample limit: 2^23 x 2^40 < 2^63
 
 // Normalised group `gid` (flat over rows x groups) of W [rows][D]: lane holds columns lane and
 // lane + 32 of the rotated, normalised group; returns the group scale.
@@ -73,11 +74,15 @@ __device__ __forceinline__ void pk_load_codebook(float4* cs, const float4* C, in
 
 __global__ void __launch_bounds__(PK_THREADS) pack_gather_kernel(const void* __restrict__ W, int dt, int D, int ng,
                                                                  const long long* __restrict__ vidx, long long n,
-                                                                 float4* __restrict__ out) {
+                                                                 long long nvec, float4* __restrict__ out) {
   const int lane = threadIdx.x & 31;
   const long long s = ((long long)blockIdx.x * PK_THREADS + threadIdx.x) >> 5;
   if (s >= n) return;
   const long long v = vidx[s];
+  if (v < 0 || v >= nvec) {                 // out-of-range index: skip the load, record the error
+    if (lane == 0) set_status(VQ2_ERR_SHAPE);
+    return;
+  }
   const int j = (int)(v & 15);
   float a, b;
   pk_rotate(W, dt, v >> 4, ng, D, lane, a, b);
@@ -278,7 +283,8 @@ __global__ void __launch_bounds__(PK_THREADS) pack_assign_kernel(const void* __r
 
 inline int pk_grid(long long warps_needed) {
   long long b = (warps_needed + PK_THREADS / 32 - 1) / (PK_THREADS / 32);
-  return (int)std::min<long long>(std::max<long long>(b, 1), 148LL * 8);
+  const long long nsm = std::max(device_sm_count(), 1);
+  return (int)std::min<long long>(std::max<long long>(b, 1), nsm * 8);
 }
 
 }  // namespace vq2
@@ -295,7 +301,7 @@ extern "C" int vq2_pack_gather(const void* W, int w_dtype, long long rows, int D
   const int ng = (D + 63) / 64;
   const long long blocks = (n * 32 + PK_THREADS - 1) / PK_THREADS;
   pack_gather_kernel<<<(unsigned)blocks, PK_THREADS, 0, (cudaStream_t)stream>>>(W, w_dtype, D, ng, vec_idx, n,
-                                                                                (float4*)out);
+                                                                                rows * ng * 16, (float4*)out);
   return cudaGetLastError() == cudaSuccess ? VQ2_OK : VQ2_ERR_CUDA;
 }
 
@@ -308,6 +314,8 @@ extern "C" int vq2_kmeans(const float* samp, long long n, float* C, int k, int i
                           void* stream) {
   if (!samp || !C) return VQ2_ERR_NULL;
   if (n <= 0 || k <= 0 || k > PK_MAX_K || iters < 0) return VQ2_ERR_SHAPE;
+  // int64 fixed-point member sums (|value| <= 1, x 2^40) cannot overflow below 2^23 members
+  if (n > PK_MAX_SAMPLES) return VQ2_ERR_SHAPE;
   if ((uintptr_t)samp % 16 || (uintptr_t)C % 16) return VQ2_ERR_ALIGN;
   if (!ws || ws_bytes < vq2_kmeans_workspace_size(k)) return VQ2_ERR_WORKSPACE;
   cudaStream_t st = (cudaStream_t)stream;

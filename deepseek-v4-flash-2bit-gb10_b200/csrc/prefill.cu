@@ -219,18 +219,6 @@ __device__ __forceinline__ void decode_b_quarter(uint32_t cbl, uint2 lo, uint32_
 // [256n, 256n+256) and the epilogue accumulates into out. Two blocks of the same expert run as
 // one pass (each decoded B tile feeds two MMAs, two TMEM accumulators); two blocks of different
 // experts run as two passes, one accumulator each.
-#ifdef VQ2_PF_PROBE
-// Development probe (off in the product build): global-timer stamps per stage of CTA (0, 0).
-__device__ unsigned long long g_pf_probe[4][64];
-__device__ __forceinline__ unsigned long long pf_time() {
-  unsigned long long t;
-  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
-  return t;
-}
-#define PF_PROBE(k, i) do { if (blockIdx.x == 0 && blockIdx.y == 0 && (i) < 64) g_pf_probe[k][i] = pf_time(); } while (0)
-#else
-#define PF_PROBE(k, i) do {} while (0)
-#endif
 
 template <bool GATEUP>
 __device__ __forceinline__ long pf_weight_row(const PfGemmArgs& a, int e, int tile, int r) {
@@ -258,7 +246,6 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
   uint8_t* itiles = btiles + PF_BSTAGES * PF_BTILE;    // index-plane ring
   PfShared* sh = (PfShared*)(itiles + PF_ISTAGES * PF_IDX);
   const int tile = blockIdx.x, b0 = blockIdx.y * PF_MB;
-  if (threadIdx.x == 0) PF_PROBE(3, 0);
   if (!a.val[(size_t)b0 * PF_BM]) return;            // blocks past the last expert hold no pair
   const bool v1 = b0 + 1 < nblk && a.val[(size_t)(b0 + 1) * PF_BM];
   const int e0 = a.be[b0], e1 = v1 ? a.be[b0 + 1] : -1;
@@ -316,7 +303,6 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
   tc_fence_before();
   __syncthreads();                                    // codebook ready, staging tile free again
   tc_fence_after();
-  if (threadIdx.x == 0) PF_PROBE(3, 1);
   const uint32_t tmem = sh->tmem_base;
 
   if (warp == 0) {
@@ -331,7 +317,6 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
           mbar_arrive_expect_tx(&sh->full_a[slot], P.mb * PF_TILE);
           tma_load_2d(A_t(slot), &tm_act, c * 128, P.blk * PF_BM, &sh->full_a[slot]);
           if (P.mb == 2) tma_load_2d(A_t(slot) + PF_TILE, &tm_act, c * 128, (P.blk + 1) * PF_BM, &sh->full_a[slot]);
-          PF_PROBE(0, gc);
         }
       }
     }
@@ -386,9 +371,7 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
         for (int c = 0; c < nchunks; ++c, ++gc) {
           const int slot = gc % PF_STAGES, bslot = gc % PF_BSTAGES;
           if (!mbar_wait(&sh->full_a[slot], (gc / PF_STAGES) & 1)) { ok = false; break; }
-          PF_PROBE(1, gc);
           if (!mbar_wait(&sh->full_b[bslot], (gc / PF_BSTAGES) & 1)) { ok = false; break; }
-          PF_PROBE(2, gc);
           fence_async_smem();                             // cp.async-written data visible to the tensor core
           tc_fence_after();
           const uint32_t abase = smem_u32(A_t(slot)), bbase = smem_u32(B_t(bslot));   // B: 256 rows
@@ -484,12 +467,10 @@ prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, co
           }
         }
       }
-      if (threadIdx.x == 96) PF_PROBE(3, 2);
     }
   }
   tc_fence_before();
   __syncthreads();
-  if (threadIdx.x == 0) PF_PROBE(3, 3);
   if (warp == 0) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PF_TMEM_COLS) : "memory");
@@ -641,9 +622,6 @@ static bool g_pf_attr[64];
 
 using namespace vq2;
 
-#ifdef VQ2_PF_PROBE
-extern "C" int vq2_pf_probe_read(void* host) { return (int)cudaMemcpyFromSymbol(host, g_pf_probe, sizeof(g_pf_probe)); }
-#endif
 
 extern "C" size_t vq2_prefill_workspace_size(int N, int topk, int E, int H, int I, int precision) {
   if (N <= 0 || topk <= 0 || E <= 0) return 0;

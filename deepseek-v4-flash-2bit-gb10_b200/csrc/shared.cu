@@ -210,9 +210,12 @@ __global__ void __launch_bounds__(SE_THREADS, SE_CTAS_PER_SM) shared_down_kernel
   }
 }
 
+constexpr int SE_SMEM_CAP = 200 * 1024;   // dynamic shared memory of either kernel (x or inter as fp32)
+
 inline int se_grid(long long warps) {
   const long long b = (warps + SE_WARPS - 1) / SE_WARPS;
-  return (int)std::min<long long>(std::max<long long>(b, 1), 148LL * SE_CTAS_PER_SM);
+  const long long nsm = std::max(device_sm_count(), 1);
+  return (int)std::min<long long>(std::max<long long>(b, 1), nsm * SE_CTAS_PER_SM);
 }
 
 }  // namespace vq2
@@ -229,14 +232,22 @@ extern "C" int vq2_shared_expert(const void* x, int x_dtype, const void* w13, co
   if (!x || !w13 || !w2 || !out) return VQ2_ERR_NULL;
   if (N <= 0 || N > SE_MAX_N || H <= 0 || Is <= 0 || H % 256 || Is % 256 || H % 2) return VQ2_ERR_SHAPE;
   const size_t sm_gu = (size_t)N * H * sizeof(float), sm_dn = (size_t)N * Is * sizeof(float);
-  if (sm_gu > 200 * 1024 || sm_dn > 200 * 1024) return VQ2_ERR_SHAPE;
+  if (sm_gu > (size_t)SE_SMEM_CAP || sm_dn > (size_t)SE_SMEM_CAP) return VQ2_ERR_SHAPE;
   if (x_dtype < 0 || x_dtype > 2) return VQ2_ERR_DTYPE;
   if ((uintptr_t)w13 % 16 || (uintptr_t)w2 % 16 || (uintptr_t)x % 16) return VQ2_ERR_ALIGN;
   if (!ws || ws_bytes < vq2_shared_expert_workspace_size(N, Is)) return VQ2_ERR_WORKSPACE;
   float* inter = (float*)(((uintptr_t)ws + 255) & ~(uintptr_t)255);
-  if (cudaFuncSetAttribute(shared_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_gu) != cudaSuccess ||
-      cudaFuncSetAttribute(shared_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm_dn) != cudaSuccess)
-    return VQ2_ERR_CUDA;
+  // The dynamic shared-memory limit is raised once per device to the cap every call fits in, so
+  // calls with different N (other threads, captured graphs) never lower it under one another.
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VQ2_ERR_NO_DEVICE;
+  static bool attr_set[64];
+  if (!attr_set[dev]) {
+    if (cudaFuncSetAttribute(shared_gateup_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SE_SMEM_CAP) != cudaSuccess ||
+        cudaFuncSetAttribute(shared_down_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SE_SMEM_CAP) != cudaSuccess)
+      return VQ2_ERR_CUDA;
+    attr_set[dev] = true;
+  }
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;

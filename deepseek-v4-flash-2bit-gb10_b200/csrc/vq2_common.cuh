@@ -162,6 +162,17 @@ __device__ __forceinline__ void unpack_ids4(uint32_t lo_word, uint32_t hb, uint3
   ids13 = e13 | ((hb * 0x00040040u) & 0x03000300u);         // hb bits 2-3 -> 8-9, bits 6-7 -> 24-25
 }
 
+// Streaming-multiprocessor count of the current device, looked up once per device (grids of the
+// grid-stride kernels are sized from it). Returns 0 if the query fails.
+inline int device_sm_count() {
+  static int counts[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return 0;
+  if (!counts[dev] && cudaDeviceGetAttribute(&counts[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    counts[dev] = 0;
+  return counts[dev];
+}
+
 __device__ __forceinline__ int load_id(const void* ids, int ids_dtype, int m) {
   return ids_dtype == VQ2_ID_I64 ? (int)((const long long*)ids)[m] : ((const int*)ids)[m];
 }

@@ -7,6 +7,7 @@ from __future__ import annotations
 
 import ctypes
 import os
+import threading
 
 import torch
 
@@ -136,14 +137,19 @@ def workspace(nbytes: int, device, stream=None) -> torch.Tensor:
     return buf
 
 
-_ARGS = {}
+_TLS = threading.local()
 
 
 def moe_args(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, out, expert_base=0, E=None):
     """The vq2_moe_args struct for one call. The weight part is cached per layer (keyed by the
-    weight pointers and shapes), so a call only rewrites the per-call fields."""
+    weight pointers and shapes) and per host thread, so a call only rewrites the per-call fields
+    and two threads calling the same layer never share (and race on) one struct. The struct is
+    read by the library during the call only."""
     wkey = (Cgu.data_ptr(), lgu.data_ptr(), hgu.data_ptr(), sgu.data_ptr(), Cd.data_ptr(), ld.data_ptr(),
             hd.data_ptr(), sdn.data_ptr(), lgu.shape, E)
+    _ARGS = getattr(_TLS, "args", None)
+    if _ARGS is None:
+        _ARGS = _TLS.args = {}
     a = _ARGS.get(wkey)
     if a is None:
         a = Vq2MoeArgs()

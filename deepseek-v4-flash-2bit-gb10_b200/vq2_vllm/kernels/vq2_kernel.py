@@ -85,7 +85,8 @@ def vq2_moe_fused_10b(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, 
     """Decode MoE over 10-bit byte-plane VQ experts -> fp32 [N, H]
     (reference vq2_kernel.py:569-594). ``expert_base`` (extension, default 0): ids are global and
     only experts [expert_base, expert_base + E) held in these tensors are applied (expert
-    parallelism). Batches above the decode kernel's pair limit go to the grouped GEMM path."""
+    parallelism). Batches above the decode kernel's pair limit go to the grouped GEMM path, in the
+    precision VQ2_FP8_PREFILL selects (fp8 by default, as the plugin's prefill dispatch)."""
     if group != 64:
         raise ValueError("vq2: only group=64 is supported")
     if x.is_cuda and x.get_device() != torch.cuda.current_device():   # the library launches on the current device
@@ -96,12 +97,12 @@ def vq2_moe_fused_10b(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, 
     if N * k > _lib.DECODE_MAX_PAIRS:
         from .ds4_vq2_cuda import vq2_moe_grouped_wmma
         return vq2_moe_grouped_wmma(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, group=group,
-                                    expert_base=expert_base, precision="f16")
+                                    expert_base=expert_base)   # VQ2_FP8_PREFILL selects fp8 (default) / f16
     t = _prep(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn)
     out = torch.empty(N, x.shape[1], device=x.device, dtype=torch.float32)
     L = _lib.lib()
     a = _lib.moe_args(*t, out, expert_base=expert_base)
-    nb = (N * k * ((x.shape[1] // 64 + 31) // 32) * 2 * a.I) * 4 + 256     # vq2_decode_workspace_size
+    nb = L.vq2_decode_workspace_size(N, k, a.H, a.I)
     stream = torch.cuda.current_stream(x.device).cuda_stream
     ws = _lib.workspace(nb, x.device, stream)
     rc = L.vq2_decode(a, ws.data_ptr(), ws.numel(), stream)

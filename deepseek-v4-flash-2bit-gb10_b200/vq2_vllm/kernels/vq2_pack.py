@@ -55,6 +55,11 @@ def pack_from_sample(W, si, init, iters=12, planes=True, ids=True, dq=True):
         st = _lib.stream_ptr(dev)
         dt = _lib.DT[W.dtype]
         si = si.to(torch.int64).contiguous()
+        nvec = rows * ng * 16
+        if si.numel() and (int(si.min()) < 0 or int(si.max()) >= nvec):
+            raise ValueError(f"vq2 packer: sample indices must lie in [0, {nvec})")
+        if init.numel() == 0 or int(init.min()) < 0 or int(init.max()) >= si.shape[0]:
+            raise ValueError(f"vq2 packer: init positions must lie in [0, {si.shape[0]})")
         samp = torch.empty(si.shape[0], 4, dtype=torch.float32, device=dev)
         _lib.check(L.vq2_pack_gather(W.data_ptr(), dt, rows, D, si.data_ptr(), si.shape[0], samp.data_ptr(), st),
                    "vq2_pack_gather")

@@ -60,10 +60,11 @@ def apply_moe(layer, x, topk_weights, topk_ids, group=64):
     from .kernels.vq2_kernel import vq2_moe_fused_10b
     args = (layer.w13_cb, layer.w13_lo, layer.w13_hi, layer.w13_sc, layer.w2_cb, layer.w2_lo, layer.w2_hi,
             layer.w2_sc)
+    base = int(getattr(layer, "vq2_expert_base", 0))   # set when the layer holds a slice of the experts
     if _WMMA_PREFILL and x.shape[0] >= _WMMA_MIN:
-        out = vq2_moe_grouped_wmma(x, topk_ids, topk_weights, *args, group=group)
+        out = vq2_moe_grouped_wmma(x, topk_ids, topk_weights, *args, group=group, expert_base=base)
     else:
-        out = vq2_moe_fused_10b(x, topk_ids, topk_weights, *args, group=group)
+        out = vq2_moe_fused_10b(x, topk_ids, topk_weights, *args, group=group, expert_base=base)
     return out.to(x.dtype)
 
 
@@ -96,6 +97,27 @@ def load_fused_layer_file(layer, layer_index: int, directory: str | None = None,
     for name in PARAMS:
         getattr(layer, name).data.copy_(t[name])
     return True
+
+
+def process_weights_after_loading(layer, directory: str | None = None) -> bool:
+    """The method's post-load hook (reference vq2_vllm/__init__.py:220-235): when the fused file
+    of the layer's index (from ``layer_name`` / ``prefix``, "...layers.{L}....") exists, its 8
+    tensors are read straight onto the parameters' device. A layer holding fewer experts than the
+    file (expert parallelism: ``local_num_experts`` and ``ep_rank``, as vLLM's FusedMoE has them)
+    reads only its contiguous slice [ep_rank * local, (ep_rank + 1) * local) and records the first
+    one as ``vq2_expert_base``, so apply() maps the global expert ids onto it."""
+    m = re.search(r"layers\.(\d+)\.", str(getattr(layer, "layer_name", "") or getattr(layer, "prefix", "")))
+    if m is None:
+        return False
+    E_local = int(layer.w13_lo.shape[0])
+    rng = None
+    if getattr(layer, "local_num_experts", None) is not None and getattr(layer, "ep_rank", None) is not None:
+        lo = int(layer.ep_rank) * int(layer.local_num_experts)
+        rng = (lo, lo + E_local)
+    ok = load_fused_layer_file(layer, int(m.group(1)), directory, expert_range=rng)
+    if ok and rng is not None:
+        layer.vq2_expert_base = rng[0]
+    return ok
 
 
 _CONFIG_CLS = None
@@ -133,9 +155,7 @@ def _bind():
             return apply_moe(layer, x, topk_weights, topk_ids, group=self.quant_config.group)
 
         def process_weights_after_loading(self, layer):
-            m = re.search(r"layers\.(\d+)\.", str(getattr(layer, "layer_name", "") or getattr(layer, "prefix", "")))
-            if m is not None:
-                load_fused_layer_file(layer, int(m.group(1)))
+            process_weights_after_loading(layer)
 
     class Vq2Config(QuantizationConfig):
         """Quantisation config "vq2" (reference vq2_vllm/__init__.py:293-357, MoE part)."""

@@ -108,7 +108,6 @@ int vq2_quant_fp8_rows(const float* x, int rows, int cols, uint8_t* out, float* 
  * (reference vq2_vllm/kernels/vq2_kernel.py:188-195). */
 int vq2_hadamard_rows(const void* x, int in_dtype, void* y, int out_dtype, long rows, int cols, void* stream);
 
-/* Error word written by bounded device waits (0 = none). Synchronises the device. */
 /* ---- expert-parallel token exchange over NVLink peer memory (no counterpart in the reference,
    which runs on one device). One exchange region per rank, allocated by vq2_ep_alloc (zeroed) and
    shared through CUDA IPC handles; regions are laid out identically on every rank:
@@ -156,12 +155,16 @@ int vq2_router_topk(const void* x, int x_dtype, const void* w_r, int N, int H, i
    group). Rotation is the group Hadamard (fp32 butterfly), scale s = max(|group|, 1e-8), values
    normalised by s; distances ((d0^2+d1^2)+d2^2)+d3^2 with each operation rounded separately, lowest
    index on ties; k <= 1024. */
-/* out f32 [n][4] (16-byte aligned): the normalised sub-vectors vec_idx[0..n). */
+/* out f32 [n][4] (16-byte aligned): the normalised sub-vectors vec_idx[0..n). An index outside
+   [0, rows*ng*16) is skipped (its output row is left as it was) and vq2_device_status reports
+   VQ2_ERR_SHAPE. */
 int vq2_pack_gather(const void* W, int w_dtype, long long rows, int D, const long long* vec_idx, long long n,
                     float* out, void* stream);
 /* `iters` Lloyd iterations over samp f32 [n][4] starting from C f32 [k][4] (updated in place): each
    centroid with members becomes their mean (members summed as int64 fixed point, value x 2^40
-   rounded to nearest even; mean = (double)sum * 2^-40 / count rounded to f32); empty ones stay. */
+   rounded to nearest even; mean = (double)sum * 2^-40 / count rounded to f32); empty ones stay.
+   samp values must be at most 1 in magnitude (the normalised sub-vectors vq2_pack_gather writes)
+   and n <= 2^23 (VQ2_ERR_SHAPE above), so the int64 sums cannot overflow. */
 size_t vq2_kmeans_workspace_size(int k);
 int vq2_kmeans(const float* samp, long long n, float* C, int k, int iters, void* workspace, size_t ws_bytes,
                void* stream);
@@ -182,6 +185,8 @@ size_t vq2_shared_expert_workspace_size(int N, int Is);
 int vq2_shared_expert(const void* x, int x_dtype, const void* w13, const void* w2, int N, int H, int Is, float* out,
                       int accumulate, void* workspace, size_t ws_bytes, void* stream);
 
+/* Error word written by bounded device waits and device-side range checks (0 = none);
+   reset = 1 clears it. Synchronises the device. */
 int vq2_device_status(int reset);
 const char* vq2_strerror(int code);
 int vq2_version(void);

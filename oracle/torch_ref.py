@@ -95,3 +95,30 @@ def moe_prefill_fp8_ref(x, topk_ids, topk_w, layer, expert_base=0, E=None):
         d = (vq @ bdn.T) * (topk_w.float()[n_idx, j_idx] * inv_v)[:, None]
         out.index_add_(0, n_idx, d)
     return out
+
+
+def moe_decode_bf16_ref(x, topk_ids, topk_w, layer, expert_base=0, E=None):
+    """The reference's own decode algorithm (vq2_vllm/kernels/vq2_kernel.py:569-594 with its
+    defaults VQ2_BF16_ACT=1, VQ2_BF16_INTER=1): the Hadamard-rotated activation xh rounded to bf16
+    (:584), fp32 dot products, inter = silu(g) * u rounded to bf16 (:585-588), vb = had(inter)
+    rounded to bf16 (:589), fp32 down products weighted by w (:590-593). Dense dequantised
+    weights as in moe_ref; used to bound the decode kernel's error by the reference's own."""
+    x = x.float()
+    N, H = x.shape
+    E = layer["w13_lo"].shape[0] if E is None else E
+    I = layer["w13_lo"].shape[1] // 2
+    ids = topk_ids.long() - expert_base
+    out = torch.zeros(N, H, device=x.device)
+    bf = lambda t: t.bfloat16().float()
+    xh = bf(had_rows(bf(x)))
+    for e in torch.unique(ids).tolist():
+        if e < 0 or e >= E:
+            continue
+        n_idx, j_idx = torch.nonzero(ids == e, as_tuple=True)
+        wgu = dequant_rot(layer["w13_cb"], layer["w13_lo"][e], layer["w13_hi"][e], layer["w13_sc"][e])
+        wdn = dequant_rot(layer["w2_cb"], layer["w2_lo"][e], layer["w2_hi"][e], layer["w2_sc"][e])
+        g = xh[n_idx] @ wgu.T
+        a = bf(torch.nn.functional.silu(g[:, :I]) * g[:, I:])
+        d = bf(had_rows(a)) @ wdn.T
+        out.index_add_(0, n_idx, d * topk_w.float()[n_idx, j_idx, None])
+    return out

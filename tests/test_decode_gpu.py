@@ -114,3 +114,43 @@ def test_properties_full_size(big_layer):
     perm = torch.stack([torch.randperm(8, generator=torch.Generator().manual_seed(64 + n)) for n in range(N)]).cuda()
     got = f(ids.gather(1, perm), w1.gather(1, perm))
     assert torch_ref.rel_l2(got, f(ids, w1)) < 1e-5
+
+
+def _wide_range_layer(E, seed):
+    """A config-1 layer with real-model dynamic range: a heavy-tailed codebook (2 % of the entries
+    x25, max |C| about 60x the typical entry) and group scales spanning 2^-8 .. 2^4."""
+    from vq2_vllm import synth
+    L = synth.make_layer(E, 4096, 2048, seed=seed, device="cuda")
+    g = torch.Generator(device="cuda").manual_seed(seed + 1)
+    for key in ("w13_cb", "w2_cb"):
+        cb = L[key].float()
+        tail = torch.rand(cb.shape, generator=g, device="cuda") < 0.02
+        L[key] = torch.where(tail, cb * 25.0, cb).half()
+    for key in ("w13_sc", "w2_sc"):
+        ex = torch.randint(-8, 5, L[key].shape, generator=g, device="cuda").float()
+        L[key] = (torch.exp2(ex) * (0.75 + 0.5 * torch.rand(L[key].shape, generator=g, device="cuda"))).half()
+    return L
+
+
+@pytest.mark.parametrize("N,outlier", [(1, 50.0), (3, 100.0), (8, 100.0)])
+def test_wide_dynamic_range(N, outlier):
+    """Outlier activation channels (a few at 50-100 sigma, as real DS4 activations have), a
+    heavy-tailed codebook and scales over 2^-8..2^4 at the full config-1 width. The decode keeps
+    group partial sums in fp16 (power-of-two group scaling); it must stay within 1e-2 of the
+    fp32 oracle and no further from it than the reference's own decode algorithm (bf16
+    activations and intermediate, oracle/torch_ref.moe_decode_bf16_ref)."""
+    from vq2_vllm import synth
+    L = _wide_range_layer(64, seed=40 + N)
+    g = torch.Generator(device="cuda").manual_seed(50 + N)
+    x = torch.randn(N, 4096, generator=g, device="cuda")
+    ch = torch.randperm(4096, generator=g, device="cuda")[:6]
+    sign = torch.where(torch.rand(N, 6, generator=g, device="cuda") < 0.5, -1.0, 1.0)
+    x[:, ch] = sign * outlier * (0.5 + 0.5 * torch.rand(N, 6, generator=g, device="cuda"))
+    x = x.bfloat16()
+    ids, tw = synth.route_softmax_topk(x, 64, 8, w_std=0.02, seed=60 + N)
+    out = _moe()(x, ids, tw, *synth.layer_args(L))
+    ref = torch_ref.moe_ref(x, ids, tw, L)
+    ours = torch_ref.rel_l2(out, ref)
+    theirs = torch_ref.rel_l2(torch_ref.moe_decode_bf16_ref(x, ids, tw, L), ref)
+    assert ours < TOL, f"rel-L2 {ours:.3e} against fp32"
+    assert ours <= theirs * 1.05 + 1e-5, f"ours {ours:.3e} vs the reference algorithm's {theirs:.3e}"

@@ -82,3 +82,40 @@ def test_fused_layer_file_sharded_read(tmp_path):
         for k in layer:
             assert torch.equal(mine[k], ref[k]), (rank, k)
         assert mine["w13_lo"].shape[0] == 2 and mine["w13_cb"].shape == (1024, 4)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("N", [4, 300])
+def test_fused_layer_file_to_device_then_apply(tmp_path, N):
+    """Row f3 on the device: a fused layer file on disk, an expert-parallel rank's layer whose
+    parameters live on the GPU, the post-load hook reading only that rank's experts onto it, then
+    apply() on global expert ids — against the oracle over the same expert window."""
+    from types import SimpleNamespace
+
+    from safetensors.torch import save_file
+
+    from oracle import torch_ref
+    from vq2_vllm import synth
+    from vq2_vllm.plugin import apply_moe, param_shapes, process_weights_after_loading
+    E, H, I, world, rank = 16, 1024, 512, 4, 2
+    full = synth.make_layer(E, H, I, seed=5)
+    save_file({k: v.contiguous() for k, v in full.items()}, str(tmp_path / "experts_fused_layer_3.safetensors"))
+    per = E // world
+    params = {k: torch.empty(*shape, dtype=dt, device="cuda") for k, (shape, dt) in param_shapes(per, H, I).items()}
+    layer = SimpleNamespace(layer_name="model.layers.3.mlp.experts", local_num_experts=per, ep_rank=rank,
+                            **{k: torch.nn.Parameter(v, requires_grad=False) for k, v in params.items()})
+    assert process_weights_after_loading(layer, directory=str(tmp_path))
+    assert layer.vq2_expert_base == rank * per
+    for k, v in full.items():
+        want = v if k.endswith("cb") else v[rank * per:(rank + 1) * per]
+        assert torch.equal(getattr(layer, k).cpu(), want), k
+    x = synth.make_tokens(N, H, seed=6, device="cuda")
+    ids, w = synth.route_uniform(N, E, 8, seed=7, device="cuda")
+    out = apply_moe(layer, x, w, ids).float()
+    Lc = {k: v.cuda() for k, v in full.items()}
+    win = {k: (v if k.endswith("cb") else v[rank * per:(rank + 1) * per]) for k, v in Lc.items()}
+    f = torch_ref.moe_ref if N < 256 else torch_ref.moe_prefill_fp8_ref
+    ref = f(x, ids, w, win, expert_base=rank * per)
+    assert torch_ref.rel_l2(out, ref) < 3e-2
+    other = SimpleNamespace(layer_name="model.layers.9.mlp.experts", **params)
+    assert not process_weights_after_loading(other, directory=str(tmp_path))   # no file: nothing read

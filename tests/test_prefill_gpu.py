@@ -4,6 +4,8 @@ fp16 operands: within 3e-2 relative L2 of the fp32 dequant+matmul oracle (the pr
 fp8 operands: the reference's fp8 algorithm — within 3e-2 of the oracle's fp8 restatement
 (oracle/torch_ref.moe_prefill_fp8_ref, pinned to the numpy oracle); its distance to fp32 is the
 reference algorithm's own (about 7 % on these weights) and is only bounded loosely here."""
+import os
+
 import pytest
 import torch
 
@@ -72,8 +74,14 @@ def test_decode_entry_routes_large_batches_to_grouped(small):
     N = 600
     x = synth.make_tokens(N, 512, seed=11, device="cuda")
     ids, tw = synth.route_zipf(N, 8, 2, seed=12, device="cuda")
-    out = vq2_moe_fused_10b(x, ids, tw, *synth.layer_args(small))
-    assert torch_ref.rel_l2(out, torch_ref.moe_ref(x, ids, tw, small)) < TOL
+    out = vq2_moe_fused_10b(x, ids, tw, *synth.layer_args(small))      # VQ2_FP8_PREFILL default: fp8
+    assert torch_ref.rel_l2(out, torch_ref.moe_prefill_fp8_ref(x, ids, tw, small)) < TOL
+    os.environ["VQ2_FP8_PREFILL"] = "0"
+    try:
+        out16 = vq2_moe_fused_10b(x, ids, tw, *synth.layer_args(small))
+    finally:
+        del os.environ["VQ2_FP8_PREFILL"]
+    assert torch_ref.rel_l2(out16, torch_ref.moe_ref(x, ids, tw, small)) < TOL
 
 
 def test_prefill_fp8_linear_in_routing_weights():
@@ -87,3 +95,28 @@ def test_prefill_fp8_linear_in_routing_weights():
     w2 = torch.rand_like(w1)
     f = lambda w: vq2_moe_grouped_wmma(x, ids, w, *synth.layer_args(L), precision="fp8")
     assert torch_ref.rel_l2(f(2.0 * w1 + 0.5 * w2), 2.0 * f(w1) + 0.5 * f(w2)) < 1e-5
+
+
+@pytest.fixture(scope="module")
+def config2():
+    """The exact config-2 layer and routing: 8,192 tokens, 256 experts, H=4096, I=2048, Zipf(1.1)
+    top-8 (65,536 pairs; Pmax 98,304 at 128-slot blocks, 768 blocks)."""
+    from vq2_vllm import synth
+    L = synth.make_layer(256, 4096, 2048, seed=10, device="cuda")
+    x = synth.make_tokens(8192, 4096, seed=300, device="cuda")
+    ids, tw = synth.route_zipf(8192, 256, 8, s=1.1, seed=301, device="cuda")
+    return L, x, ids, tw
+
+
+@pytest.mark.parametrize("prec", ["fp8", "f16"])
+def test_config2_full_size(config2, prec):
+    """The benchmark's prefill configuration end to end: multi-chunk align feeding the GEMMs,
+    the heaviest Zipf experts spanning dozens of blocks, every block pair of the grid."""
+    L, x, ids, tw = config2
+    out = _run(x, ids, tw, L, prec)
+    if prec == "fp8":
+        ref = torch_ref.moe_prefill_fp8_ref(x, ids, tw, L)
+    else:
+        ref = torch_ref.moe_ref(x, ids, tw, L)
+    assert torch_ref.rel_l2(out, ref) < TOL
+    assert torch.isfinite(out).all()

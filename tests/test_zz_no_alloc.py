@@ -13,7 +13,7 @@ import pytest
 import torch
 
 pytestmark = pytest.mark.gpu
-TOL = 1e-2
+TOL = 1e-5   # same kernels; only the order of the fp32 output atomics differs
 
 
 def _call(entry, layer, x, ids, tw):
