@@ -92,6 +92,24 @@ class Clocks:
                 "reasons": reasons, "samples": len(rows)}
 
 
+def cpu_model():
+    """Host CPU model name (for the CPU baselines), from /proc/cpuinfo."""
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return None
+
+
+# DRAM bytes (read + write) per distinct expert of one decode layer call, from the ncu capture in
+# profiles/decode_config1_b1.txt (69.97 MB over 8 distinct experts, both kernels), so the roofline
+# line scales it to its own run's distinct-expert count.
+NCU_DECODE_BYTES_PER_EXPERT = 69.97e6 / 8
+
+
 def make_routing(x, seed):
     from vq2_vllm import synth
     return synth.route_softmax_topk(x, E, K, w_std=0.02, seed=seed)
@@ -322,7 +340,8 @@ def run_reference(args, rank, world):
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": v / 1e3, "higher_is_better": False,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": "config1 decode batch 1 (CPU sample)", "H": H, "I": I, "E": E, "topk": K},
-            "cpu_baseline": {"value": v, "unit": "us/token", "cores": threads, "kind": "port", "sample": sample},
+            "cpu_baseline": {"value": v, "unit": "us/token", "cores": threads, "kind": "port", "sample": sample,
+                             "cpu_model": cpu_model()},
             "e2e": {"value": v, "unit": "us/token", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
 
@@ -419,20 +438,18 @@ def run_ours(args, rank, world):
     all_bytes = idx_bytes + u1 * SC_BYTES_PER_EXPERT + 2 * 8192
     achieved = idx_bytes / (ms1 * 1e-3) / 1e9
 
-    # e2e: the public API with host buffers; H2D of x / ids / weights and D2H of the output
-    from vq2_vllm.kernels.vq2_kernel import vq2_moe_fused_10b
+    # e2e: the public host-buffer entry (vq2_moe_fused_10b_host -> vq2_decode_host): every step
+    # copies its token row, ids and routing weights from page-locked host memory to the device and
+    # the fp32 result back, inside the timed region
+    from vq2_vllm.kernels.vq2_kernel import vq2_moe_fused_10b_host
     xh = [x.cpu().pin_memory() for x in [synth.make_tokens(1, H, seed=100 + j) for j in range(8)]]
     rh = [(r[0].cpu().pin_memory(), r[1].cpu().pin_memory()) for r in
           [make_routing(synth.make_tokens(1, H, seed=100 + j, device=dev), 200 + j) for j in range(8)]]
-    outh = torch.empty(1, H, dtype=torch.float32).pin_memory()
+    outh = [torch.empty(1, H, dtype=torch.float32).pin_memory() for _ in range(2)]
 
     def e2e_step(i):
         L = layers[i % nlayers]
-        x = xh[i % 8].to(dev, non_blocking=True)
-        ids = rh[i % 8][0].to(dev, non_blocking=True)
-        tw = rh[i % 8][1].to(dev, non_blocking=True)
-        out = vq2_moe_fused_10b(x, ids, tw, *synth.layer_args(L))
-        outh.copy_(out, non_blocking=True)
+        vq2_moe_fused_10b_host(xh[i % 8], rh[i % 8][0], rh[i % 8][1], *synth.layer_args(L), out=outh[i % 2])
 
     for i in range(3):
         e2e_step(i)
@@ -482,14 +499,17 @@ def run_ours(args, rank, world):
                          "frac": achieved / hbm,
                          # dram read+write of one layer call (both decode kernels), from the ncu
                          # capture summarised in profiles/decode_config1_b1.txt (8 distinct experts)
-                         "traffic": 69.97e6, "traffic_unit": "bytes per layer call",
+                         "traffic": NCU_DECODE_BYTES_PER_EXPERT * u1, "traffic_unit": "bytes per layer call",
+                         "traffic_source": "ncu dram read+write per distinct expert (profiles/decode_config1_b1.txt) x this run's distinct experts",
                          "kernel": "decode layer call (gate/up + down kernels, CUDA events around both)",
                          "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src,
                          "bytes": "index planes of distinct experts + x + out per layer call",
                          "achieved_incl_scales": all_bytes / (ms1 * 1e-3) / 1e9},
             "cpu_baseline": {"value": cpu_v, "unit": "us/token", "cores": os.cpu_count(), "kind": "port",
+                             "cpu_model": cpu_model(),
                              "sample": cpu_sample},
             "cpu_baseline_prefill": {"value": cpu_pf, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                                     "cpu_model": cpu_model(),
                                      "sample": cpu_pf_sample},
             "e2e": {"value": e2e_ms * 1e3, "unit": "us/token", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "prefill": prefill,
@@ -596,6 +616,32 @@ def run_ref_gpu(args):
     print(json.dumps(out), flush=True)
 
 
+def run_profile_case(case):
+    """--profile-case: a small, self-contained invocation of one hot kernel for ncu captures (a few
+    GB on the device at most, a handful of launches): "decode" = four config-1 decode layer calls
+    at batch 1 over two layers; "prefill" = two fp8 grouped-GEMM calls, 2048 tokens over 64
+    experts, Zipf(1.1) top-8 (a small case of the config-2 kernels)."""
+    from vq2_vllm import synth
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    if case == "decode":
+        from vq2_vllm.kernels.vq2_kernel import vq2_moe_fused_10b
+        layers = [synth.make_layer(E, H, I, seed=s, device=dev) for s in range(2)]
+        x = synth.make_tokens(1, H, seed=1, device=dev)
+        ids, tw = make_routing(x, 2)
+        for i in range(4):
+            vq2_moe_fused_10b(x, ids, tw, *synth.layer_args(layers[i % 2]))
+    else:
+        from vq2_vllm.kernels.ds4_vq2_cuda import vq2_moe_grouped_wmma
+        L = synth.make_layer(64, H, I, seed=0, device=dev)
+        x = synth.make_tokens(2048, H, seed=1, device=dev)
+        ids, tw = synth.route_zipf(2048, 64, K, seed=2, device=dev)
+        for _ in range(2):
+            vq2_moe_grouped_wmma(x, ids, tw, *synth.layer_args(L), precision="fp8")
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": case, "ok": True}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -606,7 +652,11 @@ def main():
     ap.add_argument("--soak", type=float, default=0.6, help="untimed seconds before the timed decode steps")
     ap.add_argument("--ref-gpu", action="store_true",
                     help="time the reference's own GPU path (baseline/_ref) beside ours; one JSON line")
+    ap.add_argument("--profile-case", choices=["decode", "prefill"],
+                    help="run a small invocation of one hot kernel (for ncu captures) and exit")
     args = ap.parse_args()
+    if args.profile_case:
+        return run_profile_case(args.profile_case)
     if args.ref_gpu:
         return run_ref_gpu(args)
     rank = int(os.environ.get("RANK", 0))

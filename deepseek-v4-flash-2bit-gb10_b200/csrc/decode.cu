@@ -783,6 +783,46 @@ extern "C" int vq2_decode(const vq2_moe_args* a, void* ws, size_t ws_bytes, void
   if (cudaLaunchKernelEx(&cfg, kb, args, (const float*)part, khA) != cudaSuccess) return VQ2_ERR_CUDA;
   return VQ2_OK;
 }
+// ------------------------------------------------------------------ decode from host buffers
+// One call per decode step for a caller whose inputs and result live in host memory: the three
+// input copies, both kernels and the output copy are queued on `stream` from C, so a step costs
+// one library call on the host. Device staging (caller-owned) holds x | ids | w | out.
+static size_t stage_part(size_t b) { return (b + 255) & ~(size_t)255; }
+
+extern "C" size_t vq2_decode_host_stage_size(int N, int topk, int H, int x_dtype, int ids_dtype) {
+  if (N <= 0 || topk <= 0 || H <= 0) return 0;
+  const size_t xe = x_dtype == VQ2_DT_F32 ? 4 : 2, ie = ids_dtype == VQ2_ID_I64 ? 8 : 4;
+  return stage_part((size_t)N * H * xe) + stage_part((size_t)N * topk * ie) + stage_part((size_t)N * topk * 4) +
+         stage_part((size_t)N * H * 4) + 256;
+}
+
+extern "C" int vq2_decode_host(const vq2_moe_args* a, const void* h_x, const void* h_ids, const float* h_w,
+                               float* h_out, void* stage, size_t stage_bytes, void* ws, size_t ws_bytes,
+                               void* stream) {
+  if (!a || !h_x || !h_ids || !h_w || !h_out || !stage) return VQ2_ERR_NULL;
+  if (a->N <= 0 || a->topk <= 0 || a->H <= 0) return VQ2_ERR_SHAPE;
+  if (a->x_dtype < 0 || a->x_dtype > 2 || a->ids_dtype < 0 || a->ids_dtype > 1) return VQ2_ERR_DTYPE;
+  if (stage_bytes < vq2_decode_host_stage_size(a->N, a->topk, a->H, a->x_dtype, a->ids_dtype))
+    return VQ2_ERR_WORKSPACE;
+  const size_t xb = (size_t)a->N * a->H * (a->x_dtype == VQ2_DT_F32 ? 4 : 2);
+  const size_t ib = (size_t)a->N * a->topk * (a->ids_dtype == VQ2_ID_I64 ? 8 : 4);
+  const size_t wb = (size_t)a->N * a->topk * 4, ob = (size_t)a->N * a->H * 4;
+  uint8_t* d = (uint8_t*)(((uintptr_t)stage + 255) & ~(uintptr_t)255);
+  vq2_moe_args b = *a;
+  b.x = d;
+  b.topk_ids = d + stage_part(xb);
+  b.topk_w = (const float*)(d + stage_part(xb) + stage_part(ib));
+  b.out = (float*)(d + stage_part(xb) + stage_part(ib) + stage_part(wb));
+  cudaStream_t st = (cudaStream_t)stream;
+  if (cudaMemcpyAsync((void*)b.x, h_x, xb, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync((void*)b.topk_ids, h_ids, ib, cudaMemcpyHostToDevice, st) != cudaSuccess ||
+      cudaMemcpyAsync((void*)b.topk_w, h_w, wb, cudaMemcpyHostToDevice, st) != cudaSuccess)
+    return VQ2_ERR_CUDA;
+  const int rc = vq2_decode(&b, ws, ws_bytes, stream);
+  if (rc) return rc;
+  return cudaMemcpyAsync(h_out, b.out, ob, cudaMemcpyDeviceToHost, st) == cudaSuccess ? VQ2_OK : VQ2_ERR_CUDA;
+}
+
 static_assert(offsetof(vq2::DecodeShared, xs) % 16 == 0, "xs must be 16-byte aligned");
 static_assert(offsetof(vq2::DecodeShared, scratch) % 16 == 0, "bulk-copy destination must be 16-byte aligned");
 static_assert(offsetof(vq2::DecodeShared, ekey) % 16 == 0, "ekey is read as int4");

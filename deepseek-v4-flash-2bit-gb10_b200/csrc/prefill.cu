@@ -33,60 +33,6 @@ namespace vq2 {
 int launch_align_ex(const void* ids, int dt, long N, int k, int E, int BM, int base, int drop, int32_t* st,
                     int32_t* ss, uint8_t* val, int32_t* be, int* counts, cudaStream_t stream);
 
-constexpr int PF_BM = 128;            // slots per block (MMA M)
-constexpr int PF_BN = 256;            // weight rows per tile (MMA N)
-constexpr int PF_MB = 2;              // blocks of one expert sharing each decoded B tile
-constexpr int PF_STAGES = 2;          // ring of A tiles (PF_MB blocks each): TMA from L2
-constexpr int PF_ISTAGES = 3;         // ring of staged index planes: run ahead of the activations
-constexpr int PF_BSTAGES = 2;         // ring of decoded B tiles: produced in the CTA
-constexpr int PF_DEC_WARPS = 16;      // decoders; four per TMEM lane quarter in the epilogue
-constexpr int PF_THREADS = (3 + PF_DEC_WARPS) * 32;   // A loader, index loader, MMA issuer, decoders
-constexpr int PF_TILE = 16384;        // one 128-row x 128-byte activation tile
-constexpr int PF_BTILE = PF_BN * 128; // the weight tile: 256 rows x 128 bytes
-constexpr int PF_ATILE = PF_MB * PF_TILE;
-constexpr int PF_CB_COPIES = 8;
-constexpr int PF_CB_BYTES = 1024 * 8 * PF_CB_COPIES;
-constexpr int PF_IDX = 11264;  // staged index planes of one stage: lo 8192 B, hi 2048 B, sc 1024 B
-constexpr int PF_IDX_HI = 8192, PF_IDX_SC = 10240;
-static_assert(PF_IDX % 16 == 0, "index stages keep 16-byte alignment");
-constexpr int PF_TMEM_COLS = PF_MB * PF_BN;
-
-struct PfShared {
-  uint64_t full_a[PF_STAGES];
-  uint64_t empty[PF_STAGES];
-  uint64_t full_i[PF_ISTAGES];
-  uint64_t empty_i[PF_ISTAGES];
-  uint64_t full_b[PF_BSTAGES];
-  uint64_t empty_b[PF_BSTAGES];
-  uint64_t done[2];             // per pass: all MMAs of the pass complete
-  uint64_t cbbar;
-  uint32_t tmem_base;
-};
-
-constexpr size_t PF_SMEM = (size_t)PF_CB_BYTES + (size_t)PF_STAGES * PF_ATILE + (size_t)PF_ISTAGES * PF_IDX + (size_t)PF_BSTAGES * PF_BTILE +
-                           sizeof(PfShared) + 1024;
-
-struct PfGemmArgs {
-  const uint8_t* act;        // activation rows (token rows for gate/up, slot rows for down)
-  const float* inv_act;      // per activation row: inverse quantisation scale
-  const int32_t* st;         // sorted_tok [Pmax]
-  const int32_t* ss;         // sorted_slot [Pmax]
-  const uint8_t* val;        // valid [Pmax]
-  const int32_t* be;         // block -> local expert
-  const uint8_t* lo;
-  const uint8_t* hi;
-  const uint16_t* sc;
-  const uint16_t* cb;
-  const float* topk_w;
-  float* inter;              // gate/up output [Pmax, I]
-  float* out;                // down output [N, H]
-  int K;                     // input width (elements)
-  int R;                     // weight rows per expert (2I or H)
-  int I;
-  int H;
-  int topk;
-};
-
 // ------------------------------------------------------------------ tcgen05 helpers
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 B apart (stride
 // byte offset), leading byte offset unused for this layout (1), descriptor version 1 (sm_100).
@@ -98,22 +44,6 @@ __device__ __forceinline__ uint64_t umma_desc_sw128(uint32_t saddr) {
   d |= (uint64_t)1 << 46;
   d |= (uint64_t)2 << 61;
   return d;
-}
-
-// Instruction descriptor: D fp32, A/B format 0 (e4m3 for kind::f8f6f4, f16 for kind::f16),
-// both K-major, N = 128, M = 128.
-constexpr uint32_t PF_IDESC = (1u << 4) | ((uint32_t)(PF_BN >> 3) << 17) | ((uint32_t)(PF_BM >> 4) << 24);
-
-template <int PREC>
-__device__ __forceinline__ void umma(uint32_t tmem_d, uint64_t da, uint64_t db, uint32_t acc) {
-  if (PREC == VQ2_PREC_FP8)
-    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-                 " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n}"
-                 ::"r"(tmem_d), "l"(da), "l"(db), "r"(PF_IDESC), "r"(acc));
-  else
-    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-                 " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}"
-                 ::"r"(tmem_d), "l"(da), "l"(db), "r"(PF_IDESC), "r"(acc));
 }
 
 __device__ __forceinline__ void umma_commit(uint64_t* bar) {
@@ -162,318 +92,404 @@ __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commi
 template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
-// byte offset of 16-byte chunk kc of row r in a 128 x 128-byte SW128 K-major tile
-__device__ __forceinline__ uint32_t sw128_off(int r, int kc) {
-  return (uint32_t)((r >> 3) * 1024 + (r & 7) * 128 + ((kc ^ (r & 7)) << 4));
-}
-
-// ------------------------------------------------------------------ weight tile decode
-// Decoder thread (row r, quarter h) fills 16-byte chunks 2h, 2h+1 of B row r of one stage:
-// fp8: 8 sub-vectors -> 32 e4m3 values = e4m3(sat(C[id] * sc)) (reference vq2_grouped.cu:434-446);
-// f16: 4 sub-vectors -> 16 f16 values C[id] * sc. lo: the sub-vectors' low bytes (little-endian
-// in lo.x, lo.y); hw: their hi bits (2 per sub-vector from bit 0). cbl: this lane's codebook copy.
-template <int PREC>
-__device__ __forceinline__ void decode_b_quarter(uint32_t cbl, uint2 lo, uint32_t hw, float scf, uint32_t tile,
-                                                 int r, int h) {
-  if (PREC == VQ2_PREC_FP8) {
+// ------------------------------------------------------------------ weight decode into registers
+// fp8: the 16 sub-vectors of one 64-group of a weight row (lo: their 16 low index bytes, hw: their
+// 4 hi bytes, scf: the group scale) -> 16 words of 4 e4m3 values, e4m3(sat(C[id] * sc)) with the
+// product exact in fp32 and one rounding (reference vq2_grouped.cu:434-446).
+// cbl: this lane's codebook copy (entries 128 bytes apart: 16 copies, lane l reads copy l mod 16,
+// so a warp's 8-byte gathers are conflict-free).
+__device__ __forceinline__ void decode16_fp8(uint32_t cbl, uint4 lo, uint32_t hw, float scf, uint32_t* v) {
+  const float2 s2 = make_float2(scf, scf);
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {            // chunk 2h+q: sub-vectors 4q..4q+3
-      uint32_t ids[2];
-      unpack_ids4(q ? lo.y : lo.x, (hw >> (8 * q)) & 0xFFu, ids[0], ids[1]);
-      uint32_t packed[4];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        const uint32_t id = (j & 2) ? (ids[j & 1] >> 16) : (ids[j & 1] & 0xFFFFu);
-        const uint2 c = lds64(cbl + (id << 6));
-        const float2 a = __half22float2(*(const __half2*)&c.x), b = __half22float2(*(const __half2*)&c.y);
-        const __nv_fp8x2_storage_t p0 = __nv_cvt_float2_to_fp8x2(make_float2(a.x * scf, a.y * scf), __NV_SATFINITE, __NV_E4M3);
-        const __nv_fp8x2_storage_t p1 = __nv_cvt_float2_to_fp8x2(make_float2(b.x * scf, b.y * scf), __NV_SATFINITE, __NV_E4M3);
-        packed[j] = (uint32_t)p0 | ((uint32_t)p1 << 16);
-      }
-      sts128_v(tile + sw128_off(r, 2 * h + q), make_uint4(packed[0], packed[1], packed[2], packed[3]));
-    }
-  } else {
-    const __half2 s2 = __float2half2_rn(scf);
+  for (int q = 0; q < 4; ++q) {
     uint32_t ids[2];
-    unpack_ids4(lo.x, hw & 0xFFu, ids[0], ids[1]);
+    unpack_ids4(q == 0 ? lo.x : q == 1 ? lo.y : q == 2 ? lo.z : lo.w, (hw >> (8 * q)) & 0xFFu, ids[0], ids[1]);
 #pragma unroll
-    for (int q = 0; q < 2; ++q) {            // chunk 2h+q: sub-vectors 2q, 2q+1 (8 f16)
-      uint32_t w[4];
-#pragma unroll
-      for (int jj = 0; jj < 2; ++jj) {
-        const int j = 2 * q + jj;
-        const uint32_t id = (j & 2) ? (ids[j & 1] >> 16) : (ids[j & 1] & 0xFFFFu);
-        const uint2 c = lds64(cbl + (id << 6));
-        const __half2 v0 = __hmul2(*(const __half2*)&c.x, s2), v1 = __hmul2(*(const __half2*)&c.y, s2);
-        w[2 * jj] = *(const uint32_t*)&v0;
-        w[2 * jj + 1] = *(const uint32_t*)&v1;
-      }
-      sts128_v(tile + sw128_off(r, 2 * h + q), make_uint4(w[0], w[1], w[2], w[3]));
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t id = (j & 2) ? (ids[j & 1] >> 16) : (ids[j & 1] & 0xFFFFu);
+      const uint2 c = lds64(cbl + (id << 7));
+      const float2 x0 = fmul2(__half22float2(*(const __half2*)&c.x), s2);
+      const float2 x1 = fmul2(__half22float2(*(const __half2*)&c.y), s2);
+      const __nv_fp8x2_storage_t p0 = __nv_cvt_float2_to_fp8x2(x0, __NV_SATFINITE, __NV_E4M3);
+      const __nv_fp8x2_storage_t p1 = __nv_cvt_float2_to_fp8x2(x1, __NV_SATFINITE, __NV_E4M3);
+      v[4 * q + j] = (uint32_t)p0 | ((uint32_t)p1 << 16);
     }
   }
+}
+
+// f16: 8 sub-vectors of a row (lo: 8 low index bytes, hw: 2 hi bytes) -> 16 words of 2 f16 values,
+// C[id] * sc in fp16.
+__device__ __forceinline__ void decode8_f16(uint32_t cbl, uint2 lo, uint32_t hw, float scf, uint32_t* v) {
+  const __half2 s2 = __float2half2_rn(scf);
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    uint32_t ids[2];
+    unpack_ids4(q ? lo.y : lo.x, (hw >> (8 * q)) & 0xFFu, ids[0], ids[1]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t id = (j & 2) ? (ids[j & 1] >> 16) : (ids[j & 1] & 0xFFFFu);
+      const uint2 c = lds64(cbl + (id << 7));
+      const __half2 a0 = __hmul2(*(const __half2*)&c.x, s2), a1 = __hmul2(*(const __half2*)&c.y, s2);
+      v[2 * (4 * q + j)] = *(const uint32_t*)&a0;
+      v[2 * (4 * q + j) + 1] = *(const uint32_t*)&a1;
+    }
+  }
+}
+
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+               ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
+                 "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
+               : "memory");
+}
+__device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// D (TMEM) += A (TMEM, M = 128 weight rows, K-major) . B (shared memory descriptor, N slots)^T
+template <int PREC>
+__device__ __forceinline__ void umma_tmem_a(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc,
+                                            uint32_t acc) {
+  if (PREC == VQ2_PREC_FP8)
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                 " tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n}"
+                 ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc));
+  else
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                 " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}"
+                 ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc));
 }
 
 // ------------------------------------------------------------------ grouped GEMM kernel
-// grid (tiles along N, pairs of 128-slot blocks). GATEUP: tile n covers gate rows [128n, 128n+128)
-// and the matching up rows; the epilogue writes inter. Otherwise tile n covers output rows
-// [256n, 256n+256) and the epilogue accumulates into out. Two blocks of the same expert run as
-// one pass (each decoded B tile feeds two MMAs, two TMEM accumulators); two blocks of different
-// experts run as two passes, one accumulator each.
+// Persistent; one CTA per SM walks the work list w = blockIdx.x, blockIdx.x + gridDim.x, ...
+// (w -> chunk w / T, row tile w % T; chunks heaviest first). A work item is one chunk of up to
+// P2_NMAX consecutive slots of one expert (its tokens, padded to P2_BM) against P2_NT x 128
+// weight rows: GATEUP = 128 gate rows and the 128 matching up rows of tile t; otherwise 256
+// down rows. Per 128-byte K stage the decoder warps write the decoded rows into tensor memory
+// (the MMA's A operand, one 128-lane tile per 128 rows), warp 0 loads the chunk's activation rows
+// by TMA (B operand), warp 2 issues M=128 x N=slots MMAs into one TMEM accumulator per row tile.
+// The epilogue reads the accumulators (lane = weight row, column = slot): gate/up writes
+// inter[slot][i] = silu(g * inv) * (u * inv) (reference vq2_grouped.cu:255-264); down adds
+// acc * w * inv_vb into out[token] with fp32 reductions.
+constexpr int P2_ROWS = 128;                 // weight rows per A tile (MMA M)
+constexpr int P2_NT = 2;                     // A tiles per work item
+constexpr int P2_NMAX = 192;                 // slots per chunk (MMA N at most)
+constexpr int P2_BM = 32;                    // per-expert slot padding (moe_align block)
+constexpr int P2_CHUNK_BLOCKS = P2_NMAX / P2_BM;
+constexpr int P2_BSTAGES = 2, P2_ISTAGES = 3, P2_ASTAGES = 2;
+constexpr int P2_DEC_WARPS = 16;
+constexpr int P2_THREADS = (3 + P2_DEC_WARPS) * 32;
+constexpr int P2_BTILE = P2_NMAX * 128;      // one B stage: 192 slot rows x 128 bytes (SW128)
+constexpr int P2_CB_COPIES = 16;
+constexpr int P2_CB_BYTES = 1024 * 8 * P2_CB_COPIES;
+constexpr int P2_IDX = 11264;                // index planes of one stage: lo 256 x 32, hi 256 x 8, sc 256 x 4
+constexpr int P2_IDX_HI = 8192, P2_IDX_SC = 10240;
+constexpr uint32_t P2_TMEM_COLS = 512;
+// TMEM columns: accumulator of tile 0 at 0 (N <= 192), A stage 0 at 192 (2 tiles x 32 columns),
+// accumulator of tile 1 at 256, A stage 1 at 448.
+__host__ __device__ constexpr uint32_t p2_acc_col(int t) { return t ? 256u : 0u; }
+__host__ __device__ constexpr uint32_t p2_a_col(int s, int t) { return (s ? 448u : 192u) + 32u * t; }
 
-template <bool GATEUP>
-__device__ __forceinline__ long pf_weight_row(const PfGemmArgs& a, int e, int tile, int r) {
-  constexpr int HALF = PF_BN / 2;
-  if (GATEUP) return (long)e * a.R + (r < HALF ? tile * HALF + r : a.I + tile * HALF + (r - HALF));
-  return (long)e * a.R + tile * PF_BN + r;
-}
+struct P2Shared {
+  uint64_t full_b[P2_BSTAGES], empty_b[P2_BSTAGES];
+  uint64_t full_i[P2_ISTAGES], empty_i[P2_ISTAGES];
+  uint64_t full_a[P2_ASTAGES], empty_a[P2_ASTAGES];
+  uint64_t done, acc_empty, cbbar, drain;
+  uint32_t tmem_base;
+  int abort;
+};
+constexpr size_t P2_SMEM = (size_t)P2_CB_BYTES + (size_t)P2_BSTAGES * P2_BTILE + (size_t)P2_ISTAGES * P2_IDX +
+                           sizeof(P2Shared) + 1024;
+static_assert(P2_SMEM <= 227 * 1024, "prefill GEMM shared memory");
 
-struct PfPass {
-  int blk;      // first block of the pass
-  int mb;       // blocks in the pass (1 or 2)
-  int e;        // local expert
-  int acc;      // first TMEM accumulator
+struct P2Args {
+  const int4* chunks;        // {expert, first slot, slots, 0}, heaviest first
+  const int* nchunks;        // device count of chunks
+  const float* inv_slot;     // per slot: inverse quantisation scale of its activation row
+  const int32_t* st;         // sorted_tok [Pmax]
+  const int32_t* ss;         // sorted_slot [Pmax]
+  const uint8_t* val;        // valid [Pmax]
+  const uint8_t* lo;
+  const uint8_t* hi;
+  const uint16_t* sc;
+  const uint16_t* cb;
+  const float* topk_w;
+  float* inter;              // gate/up output [Pmax, I]
+  float* out;                // down output [N, H]
+  int K;                     // input width (elements)
+  int R;                     // weight rows per expert (2I or H)
+  int I, H, topk;
+  int T;                     // row tiles per chunk
 };
 
-template <int PREC, bool GATEUP>
-__global__ void __launch_bounds__(PF_THREADS, 1)
-prefill_gemm_kernel(PfGemmArgs a, const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_lo,
-                    int nblk) {
-  extern __shared__ __align__(1024) uint8_t pf_smem_raw[];
-  uint8_t* smem = (uint8_t*)(((uintptr_t)pf_smem_raw + 1023) & ~(uintptr_t)1023);
-  uint8_t* cbs = smem;
-  uint8_t* atiles = smem + PF_CB_BYTES;                // A ring (PF_MB tiles per stage)
-  uint8_t* btiles = atiles + PF_STAGES * PF_ATILE;     // B ring
-  uint8_t* itiles = btiles + PF_BSTAGES * PF_BTILE;    // index-plane ring
-  PfShared* sh = (PfShared*)(itiles + PF_ISTAGES * PF_IDX);
-  const int tile = blockIdx.x, b0 = blockIdx.y * PF_MB;
-  if (!a.val[(size_t)b0 * PF_BM]) return;            // blocks past the last expert hold no pair
-  const bool v1 = b0 + 1 < nblk && a.val[(size_t)(b0 + 1) * PF_BM];
-  const int e0 = a.be[b0], e1 = v1 ? a.be[b0 + 1] : -1;
-  // at most two passes, kept in registers (a run-time-indexed array would live in local memory)
-  PfPass pass0, pass1 = {b0 + 1, 1, e1, 1};
-  int npass;
-  if (v1 && e1 == e0) { pass0 = {b0, 2, e0, 0}; npass = 1; }
-  else if (v1) { pass0 = {b0, 1, e0, 0}; npass = 2; }
-  else { pass0 = {b0, 1, e0, 0}; npass = 1; }
-  auto pass_of = [&](int pi) { return pi == 0 ? pass0 : pass1; };
+// weight row of A tile t, lane r, for row tile `tile` of expert e
+template <bool GATEUP>
+__device__ __forceinline__ long p2_weight_row(const P2Args& a, int e, int tile, int t, int r) {
+  if (GATEUP) return (long)e * a.R + (long)t * a.I + tile * P2_ROWS + r;
+  return (long)e * a.R + (long)tile * (P2_NT * P2_ROWS) + t * P2_ROWS + r;
+}
 
+template <int PREC, bool GATEUP>
+__global__ void __launch_bounds__(P2_THREADS, 1)
+prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const __grid_constant__ CUtensorMap tm_lo) {
+  extern __shared__ __align__(1024) uint8_t p2_smem_raw[];
+  uint8_t* smem = (uint8_t*)(((uintptr_t)p2_smem_raw + 1023) & ~(uintptr_t)1023);
+  uint8_t* cbs = smem;
+  uint8_t* btiles = smem + P2_CB_BYTES;
+  uint8_t* itiles = btiles + P2_BSTAGES * P2_BTILE;
+  P2Shared* sh = (P2Shared*)(itiles + P2_ISTAGES * P2_IDX);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   constexpr int elem = PREC == VQ2_PREC_FP8 ? 1 : 2;
-  constexpr int KE = 128 / elem;                      // K elements per stage (128 bytes per row)
-  const int nchunks = a.K / KE;
+  constexpr int KE = 128 / elem;               // K elements per stage (128 bytes)
+  constexpr int LOB = KE / 4;                  // lo bytes per row per stage
+  const int nstage = a.K / KE;
   const int nsub = a.K / 4, ngk = a.K / 64;
-  auto A_t = [&](int slot) { return atiles + slot * PF_ATILE; };
-  auto B_t = [&](int slot) { return btiles + slot * PF_BTILE; };
-  auto I_t = [&](int slot) { return itiles + slot * PF_IDX; };   // lo | hi | sc
+  const int nwork = *a.nchunks * a.T;
+  auto B_t = [&](int slot) { return btiles + slot * P2_BTILE; };
+  auto I_t = [&](int slot) { return itiles + slot * P2_IDX; };
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < PF_STAGES; ++s) {
-      mbar_init(&sh->full_a[s], 1);         // TMA bytes
-      mbar_init(&sh->empty[s], 1);
-    }
-    for (int s = 0; s < PF_ISTAGES; ++s) {
-      mbar_init(&sh->full_i[s], 33);        // TMA bytes (1 arrival) + 32 lanes' cp.async
-      mbar_init(&sh->empty_i[s], PF_DEC_WARPS);
-    }
-    for (int s = 0; s < PF_BSTAGES; ++s) {
-      mbar_init(&sh->full_b[s], PF_DEC_WARPS);
-      mbar_init(&sh->empty_b[s], 1);
-    }
-    mbar_init(&sh->done[0], 1);
-    mbar_init(&sh->done[1], 1);
+    for (int s = 0; s < P2_BSTAGES; ++s) { mbar_init(&sh->full_b[s], 1); mbar_init(&sh->empty_b[s], 1); }
+    for (int s = 0; s < P2_ISTAGES; ++s) { mbar_init(&sh->full_i[s], 33); mbar_init(&sh->empty_i[s], P2_DEC_WARPS); }
+    for (int s = 0; s < P2_ASTAGES; ++s) { mbar_init(&sh->full_a[s], P2_DEC_WARPS); mbar_init(&sh->empty_a[s], 1); }
+    mbar_init(&sh->done, 1);
+    mbar_init(&sh->acc_empty, P2_DEC_WARPS);
     mbar_init(&sh->cbbar, 1);
+    mbar_init(&sh->drain, 1);
+    sh->abort = 0;
     fence_mbar_init();
     mbar_arrive_expect_tx(&sh->cbbar, 1024 * 8);
-    bulk_g2s(B_t(0), a.cb, 1024 * 8, &sh->cbbar);     // codebook lands in a B tile first
+    bulk_g2s(B_t(0), a.cb, 1024 * 8, &sh->cbbar);     // the codebook lands in a B stage first
   }
   if (warp == 0) {
     asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
-                 ::"r"(smem_u32(&sh->tmem_base)), "r"(PF_TMEM_COLS) : "memory");
+                 ::"r"(smem_u32(&sh->tmem_base)), "r"(P2_TMEM_COLS) : "memory");
     asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
   }
-  __syncthreads();                                    // barrier inits visible
-  mbar_wait(&sh->cbbar, 0);
-  {  // replicate: entry e of copy c at e*64 + c*8; consecutive 16-byte stores
+  __syncthreads();
+  if (!mbar_wait(&sh->cbbar, 0)) sh->abort = 1;
+  {  // replicate: entry e of copy c at e * 128 + c * 8; consecutive 16-byte stores
     const uint2* src = (const uint2*)B_t(0);
-    for (int idx = threadIdx.x; idx < 1024 * (PF_CB_COPIES / 2); idx += blockDim.x) {
-      const uint2 v = src[idx / (PF_CB_COPIES / 2)];
+    for (int idx = threadIdx.x; idx < 1024 * (P2_CB_COPIES / 2); idx += blockDim.x) {
+      const uint2 v = src[idx / (P2_CB_COPIES / 2)];
       *(uint4*)(cbs + idx * 16) = make_uint4(v.x, v.y, v.x, v.y);
     }
   }
   tc_fence_before();
-  __syncthreads();                                    // codebook ready, staging tile free again
+  __syncthreads();                                     // codebook ready, B stage 0 free again
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
+  volatile int* abort = &sh->abort;
 
   if (warp == 0) {
-    // ---------------- activation loader: A tiles of the pass's blocks by TMA (lane 0)
+    // ---------------- activation loader (lane 0): B stages of each item by TMA
     if (lane == 0) {
-      int gc = 0;
-      for (int pi = 0; pi < npass; ++pi) {
-        const PfPass P = pass_of(pi);
-        for (int c = 0; c < nchunks; ++c, ++gc) {
-          const int slot = gc % PF_STAGES;
-          if (gc >= PF_STAGES && !mbar_wait(&sh->empty[slot], ((gc / PF_STAGES) - 1) & 1)) { pi = npass; break; }
-          mbar_arrive_expect_tx(&sh->full_a[slot], P.mb * PF_TILE);
-          tma_load_2d(A_t(slot), &tm_act, c * 128, P.blk * PF_BM, &sh->full_a[slot]);
-          if (P.mb == 2) tma_load_2d(A_t(slot) + PF_TILE, &tm_act, c * 128, (P.blk + 1) * PF_BM, &sh->full_a[slot]);
+      int gb = 0;
+      for (int w = blockIdx.x; w < nwork && !*abort; w += gridDim.x) {
+        const int4 ch = a.chunks[w / a.T];
+        for (int c = 0; c < nstage; ++c, ++gb) {
+          const int slot = gb % P2_BSTAGES;
+          if (gb >= P2_BSTAGES && !mbar_wait(&sh->empty_b[slot], ((gb / P2_BSTAGES) - 1) & 1)) { *abort = 1; break; }
+          mbar_arrive_expect_tx(&sh->full_b[slot], P2_BTILE);
+          tma_load_2d(B_t(slot), &tm_act, c * 128, ch.y, &sh->full_b[slot]);
         }
       }
+      // every issued load has landed before the CTA can exit
+      for (int q = max(0, gb - P2_BSTAGES); q < gb; ++q) mbar_wait(&sh->full_b[q % P2_BSTAGES], (q / P2_BSTAGES) & 1);
     }
   } else if (warp == 1) {
-    // ---------------- index loader: lo plane by TMA, hi / scale planes by cp.async
-    constexpr int LOB = 128 / elem / 4;               // lo bytes per row per stage (32 fp8, 16 f16)
-    int gc = 0;
-    for (int pi = 0; pi < npass; ++pi) {
-      const PfPass P = pass_of(pi);
+    // ---------------- index loader: lo plane by TMA (two 128-row boxes), hi / scale planes by cp.async
+    int gi = 0;
+    for (int w = blockIdx.x; w < nwork && !*abort; w += gridDim.x) {
+      const int e = a.chunks[w / a.T].x, tile = w % a.T;
       const uint8_t* hi_r[8];
       const uint8_t* sc_r[8];
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
-        const long wr = pf_weight_row<GATEUP>(a, P.e, tile, lane + 32 * i);
+        const int R = lane + 32 * i;
+        const long wr = p2_weight_row<GATEUP>(a, e, tile, R >> 7, R & 127);
         hi_r[i] = a.hi + wr * (nsub / 4);
         sc_r[i] = (const uint8_t*)(a.sc + wr * ngk);
       }
-      const int row0 = (int)pf_weight_row<GATEUP>(a, P.e, tile, 0);
-      const int row1 = (int)pf_weight_row<GATEUP>(a, P.e, tile, PF_BN / 2);
-      for (int c = 0; c < nchunks; ++c, ++gc) {
-        const int slot = gc % PF_ISTAGES;
-        if (gc >= PF_ISTAGES && !mbar_wait(&sh->empty_i[slot], ((gc / PF_ISTAGES) - 1) & 1)) { pi = npass; break; }
+      const int row0 = (int)p2_weight_row<GATEUP>(a, e, tile, 0, 0);
+      const int row1 = (int)p2_weight_row<GATEUP>(a, e, tile, 1, 0);
+      for (int c = 0; c < nstage; ++c, ++gi) {
+        const int slot = gi % P2_ISTAGES;
+        if (gi >= P2_ISTAGES && !mbar_wait(&sh->empty_i[slot], ((gi / P2_ISTAGES) - 1) & 1)) { *abort = 1; break; }
         const uint32_t ibase = smem_u32(I_t(slot));
         if (lane == 0) {
-          mbar_arrive_expect_tx(&sh->full_i[slot], PF_BN * LOB);
+          mbar_arrive_expect_tx(&sh->full_i[slot], P2_NT * P2_ROWS * LOB);
           tma_load_2d(I_t(slot), &tm_lo, c * LOB, row0, &sh->full_i[slot]);
-          tma_load_2d(I_t(slot) + (PF_BN / 2) * LOB, &tm_lo, c * LOB, row1, &sh->full_i[slot]);
+          tma_load_2d(I_t(slot) + P2_ROWS * LOB, &tm_lo, c * LOB, row1, &sh->full_i[slot]);
         }
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          const int r = lane + 32 * i;
+          const int R = lane + 32 * i;
           if (PREC == VQ2_PREC_FP8) {          // hi: 8 bytes (32 sub-vectors); scales of 2 groups
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(ibase + PF_IDX_HI + r * 8), "l"(hi_r[i] + c * 8) : "memory");
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + PF_IDX_SC + r * 4), "l"(sc_r[i] + c * 4) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(ibase + P2_IDX_HI + R * 8), "l"(hi_r[i] + c * 8) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + P2_IDX_SC + R * 4), "l"(sc_r[i] + c * 4) : "memory");
           } else {                             // hi: 4 bytes (16 sub-vectors); the scale pair holding this group
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + PF_IDX_HI + r * 8), "l"(hi_r[i] + c * 4) : "memory");
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + PF_IDX_SC + r * 4), "l"(sc_r[i] + (c & ~1) * 2) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + P2_IDX_HI + R * 8), "l"(hi_r[i] + c * 4) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + P2_IDX_SC + R * 4), "l"(sc_r[i] + (c & ~1) * 2) : "memory");
           }
         }
-        // one more arrival per lane when its copies above have landed
         asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&sh->full_i[slot])) : "memory");
       }
     }
-    cp_async_wait<0>();                               // nothing in flight when the CTA retires
+    cp_async_wait<0>();
+    if (lane == 0)   // the lo-plane TMA loads of the last stages have landed
+      for (int q = max(0, gi - P2_ISTAGES); q < gi; ++q) mbar_wait(&sh->full_i[q % P2_ISTAGES], (q / P2_ISTAGES) & 1);
   } else if (warp == 2) {
-    // ---------------- MMA issuer
+    // ---------------- MMA issuer (lane 0)
     if (lane == 0) {
-      int gc = 0;
-      bool ok = true;
-      for (int pi = 0; pi < npass && ok; ++pi) {
-        const PfPass P = pass_of(pi);
-        for (int c = 0; c < nchunks; ++c, ++gc) {
-          const int slot = gc % PF_STAGES, bslot = gc % PF_BSTAGES;
-          if (!mbar_wait(&sh->full_a[slot], (gc / PF_STAGES) & 1)) { ok = false; break; }
-          if (!mbar_wait(&sh->full_b[bslot], (gc / PF_BSTAGES) & 1)) { ok = false; break; }
-          fence_async_smem();                             // cp.async-written data visible to the tensor core
+      int gb = 0, ga = 0, it = 0;
+      for (int w = blockIdx.x; w < nwork && !*abort; w += gridDim.x, ++it) {
+        const int ns = a.chunks[w / a.T].z;
+        const uint32_t idesc = (1u << 4) | ((uint32_t)(ns >> 3) << 17) | ((uint32_t)(P2_ROWS >> 4) << 24);
+        if (it > 0 && !mbar_wait(&sh->acc_empty, (it - 1) & 1)) { *abort = 1; break; }
+        tc_fence_after();
+        bool ok = true;
+        for (int c = 0; c < nstage; ++c, ++gb, ++ga) {
+          const int bslot = gb % P2_BSTAGES, aslot = ga % P2_ASTAGES;
+          if (!mbar_wait(&sh->full_b[bslot], (gb / P2_BSTAGES) & 1) ||
+              !mbar_wait(&sh->full_a[aslot], (ga / P2_ASTAGES) & 1)) { ok = false; break; }
           tc_fence_after();
-          const uint32_t abase = smem_u32(A_t(slot)), bbase = smem_u32(B_t(bslot));   // B: 256 rows
-          for (int b = 0; b < P.mb; ++b) {
-            const uint32_t td = tmem + (uint32_t)((P.acc + b) * PF_BN);
+          const uint32_t bbase = smem_u32(B_t(bslot));
+#pragma unroll
+          for (int t = 0; t < P2_NT; ++t)
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
-              umma<PREC>(td, umma_desc_sw128(abase + b * PF_TILE + ks * 32), umma_desc_sw128(bbase + ks * 32),
-                         (c | ks) != 0);
-          }
-          umma_commit(&sh->empty[slot]);
+              umma_tmem_a<PREC>(tmem + p2_acc_col(t), tmem + p2_a_col(aslot, t) + 8 * ks,
+                                umma_desc_sw128(bbase + ks * 32), idesc, (c | ks) != 0);
           umma_commit(&sh->empty_b[bslot]);
+          umma_commit(&sh->empty_a[aslot]);
         }
-        umma_commit(&sh->done[pi]);   // arrives once every MMA issued so far has completed
+        umma_commit(&sh->done);       // arrives once every MMA issued so far has completed
+        if (!ok) { *abort = 1; break; }
       }
-      for (int pi = 0; pi < npass; ++pi)
-        if (!ok) umma_commit(&sh->done[pi]);          // let the epilogue finish (results invalid)
+      umma_commit(&sh->drain);        // nothing of ours still reads TMEM or shared memory after this
+      mbar_wait(&sh->drain, 0);
     }
   } else {
-    // ---------------- weight decoders (512 threads: row r, half h of the 128-byte row)
-    // the two half-row threads of a row are adjacent lanes: index-plane reads are contiguous
-    const int dt = threadIdx.x - 96, r = dt >> 1, h = dt & 1;
-    const uint32_t cbl = smem_u32(cbs + (lane & (PF_CB_COPIES - 1)) * 8);   // shared-window address
-    int gc = 0;
-    bool ok = true;
-    for (int pi = 0; pi < npass; ++pi) {
-      const PfPass P = pass_of(pi);
-      for (int c = 0; c < nchunks && ok; ++c, ++gc) {
-        const int slot = gc % PF_ISTAGES, bslot = gc % PF_BSTAGES;
-        if (!mbar_wait(&sh->full_i[slot], (gc / PF_ISTAGES) & 1)) { ok = false; break; }
-        if (gc >= PF_BSTAGES && !mbar_wait(&sh->empty_b[bslot], ((gc / PF_BSTAGES) - 1) & 1)) { ok = false; break; }
-        const uint32_t ip = smem_u32(I_t(slot));
-        const uint32_t bt = smem_u32(B_t(bslot));
-        if (PREC == VQ2_PREC_FP8) {                   // 16 sub-vectors = one 64-group; lo rows 32 B apart
-          const uint4 lo = lds128_v(ip + r * 32 + h * 16);
-          const uint32_t hw = lds32_v(ip + PF_IDX_HI + r * 8 + h * 4);
-          const uint32_t sbits = lds16_v(ip + PF_IDX_SC + r * 4 + h * 2);
-          const float scf = __half2float(__ushort_as_half((unsigned short)sbits));
-          decode_b_quarter<PREC>(cbl, make_uint2(lo.x, lo.y), hw & 0xFFFFu, scf, bt, r, 2 * h);
-          decode_b_quarter<PREC>(cbl, make_uint2(lo.z, lo.w), hw >> 16, scf, bt, r, 2 * h + 1);
-        } else {                                      // 8 sub-vectors; lo rows 16 B apart
-          const uint2 lo = lds64_v(ip + r * 16 + h * 8);
-          const uint32_t hw = lds16_v(ip + PF_IDX_HI + r * 8 + h * 2);
-          const uint32_t sbits = lds16_v(ip + PF_IDX_SC + r * 4 + (c & 1) * 2);
-          const float scf = __half2float(__ushort_as_half((unsigned short)sbits));
-          decode_b_quarter<PREC>(cbl, make_uint2(lo.x, 0u), hw & 0xFFu, scf, bt, r, 2 * h);
-          decode_b_quarter<PREC>(cbl, make_uint2(lo.y, 0u), hw >> 8, scf, bt, r, 2 * h + 1);
+    // ---------------- decoders (16 warps): warp -> TMEM lane quarter q, row tile t, K half h
+    const int q = warp & 3, j = (warp - 3) >> 2, t = j >> 1, h = j & 1;
+    const int r = q * 32 + lane, R = t * P2_ROWS + r;
+    const uint32_t cbl = smem_u32(cbs) + (lane & (P2_CB_COPIES - 1)) * 8;
+    const uint32_t tlane = (uint32_t)(q * 32) << 16;
+    int gi = 0, ga = 0, it = 0;
+    for (int w = blockIdx.x; w < nwork; w += gridDim.x, ++it) {
+      const int4 ch = a.chunks[w / a.T];
+      const int tile = w % a.T;
+      bool ok = !*abort;
+      for (int c = 0; c < nstage && ok; ++c, ++gi, ++ga) {
+        const int islot = gi % P2_ISTAGES, aslot = ga % P2_ASTAGES;
+        if (!mbar_wait(&sh->full_i[islot], (gi / P2_ISTAGES) & 1)) { ok = false; break; }
+        if (ga >= P2_ASTAGES && !mbar_wait(&sh->empty_a[aslot], ((ga / P2_ASTAGES) - 1) & 1)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t ip = smem_u32(I_t(islot));
+        uint32_t v[16];
+        if (PREC == VQ2_PREC_FP8) {             // one 64-group: 16 sub-vectors
+          const uint4 lo = lds128_v(ip + R * 32 + h * 16);
+          const uint32_t hw = lds32_v(ip + P2_IDX_HI + R * 8 + h * 4);
+          const uint32_t sbits = lds16_v(ip + P2_IDX_SC + R * 4 + h * 2);
+          decode16_fp8(cbl, lo, hw, __half2float(__ushort_as_half((unsigned short)sbits)), v);
+        } else {                                // half of a 64-group: 8 sub-vectors
+          const uint2 lo = lds64_v(ip + R * 16 + h * 8);
+          const uint32_t hw = lds16_v(ip + P2_IDX_HI + R * 8 + h * 2);
+          const uint32_t sbits = lds16_v(ip + P2_IDX_SC + R * 4 + (c & 1) * 2);
+          decode8_f16(cbl, lo, hw, __half2float(__ushort_as_half((unsigned short)sbits)), v);
         }
-        fence_async_smem();
+        tmem_st16(tmem + tlane + p2_a_col(aslot, t) + 16 * h, v);
+        tmem_st_wait();
+        tc_fence_before();
         __syncwarp();
         if (lane == 0) {
-          mbar_arrive(&sh->full_b[bslot]);
-          mbar_arrive(&sh->empty_i[slot]);
+          mbar_arrive(&sh->full_a[aslot]);
+          mbar_arrive(&sh->empty_i[islot]);
         }
       }
-      // ---------------- epilogue of the pass out of TMEM
-      const int q = warp & 3, cq = (warp - 3) >> 2;        // TMEM lane quarter, column quarter
-      if (!mbar_wait(&sh->done[pi], 0)) continue;
+      if (!ok) *abort = 1;
+      if (*abort) break;
+      // ---------------- epilogue of the item out of TMEM (lane = weight row, column = slot)
+      if (!mbar_wait(&sh->done, it & 1)) { *abort = 1; break; }
       tc_fence_after();
-      for (int b = 0; b < P.mb; ++b) {
-        const int slot_i = q * 32 + lane;
-        const size_t p = (size_t)(P.blk + b) * PF_BM + slot_i;
-        const int tok = a.val[p] ? a.st[p] : -1;
-        const uint32_t trow = tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)((P.acc + b) * PF_BN);
-        if (GATEUP) {                                  // 32 gate + the 32 matching up columns
+      const int ncol = ch.z >> 5;                          // 32-slot column groups
+      if (GATEUP) {
+        for (int cg = j; cg < ncol; cg += 4) {
           float g[32], u[32];
-          tmem_ld32(trow + cq * 32, g);
-          tmem_ld32(trow + PF_BN / 2 + cq * 32, u);
-          const float inv = tok >= 0 ? a.inv_act[tok] : 0.f;
-          float* dst = a.inter + p * a.I + tile * (PF_BN / 2) + cq * 32;
+          tmem_ld32(tmem + tlane + p2_acc_col(0) + cg * 32, g);
+          tmem_ld32(tmem + tlane + p2_acc_col(1) + cg * 32, u);
+          const int s0 = ch.y + cg * 32;
+          const float myinv = a.inv_slot[s0 + lane];
+          float* dst = a.inter + (size_t)s0 * a.I + tile * P2_ROWS + r;
 #pragma unroll
-          for (int j = 0; j < 32; j += 4) {
-            float rr[4];
-#pragma unroll
-            for (int t = 0; t < 4; ++t) {
-              const float gg = g[j + t] * inv, uu = u[j + t] * inv;
-              rr[t] = gg / (1.f + __expf(-gg)) * uu;
-            }
-            *(float4*)(dst + j) = make_float4(rr[0], rr[1], rr[2], rr[3]);
+          for (int k = 0; k < 32; ++k) {
+            const float inv = __shfl_sync(0xffffffffu, myinv, k);
+            const float gg = g[k] * inv, uu = u[k] * inv;
+            dst[(size_t)k * a.I] = gg / (1.f + __expf(-gg)) * uu;
           }
-        } else {                                       // 64 output columns
-          const float w = tok >= 0 ? a.topk_w[(size_t)tok * a.topk + a.ss[p]] * a.inv_act[p] : 0.f;
-          float* dst = a.out + (size_t)(tok >= 0 ? tok : 0) * a.H + tile * PF_BN + cq * 64;
+        }
+      } else {
+        for (int u = j; u < P2_NT * ncol; u += 4) {
+          const int tt = u & 1, cg = u >> 1;
+          float v[32];
+          tmem_ld32(tmem + tlane + p2_acc_col(tt) + cg * 32, v);
+          const int s = ch.y + cg * 32 + lane;
+          const int mytok = a.val[s] ? a.st[s] : -1;
+          const float myw = mytok >= 0 ? a.topk_w[(size_t)mytok * a.topk + a.ss[s]] * a.inv_slot[s] : 0.f;
+          float* col = a.out + tile * (P2_NT * P2_ROWS) + tt * P2_ROWS + r;
 #pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            float v[32];
-            tmem_ld32(trow + cq * 64 + hh * 32, v);     // collective: every lane loads
-            if (tok >= 0) {
-#pragma unroll
-              for (int j = 0; j < 32; j += 4)
-                atomicAdd((float4*)(dst + hh * 32 + j), make_float4(v[j] * w, v[j + 1] * w, v[j + 2] * w, v[j + 3] * w));
-            }
+          for (int k = 0; k < 32; ++k) {
+            const int tok = __shfl_sync(0xffffffffu, mytok, k);
+            const float wk = __shfl_sync(0xffffffffu, myw, k);
+            if (tok >= 0) atomicAdd(col + (size_t)tok * a.H, v[k] * wk);
           }
         }
       }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->acc_empty);
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(PF_TMEM_COLS) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P2_TMEM_COLS) : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ work list
+// One CTA: the chunks of every expert's slot range (moe_align output with P2_BM-slot blocks;
+// each used block starts with a valid slot, the trailing unused blocks do not), at most
+// P2_CHUNK_BLOCKS blocks each, ordered by size, largest first.
+__global__ void __launch_bounds__(1024) build_chunks_kernel(const uint8_t* __restrict__ val, const int32_t* __restrict__ be,
+                                                            int nblk, int4* __restrict__ chunks, int* __restrict__ nchunks) {
+  __shared__ int cnt[P2_CHUNK_BLOCKS + 1], base[P2_CHUNK_BLOCKS + 1];
+  if (threadIdx.x <= P2_CHUNK_BLOCKS) cnt[threadIdx.x] = 0;
+  __syncthreads();
+  for (int pass = 0; pass < 2; ++pass) {
+    for (int b0 = threadIdx.x; b0 < nblk; b0 += blockDim.x) {
+      if (!val[(size_t)b0 * P2_BM]) continue;
+      const int e = be[b0];
+      if (b0 > 0 && be[b0 - 1] == e) continue;           // not the first block of its expert
+      int nb = 1;
+      while (b0 + nb < nblk && be[b0 + nb] == e && val[(size_t)(b0 + nb) * P2_BM]) ++nb;
+      for (int k = 0; k < nb; k += P2_CHUNK_BLOCKS) {
+        const int size = min(P2_CHUNK_BLOCKS, nb - k);
+        if (pass == 0) {
+          atomicAdd(&cnt[size], 1);
+        } else {
+          const int pos = base[size] + atomicAdd(&cnt[size], 1);
+          chunks[pos] = make_int4(e, (b0 + k) * P2_BM, size * P2_BM, 0);
+        }
+      }
+    }
+    __syncthreads();
+    if (pass == 0 && threadIdx.x == 0) {
+      int run = 0;
+      for (int size = P2_CHUNK_BLOCKS; size >= 1; --size) { base[size] = run; run += cnt[size]; cnt[size] = 0; }
+      *nchunks = run;
+    }
+    __syncthreads();
   }
 }
 
@@ -549,17 +565,20 @@ __global__ void __launch_bounds__(256) had_quant_rows_kernel(const void* __restr
   }
 }
 
-// Quantised token rows into slot order (padding slots zero), so the gate/up A tile of a block is
-// one contiguous 2-D TMA box.
+// Quantised token rows into slot order (padding slots zero) with their inverse scales, so the
+// activation rows of a chunk are one contiguous 2-D TMA box.
 __global__ void __launch_bounds__(256) gather_slot_rows_kernel(const uint8_t* __restrict__ src,
+                                                              const float* __restrict__ inv_tok,
                                                               const int32_t* __restrict__ st,
                                                               const uint8_t* __restrict__ val, int row_bytes,
-                                                              uint8_t* __restrict__ dst) {
+                                                              uint8_t* __restrict__ dst, float* __restrict__ inv_slot) {
   const long p = blockIdx.x;
   uint4* d = (uint4*)(dst + p * (size_t)row_bytes);
   const bool ok = val[p] != 0;
-  const uint4* s = (const uint4*)(src + (size_t)(ok ? st[p] : 0) * row_bytes);
+  const int tok = ok ? st[p] : 0;
+  const uint4* s = (const uint4*)(src + (size_t)tok * row_bytes);
   for (int i = threadIdx.x; i < row_bytes / 16; i += blockDim.x) d[i] = ok ? s[i] : make_uint4(0, 0, 0, 0);
+  if (threadIdx.x == 0) inv_slot[p] = ok ? inv_tok[tok] : 0.f;
 }
 
 // ------------------------------------------------------------------ host
@@ -587,8 +606,9 @@ static int encode_2d(CUtensorMap* m, const void* base, uint64_t inner_bytes, uin
 }
 
 struct PfLayout {
-  long M, Pmax, nblk, nchunks;
-  size_t off_st, off_ss, off_val, off_be, off_counts, off_xq, off_invx, off_xs, off_inter, off_vb, off_invvb, total;
+  long M, Pmax, nblk, nchunks_align;
+  size_t off_st, off_ss, off_val, off_be, off_counts, off_xq, off_invx, off_xs, off_invxs, off_inter, off_vb,
+      off_invvb, off_chunks, off_nchunks, total;
 };
 
 static size_t up256(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -597,21 +617,24 @@ static PfLayout pf_layout(int N, int k, int E, int H, int I, int prec) {
   PfLayout L;
   const size_t elem = prec == VQ2_PREC_FP8 ? 1 : 2;
   L.M = (long)N * k;
-  L.Pmax = L.M + (long)std::min<long>(L.M, E) * PF_BM;
-  L.nblk = L.Pmax / PF_BM;
-  L.nchunks = std::max<long>(1, (L.M + 8191) / 8192);
+  L.Pmax = L.M + (long)std::min<long>(L.M, E) * P2_BM;
+  L.nblk = L.Pmax / P2_BM;
+  L.nchunks_align = std::max<long>(1, (L.M + 8191) / 8192);
   size_t o = 0;
   L.off_st = o; o = up256(o + L.Pmax * 4);
   L.off_ss = o; o = up256(o + L.Pmax * 4);
   L.off_val = o; o = up256(o + L.Pmax);
   L.off_be = o; o = up256(o + L.nblk * 4);
-  L.off_counts = o; o = up256(o + L.nchunks * E * 4);
+  L.off_counts = o; o = up256(o + L.nchunks_align * E * 4);
   L.off_xq = o; o = up256(o + (size_t)N * H * elem);
   L.off_invx = o; o = up256(o + (size_t)N * 4);
   L.off_xs = o; o = up256(o + (size_t)L.Pmax * H * elem);
+  L.off_invxs = o; o = up256(o + (size_t)L.Pmax * 4);
   L.off_inter = o; o = up256(o + (size_t)L.Pmax * I * 4);
   L.off_vb = o; o = up256(o + (size_t)L.Pmax * I * elem);
   L.off_invvb = o; o = up256(o + (size_t)L.Pmax * 4);
+  L.off_chunks = o; o = up256(o + (size_t)L.nblk * 16);
+  L.off_nchunks = o; o = up256(o + 4);
   L.total = o + 256;
   return L;
 }
@@ -621,7 +644,6 @@ static bool g_pf_attr[64];
 }  // namespace vq2
 
 using namespace vq2;
-
 
 extern "C" size_t vq2_prefill_workspace_size(int N, int topk, int E, int H, int I, int precision) {
   if (N <= 0 || topk <= 0 || E <= 0) return 0;
@@ -641,7 +663,7 @@ extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_
   for (const void* p : ptrs)
     if (((uintptr_t)p & 15) != 0) return VQ2_ERR_ALIGN;
   const PfLayout L = pf_layout(a->N, a->topk, a->E, a->H, a->I, prec);
-  if (L.nblk > 65535) return VQ2_ERR_SHAPE;
+  if (L.Pmax > (1L << 30)) return VQ2_ERR_SHAPE;
   if (!ws || ws_bytes < L.total) return VQ2_ERR_WORKSPACE;
   uint8_t* w = (uint8_t*)(((uintptr_t)ws + 255) & ~(uintptr_t)255);
   int32_t* st = (int32_t*)(w + L.off_st);
@@ -652,61 +674,64 @@ extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_
   uint8_t* xq = w + L.off_xq;
   uint8_t* xs = w + L.off_xs;
   float* invx = (float*)(w + L.off_invx);
+  float* invxs = (float*)(w + L.off_invxs);
   float* inter = (float*)(w + L.off_inter);
   uint8_t* vb = w + L.off_vb;
   float* invvb = (float*)(w + L.off_invvb);
+  int4* chunks = (int4*)(w + L.off_chunks);
+  int* nchunks = (int*)(w + L.off_nchunks);
   cudaStream_t st_ = (cudaStream_t)stream;
 
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VQ2_ERR_NO_DEVICE;
   if (!g_pf_attr[dev]) {
     bool ok = true;
-    ok &= cudaFuncSetAttribute(prefill_gemm_kernel<VQ2_PREC_FP8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM) == cudaSuccess;
-    ok &= cudaFuncSetAttribute(prefill_gemm_kernel<VQ2_PREC_FP8, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM) == cudaSuccess;
-    ok &= cudaFuncSetAttribute(prefill_gemm_kernel<VQ2_PREC_F16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM) == cudaSuccess;
-    ok &= cudaFuncSetAttribute(prefill_gemm_kernel<VQ2_PREC_F16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)PF_SMEM) == cudaSuccess;
+    ok &= cudaFuncSetAttribute(prefill_gemm_kernel<VQ2_PREC_FP8, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P2_SMEM) == cudaSuccess;
+    ok &= cudaFuncSetAttribute(prefill_gemm_kernel<VQ2_PREC_FP8, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P2_SMEM) == cudaSuccess;
+    ok &= cudaFuncSetAttribute(prefill_gemm_kernel<VQ2_PREC_F16, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P2_SMEM) == cudaSuccess;
+    ok &= cudaFuncSetAttribute(prefill_gemm_kernel<VQ2_PREC_F16, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)P2_SMEM) == cudaSuccess;
     if (!ok) return VQ2_ERR_CUDA;
     g_pf_attr[dev] = true;
   }
-  int rc = launch_align_ex(a->topk_ids, a->ids_dtype, a->N, a->topk, a->E, PF_BM, a->expert_base, 1, st, ss, val,
+  const int nsm = device_sm_count();
+  if (nsm <= 0) return VQ2_ERR_CUDA;
+  int rc = launch_align_ex(a->topk_ids, a->ids_dtype, a->N, a->topk, a->E, P2_BM, a->expert_base, 1, st, ss, val,
                            be, counts, st_);
   if (rc) return rc;
   if (cudaMemsetAsync(a->out, 0, (size_t)a->N * a->H * sizeof(float), st_) != cudaSuccess) return VQ2_ERR_CUDA;
+  build_chunks_kernel<<<1, 1024, 0, st_>>>(val, be, (int)L.nblk, chunks, nchunks);
 
-  PfGemmArgs g = {};
-  g.act = nullptr;
-  g.st = st; g.ss = ss; g.val = val; g.be = be; g.topk_w = a->topk_w; g.inter = inter; g.out = a->out;
+  P2Args g = {};
+  g.chunks = chunks; g.nchunks = nchunks;
+  g.st = st; g.ss = ss; g.val = val; g.topk_w = a->topk_w; g.inter = inter; g.out = a->out;
   g.I = a->I; g.H = a->H; g.topk = a->topk;
-  if (prec == VQ2_PREC_FP8) {
+  if (prec == VQ2_PREC_FP8)
     had_quant_rows_kernel<VQ2_PREC_FP8><<<a->N, 256, 0, st_>>>(a->x, a->x_dtype, nullptr, a->H, xq, invx);
-  } else {
+  else
     had_quant_rows_kernel<VQ2_PREC_F16><<<a->N, 256, 0, st_>>>(a->x, a->x_dtype, nullptr, a->H, xq, invx);
-  }
   const int elem = prec == VQ2_PREC_FP8 ? 1 : 2;
   const int lob = 128 / elem / 4;
-  gather_slot_rows_kernel<<<(unsigned)L.Pmax, 256, 0, st_>>>(xq, st, val, a->H * elem, xs);
+  gather_slot_rows_kernel<<<(unsigned)L.Pmax, 256, 0, st_>>>(xq, invx, st, val, a->H * elem, xs, invxs);
   CUtensorMap tm_x, tm_v, tm_l13, tm_l2;
-  if (encode_2d(&tm_x, xs, (uint64_t)a->H * elem, L.Pmax, 128, 128, true) ||
-      encode_2d(&tm_v, vb, (uint64_t)a->I * elem, L.Pmax, 128, 128, true) ||
-      encode_2d(&tm_l13, a->w13_lo, a->H / 4, (uint64_t)a->E * 2 * a->I, lob, PF_BN / 2, false) ||
-      encode_2d(&tm_l2, a->w2_lo, a->I / 4, (uint64_t)a->E * a->H, lob, PF_BN / 2, false))
+  if (encode_2d(&tm_x, xs, (uint64_t)a->H * elem, L.Pmax, 128, P2_NMAX, true) ||
+      encode_2d(&tm_v, vb, (uint64_t)a->I * elem, L.Pmax, 128, P2_NMAX, true) ||
+      encode_2d(&tm_l13, a->w13_lo, a->H / 4, (uint64_t)a->E * 2 * a->I, lob, P2_ROWS, false) ||
+      encode_2d(&tm_l2, a->w2_lo, a->I / 4, (uint64_t)a->E * a->H, lob, P2_ROWS, false))
     return VQ2_ERR_CUDA;
-  // gate/up
-  g.inv_act = invx; g.lo = a->w13_lo; g.hi = a->w13_hi; g.sc = a->w13_sc; g.cb = a->w13_cb;
-  g.K = a->H; g.R = 2 * a->I;
-  dim3 g1(a->I / (PF_BN / 2), (unsigned)((L.nblk + PF_MB - 1) / PF_MB));
-  if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, true><<<g1, PF_THREADS, PF_SMEM, st_>>>(g, tm_x, tm_l13, (int)L.nblk);
-  else prefill_gemm_kernel<VQ2_PREC_F16, true><<<g1, PF_THREADS, PF_SMEM, st_>>>(g, tm_x, tm_l13, (int)L.nblk);
+  // gate/up: row tiles of 128 gate + 128 up rows
+  g.inv_slot = invxs; g.lo = a->w13_lo; g.hi = a->w13_hi; g.sc = a->w13_sc; g.cb = a->w13_cb;
+  g.K = a->H; g.R = 2 * a->I; g.T = a->I / P2_ROWS;
+  if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, true><<<nsm, P2_THREADS, P2_SMEM, st_>>>(g, tm_x, tm_l13);
+  else prefill_gemm_kernel<VQ2_PREC_F16, true><<<nsm, P2_THREADS, P2_SMEM, st_>>>(g, tm_x, tm_l13);
   // inter -> Hadamard -> quantised activation of the down projection
   if (prec == VQ2_PREC_FP8)
     had_quant_rows_kernel<VQ2_PREC_FP8><<<(unsigned)L.Pmax, 256, 0, st_>>>(inter, VQ2_DT_F32, val, a->I, vb, invvb);
   else
     had_quant_rows_kernel<VQ2_PREC_F16><<<(unsigned)L.Pmax, 256, 0, st_>>>(inter, VQ2_DT_F32, val, a->I, vb, invvb);
-  // down + combine
-  g.inv_act = invvb; g.lo = a->w2_lo; g.hi = a->w2_hi; g.sc = a->w2_sc; g.cb = a->w2_cb;
-  g.K = a->I; g.R = a->H;
-  dim3 g2(a->H / PF_BN, (unsigned)((L.nblk + PF_MB - 1) / PF_MB));
-  if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, false><<<g2, PF_THREADS, PF_SMEM, st_>>>(g, tm_v, tm_l2, (int)L.nblk);
-  else prefill_gemm_kernel<VQ2_PREC_F16, false><<<g2, PF_THREADS, PF_SMEM, st_>>>(g, tm_v, tm_l2, (int)L.nblk);
+  // down + combine: row tiles of 256 output rows
+  g.inv_slot = invvb; g.lo = a->w2_lo; g.hi = a->w2_hi; g.sc = a->w2_sc; g.cb = a->w2_cb;
+  g.K = a->I; g.R = a->H; g.T = a->H / (P2_NT * P2_ROWS);
+  if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, false><<<nsm, P2_THREADS, P2_SMEM, st_>>>(g, tm_v, tm_l2);
+  else prefill_gemm_kernel<VQ2_PREC_F16, false><<<nsm, P2_THREADS, P2_SMEM, st_>>>(g, tm_v, tm_l2);
   return cudaGetLastError() == cudaSuccess ? VQ2_OK : VQ2_ERR_CUDA;
 }

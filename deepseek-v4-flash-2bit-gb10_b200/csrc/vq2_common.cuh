@@ -173,6 +173,24 @@ inline int device_sm_count() {
   return counts[dev];
 }
 
+// Like unpack_ids4, but the ids come out multiplied by 64 (a byte offset into a table of 64-byte
+// entries): o02 = 64*id0 | 64*id2 << 16, o13 = 64*id1 | 64*id3 << 16 (64 * 1023 fits 16 bits).
+__device__ __forceinline__ void unpack_off4_x64(uint32_t lo_word, uint32_t hb, uint32_t& o02, uint32_t& o13) {
+  o02 = (__byte_perm(lo_word, 0u, 0x4240) << 6) | ((hb * 0x04004000u) & 0xC000C000u);   // hb bits 0-1 -> 14-15, 4-5 -> 30-31
+  o13 = (__byte_perm(lo_word, 0u, 0x4341) << 6) | ((hb * 0x01001000u) & 0xC000C000u);   // hb bits 2-3 -> 14-15, 6-7 -> 30-31
+}
+
+// Packed fp32 multiply of two pairs (Blackwell mul.rn.f32x2: each half rounded on its own).
+__device__ __forceinline__ float2 fmul2(float2 a, float2 b) {
+  unsigned long long d, x, y;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(x) : "f"(a.x), "f"(a.y));
+  asm("mov.b64 %0, {%1, %2};" : "=l"(y) : "f"(b.x), "f"(b.y));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(x), "l"(y));
+  float2 r;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(d));
+  return r;
+}
+
 __device__ __forceinline__ int load_id(const void* ids, int ids_dtype, int m) {
   return ids_dtype == VQ2_ID_I64 ? (int)((const long long*)ids)[m] : ((const int*)ids)[m];
 }

@@ -34,6 +34,10 @@ class Vq2MoeArgs(ctypes.Structure):
 _SIGS = {
     "vq2_decode_workspace_size": (ctypes.c_size_t, [ctypes.c_int] * 4),
     "vq2_decode": (ctypes.c_int, [ctypes.POINTER(Vq2MoeArgs), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
+    "vq2_decode_host_stage_size": (ctypes.c_size_t, [ctypes.c_int] * 5),
+    "vq2_decode_host": (ctypes.c_int, [ctypes.POINTER(Vq2MoeArgs), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                       ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
+                                       ctypes.c_size_t, ctypes.c_void_p]),
     "vq2_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(Vq2MoeArgs), ctypes.c_void_p]),
     "vq2_prefill_workspace_size": (ctypes.c_size_t, [ctypes.c_int] * 6),
     "vq2_prefill": (ctypes.c_int, [ctypes.POINTER(Vq2MoeArgs), ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,

@@ -111,6 +111,57 @@ def vq2_moe_fused_10b(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, 
     return out
 
 
+_HOST = {}
+
+
+def vq2_moe_fused_10b_host(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, out=None, group=64,
+                           expert_base=0):
+    """Decode step with HOST inputs and result (extension; the reference's callers hold device
+    tensors): ``x`` [N, H] bf16/fp16/fp32, ``topk_ids`` [N, k] int32/int64 and ``topk_w`` [N, k] fp32
+    are CPU tensors (page-locked for asynchronous copies), the weights are the layer's CUDA tensors.
+    One library call queues the input copies, the decode kernels and the copy of the fp32 result
+    into ``out`` (a CPU [N, H] fp32 tensor, allocated page-locked when not given) on the current
+    stream of the weights' device; ``out`` is valid once that stream is synchronised. The weights
+    are validated on their first use."""
+    if group != 64:
+        raise ValueError("vq2: only group=64 is supported")
+    dev = lgu.device
+    N, H = x.shape
+    k = topk_ids.shape[1]
+    if x.is_cuda or topk_ids.is_cuda or topk_w.is_cuda:
+        raise ValueError("vq2_moe_fused_10b_host: x, topk_ids and topk_w must be host tensors")
+    if (x.dtype not in _lib.DT or topk_ids.dtype not in _lib.ID or topk_w.dtype is not _F32 or not x.is_contiguous()
+            or not topk_ids.is_contiguous() or not topk_w.is_contiguous()):
+        raise ValueError("vq2_moe_fused_10b_host: contiguous x (bf16/fp16/fp32), ids (int32/int64), w (fp32) expected")
+    if N * k > _lib.DECODE_MAX_PAIRS:
+        raise ValueError(f"vq2_moe_fused_10b_host: N*k = {N * k} above the decode limit {_lib.DECODE_MAX_PAIRS}")
+    if out is None:
+        out = torch.empty(N, H, dtype=_F32, pin_memory=True)
+    stream = torch.cuda.current_stream(dev).cuda_stream
+    wkey = (lgu.data_ptr(), ld.data_ptr(), id(dev))
+    if wkey not in _HOST:
+        ws = [Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn]
+        want = (_F16, _U8, _U8, _F16, _F16, _U8, _U8, _F16)
+        for t, d in zip(ws, want):
+            if not _ok(t, d):
+                raise ValueError("vq2_moe_fused_10b_host: weights must be contiguous fp16 codebooks/scales and u8 planes")
+        _lib.require_cuda(*ws, device=lgu.get_device())
+        if len(_HOST) > 1024:
+            _HOST.clear()
+        _HOST[wkey] = True
+    L = _lib.lib()
+    a = _lib.moe_args(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, out, expert_base=expert_base)
+    nst = L.vq2_decode_host_stage_size(N, k, H, a.x_dtype, a.ids_dtype)
+    nws = L.vq2_decode_workspace_size(N, k, H, a.I)
+    buf = _lib.workspace(nst + nws + 256, dev, stream)
+    base = buf.data_ptr()
+    rc = L.vq2_decode_host(a, x.data_ptr(), topk_ids.data_ptr(), topk_w.data_ptr(), out.data_ptr(), base, nst,
+                           base + nst, buf.numel() - nst, stream)
+    if rc:
+        _lib.check(rc, "vq2_moe_fused_10b_host")
+    return out
+
+
 # The packer lives beside the decode entry in the reference module (vq2_kernel.py:37-72, :160-167,
 # :501-505); its implementation here is kernels/vq2_pack.py.
 from .vq2_pack import pack_vq2, pack_vq2_experts, pack_vq2_experts_10b  # noqa: E402,F401

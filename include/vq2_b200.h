@@ -69,6 +69,18 @@ typedef struct vq2_moe_args {
 size_t vq2_decode_workspace_size(int N, int topk, int H, int I);
 int vq2_decode(const vq2_moe_args* a, void* workspace, size_t ws_bytes, void* stream);
 
+/* Decode step from host buffers (no counterpart in the reference, whose callers hold device
+ * tensors): for callers whose token rows, routing and result live in host memory. Queues on
+ * `stream` the copies of h_x [N,H] (x_dtype), h_ids [N,topk] (ids_dtype) and h_w [N,topk] f32 into
+ * the caller's device `stage`, the two decode kernels and the copy of out [N,H] f32 into h_out;
+ * returns without waiting (synchronise the stream before reading h_out). Host buffers should be
+ * page-locked for the copies to run asynchronously. In `a` only the dimensions, dtypes, E,
+ * expert_base and the weight pointers are read; x, topk_ids, topk_w and out are taken from the
+ * stage. workspace as for vq2_decode. */
+size_t vq2_decode_host_stage_size(int N, int topk, int H, int x_dtype, int ids_dtype);
+int vq2_decode_host(const vq2_moe_args* a, const void* h_x, const void* h_ids, const float* h_w, float* h_out,
+                    void* stage, size_t stage_bytes, void* workspace, size_t ws_bytes, void* stream);
+
 /* Allocation-free decode: no counterpart in the reference. For callers that cannot allocate
  * device memory when they call (a memory pool that forbids new allocations, a driver callback, a
  * host runtime without a CUDA allocator): same result as vq2_decode, but the gate/up scratch is a

@@ -154,3 +154,22 @@ def test_wide_dynamic_range(N, outlier):
     theirs = torch_ref.rel_l2(torch_ref.moe_decode_bf16_ref(x, ids, tw, L), ref)
     assert ours < TOL, f"rel-L2 {ours:.3e} against fp32"
     assert ours <= theirs * 1.05 + 1e-5, f"ours {ours:.3e} vs the reference algorithm's {theirs:.3e}"
+
+
+@pytest.mark.parametrize("N,ids64", [(1, False), (3, True)])
+def test_host_buffer_entry_matches_device_entry(big_layer, N, ids64):
+    """vq2_decode_host (inputs and result in page-locked host memory, one library call per step)
+    gives the device entry's result; two steps in a row reuse the same device staging."""
+    from vq2_vllm import synth
+    from vq2_vllm.kernels.vq2_kernel import vq2_moe_fused_10b_host
+    for step in range(2):
+        x = synth.make_tokens(N, 4096, seed=80 + step, device="cuda")
+        ids, tw = synth.route_softmax_topk(x, 256, 8, w_std=0.02, seed=90 + step)
+        if ids64:
+            ids = ids.long()
+        want = _moe()(x, ids, tw, *synth.layer_args(big_layer))
+        xh, ih, wh = x.cpu().pin_memory(), ids.cpu().pin_memory(), tw.cpu().pin_memory()
+        got = vq2_moe_fused_10b_host(xh, ih, wh, *synth.layer_args(big_layer))
+        torch.cuda.synchronize()
+        assert not got.is_cuda and got.dtype == torch.float32
+        assert torch_ref.rel_l2(got, want.cpu()) < 1e-5
