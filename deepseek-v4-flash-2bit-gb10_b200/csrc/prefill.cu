@@ -80,6 +80,16 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
   for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+__device__ __forceinline__ void tmem_ld8(uint32_t taddr, float* v) {
+  uint32_t r[8];
+  asm volatile("tcgen05.ld.sync.aligned.32x32b.x8.b32 {%0,%1,%2,%3,%4,%5,%6,%7}, [%8];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7])
+               : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+#pragma unroll
+  for (int i = 0; i < 8; ++i) v[i] = __uint_as_float(r[i]);
+}
+
 __device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
   asm volatile("cp.async.bulk.tensor.2d.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
                ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar)) : "memory");
@@ -93,34 +103,21 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
 
 // ------------------------------------------------------------------ weight decode into registers
-// fp8: the 16 sub-vectors of one 64-group of a weight row (lo: their 16 low index bytes, hw: their
-// 4 hi bytes, scf: the group scale) -> 16 words of 4 e4m3 values, e4m3(sat(C[id] * sc)) with the
-// product exact in fp32 and one rounding (reference vq2_grouped.cu:434-446).
-// cbl: this lane's codebook copy (entries 128 bytes apart: 16 copies, lane l reads copy l mod 16,
-// so a warp's 8-byte gathers are conflict-free).
-__device__ __forceinline__ void decode16_fp8(uint32_t cbl, uint4 lo, uint32_t hw, float scf, uint32_t* v) {
-  const float2 s2 = make_float2(scf, scf);
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    uint32_t ids[2];
-    unpack_ids4(q == 0 ? lo.x : q == 1 ? lo.y : q == 2 ? lo.z : lo.w, (hw >> (8 * q)) & 0xFFu, ids[0], ids[1]);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const uint32_t id = (j & 2) ? (ids[j & 1] >> 16) : (ids[j & 1] & 0xFFFFu);
-      const uint2 c = lds64(cbl + (id << 7));
-      const float2 x0 = fmul2(__half22float2(*(const __half2*)&c.x), s2);
-      const float2 x1 = fmul2(__half22float2(*(const __half2*)&c.y), s2);
-      const __nv_fp8x2_storage_t p0 = __nv_cvt_float2_to_fp8x2(x0, __NV_SATFINITE, __NV_E4M3);
-      const __nv_fp8x2_storage_t p1 = __nv_cvt_float2_to_fp8x2(x1, __NV_SATFINITE, __NV_E4M3);
-      v[4 * q + j] = (uint32_t)p0 | ((uint32_t)p1 << 16);
-    }
-  }
+// Exact fp32 products of two f16 values (sm_100 mixed-precision FMA; the product of two 11-bit
+// significands fits fp32, and the -0 addend keeps the sign of a zero product): (h2.lo * s, h2.hi * s).
+__device__ __forceinline__ float2 f16x2_times_f16(uint32_t h2, unsigned short s) {
+  float2 r;
+  asm("{\n .reg .b16 a, b;\n mov.b32 {a, b}, %2;\n fma.rn.f32.f16 %0, a, %3, %4;\n fma.rn.f32.f16 %1, b, %3, %4;\n}"
+      : "=f"(r.x), "=f"(r.y) : "r"(h2), "h"(s), "f"(-0.0f));
+  return r;
 }
 
-// f16: 8 sub-vectors of a row (lo: 8 low index bytes, hw: 2 hi bytes) -> 16 words of 2 f16 values,
-// C[id] * sc in fp16.
-__device__ __forceinline__ void decode8_f16(uint32_t cbl, uint2 lo, uint32_t hw, float scf, uint32_t* v) {
-  const __half2 s2 = __float2half2_rn(scf);
+// fp8: 8 sub-vectors of a weight row (lo: their 8 low index bytes, hw: their 2 hi bytes in the
+// low 16 bits, sb: the f16 bits of the group scale) -> 8 words of 4 e4m3 values,
+// e4m3(sat(C[id] * sc)) with the product exact in fp32 and one rounding (reference
+// vq2_grouped.cu:434-446). cbl: this lane's codebook copy (entries 128 bytes apart: 16 copies,
+// lane l reads copy l mod 16, so a warp's 8-byte gathers are conflict-free).
+__device__ __forceinline__ void decode8_fp8(uint32_t cbl, uint2 lo, uint32_t hw, unsigned short sb, uint32_t* v) {
 #pragma unroll
   for (int q = 0; q < 2; ++q) {
     uint32_t ids[2];
@@ -129,19 +126,55 @@ __device__ __forceinline__ void decode8_f16(uint32_t cbl, uint2 lo, uint32_t hw,
     for (int j = 0; j < 4; ++j) {
       const uint32_t id = (j & 2) ? (ids[j & 1] >> 16) : (ids[j & 1] & 0xFFFFu);
       const uint2 c = lds64(cbl + (id << 7));
-      const __half2 a0 = __hmul2(*(const __half2*)&c.x, s2), a1 = __hmul2(*(const __half2*)&c.y, s2);
-      v[2 * (4 * q + j)] = *(const uint32_t*)&a0;
-      v[2 * (4 * q + j) + 1] = *(const uint32_t*)&a1;
+      const __nv_fp8x2_storage_t p0 = __nv_cvt_float2_to_fp8x2(f16x2_times_f16(c.x, sb), __NV_SATFINITE, __NV_E4M3);
+      const __nv_fp8x2_storage_t p1 = __nv_cvt_float2_to_fp8x2(f16x2_times_f16(c.y, sb), __NV_SATFINITE, __NV_E4M3);
+      v[4 * q + j] = (uint32_t)p0 | ((uint32_t)p1 << 16);
     }
   }
 }
 
+// fp8: the 16 sub-vectors of one 64-group (one scale) -> 16 words.
+__device__ __forceinline__ void decode16_fp8(uint32_t cbl, uint4 lo, uint32_t hw, unsigned short sb, uint32_t* v) {
+  decode8_fp8(cbl, make_uint2(lo.x, lo.y), hw & 0xFFFFu, sb, v);
+  decode8_fp8(cbl, make_uint2(lo.z, lo.w), hw >> 16, sb, v + 8);
+}
+
+// f16: 4 sub-vectors of a row (lo: 4 low index bytes, hw: 1 hi byte) -> 8 words of 2 f16 values,
+// C[id] * sc in fp16.
+__device__ __forceinline__ void decode4_f16(uint32_t cbl, uint32_t lo, uint32_t hw, unsigned short sb, uint32_t* v) {
+  const __half2 s2 = __half2half2(__ushort_as_half(sb));
+  uint32_t ids[2];
+  unpack_ids4(lo, hw & 0xFFu, ids[0], ids[1]);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    const uint32_t id = (j & 2) ? (ids[j & 1] >> 16) : (ids[j & 1] & 0xFFFFu);
+    const uint2 c = lds64(cbl + (id << 7));
+    const __half2 a0 = __hmul2(*(const __half2*)&c.x, s2), a1 = __hmul2(*(const __half2*)&c.y, s2);
+    v[2 * j] = *(const uint32_t*)&a0;
+    v[2 * j + 1] = *(const uint32_t*)&a1;
+  }
+}
+
+__device__ __forceinline__ void tmem_st8(uint32_t taddr, const uint32_t* v) {
+  asm volatile("tcgen05.st.sync.aligned.32x32b.x8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};"
+               ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
 __device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t* v) {
   asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
                ::"r"(taddr), "r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]),
                  "r"(v[8]), "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15])
                : "memory");
 }
+__device__ __forceinline__ void keep_live16(const uint32_t* v) {
+  asm volatile("" ::"r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]), "r"(v[8]),
+               "r"(v[9]), "r"(v[10]), "r"(v[11]), "r"(v[12]), "r"(v[13]), "r"(v[14]), "r"(v[15]));
+}
+// An empty statement that reads 8 registers: keeps them allocated (unmodified) up to this point.
+__device__ __forceinline__ void keep_live8(const uint32_t* v) {
+  asm volatile("" ::"r"(v[0]), "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7]));
+}
+
 __device__ __forceinline__ void tmem_st_wait() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // D (TMEM) += A (TMEM, M = 128 weight rows, K-major) . B (shared memory descriptor, N slots)^T
@@ -175,7 +208,7 @@ constexpr int P2_NMAX = 192;                 // slots per chunk (MMA N at most)
 constexpr int P2_BM = 32;                    // per-expert slot padding (moe_align block)
 constexpr int P2_CHUNK_BLOCKS = P2_NMAX / P2_BM;
 constexpr int P2_BSTAGES = 2, P2_ISTAGES = 3, P2_ASTAGES = 2;
-constexpr int P2_DEC_WARPS = 16;
+constexpr int P2_DEC_WARPS = 16;            // 4 per TMEM lane quarter: row tile x K half
 constexpr int P2_THREADS = (3 + P2_DEC_WARPS) * 32;
 constexpr int P2_BTILE = P2_NMAX * 128;      // one B stage: 192 slot rows x 128 bytes (SW128)
 constexpr int P2_CB_COPIES = 16;
@@ -300,15 +333,14 @@ prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const 
     int gi = 0;
     for (int w = blockIdx.x; w < nwork && !*abort; w += gridDim.x) {
       const int e = a.chunks[w / a.T].x, tile = w % a.T;
-      const uint8_t* hi_r[8];
-      const uint8_t* sc_r[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        const int R = lane + 32 * i;
-        const long wr = p2_weight_row<GATEUP>(a, e, tile, R >> 7, R & 127);
-        hi_r[i] = a.hi + wr * (nsub / 4);
-        sc_r[i] = (const uint8_t*)(a.sc + wr * ngk);
-      }
+      // this lane's rows are lane + 32 i (i < 4: tile 0, else tile 1); hi / scale row pointers
+      // are formed from one base per tile
+      const long wr0 = p2_weight_row<GATEUP>(a, e, tile, 0, lane), wr1 = p2_weight_row<GATEUP>(a, e, tile, 1, lane);
+      const uint8_t* hi_b0 = a.hi + wr0 * (nsub / 4);
+      const uint8_t* hi_b1 = a.hi + wr1 * (nsub / 4);
+      const uint8_t* sc_b0 = (const uint8_t*)(a.sc + wr0 * ngk);
+      const uint8_t* sc_b1 = (const uint8_t*)(a.sc + wr1 * ngk);
+      const long hi_step = 32L * (nsub / 4), sc_step = 32L * ngk * 2;
       const int row0 = (int)p2_weight_row<GATEUP>(a, e, tile, 0, 0);
       const int row1 = (int)p2_weight_row<GATEUP>(a, e, tile, 1, 0);
       for (int c = 0; c < nstage; ++c, ++gi) {
@@ -323,12 +355,14 @@ prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const 
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           const int R = lane + 32 * i;
+          const uint8_t* hi_r = (i < 4 ? hi_b0 : hi_b1) + (i & 3) * hi_step;
+          const uint8_t* sc_r = (i < 4 ? sc_b0 : sc_b1) + (i & 3) * sc_step;
           if (PREC == VQ2_PREC_FP8) {          // hi: 8 bytes (32 sub-vectors); scales of 2 groups
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(ibase + P2_IDX_HI + R * 8), "l"(hi_r[i] + c * 8) : "memory");
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + P2_IDX_SC + R * 4), "l"(sc_r[i] + c * 4) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(ibase + P2_IDX_HI + R * 8), "l"(hi_r + c * 8) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + P2_IDX_SC + R * 4), "l"(sc_r + c * 4) : "memory");
           } else {                             // hi: 4 bytes (16 sub-vectors); the scale pair holding this group
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + P2_IDX_HI + R * 8), "l"(hi_r[i] + c * 4) : "memory");
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + P2_IDX_SC + R * 4), "l"(sc_r[i] + (c & ~1) * 2) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + P2_IDX_HI + R * 8), "l"(hi_r + c * 4) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + P2_IDX_SC + R * 4), "l"(sc_r + (c & ~1) * 2) : "memory");
           }
         }
         asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&sh->full_i[slot])) : "memory");
@@ -370,41 +404,63 @@ prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const 
     }
   } else {
     // ---------------- decoders (16 warps): warp -> TMEM lane quarter q, row tile t, K half h
+    // Software-pipelined by one stage: the tensor-memory store of stage c is issued, then stage
+    // c + 1's index planes are read and decoded into registers, and only then is the store of
+    // stage c waited for and the stage handed to the MMA warp, so the store latency does not sit
+    // on the decode chain.
     const int q = warp & 3, j = (warp - 3) >> 2, t = j >> 1, h = j & 1;
     const int r = q * 32 + lane, R = t * P2_ROWS + r;
     const uint32_t cbl = smem_u32(cbs) + (lane & (P2_CB_COPIES - 1)) * 8;
     const uint32_t tlane = (uint32_t)(q * 32) << 16;
     int gi = 0, ga = 0, it = 0;
+    // stage gi of the index ring -> 16 decoded words (this thread's row, K half), then frees the
+    // slot (after the decode consumed every lane's loads of it: the next writer is the loader's
+    // TMA / cp.async)
+    auto decode_stage = [&](int c, uint32_t* v) -> bool {
+      const int islot = gi % P2_ISTAGES;
+      if (!mbar_wait(&sh->full_i[islot], (gi / P2_ISTAGES) & 1)) return false;
+      const uint32_t ip = smem_u32(I_t(islot));
+      if (PREC == VQ2_PREC_FP8) {             // one 64-group: 16 sub-vectors
+        const uint4 lo = lds128_v(ip + R * 32 + h * 16);
+        const uint32_t hw = lds32_v(ip + P2_IDX_HI + R * 8 + h * 4);
+        const uint32_t sbits = lds16_v(ip + P2_IDX_SC + R * 4 + h * 2);
+        decode16_fp8(cbl, lo, hw, (unsigned short)sbits, v);
+      } else {                                // half of a 64-group: 8 sub-vectors
+        const uint2 lo = lds64_v(ip + R * 16 + h * 8);
+        const uint32_t hw = lds16_v(ip + P2_IDX_HI + R * 8 + h * 2);
+        const uint32_t sbits = lds16_v(ip + P2_IDX_SC + R * 4 + (c & 1) * 2);
+        decode4_f16(cbl, lo.x, hw, (unsigned short)sbits, v);
+        decode4_f16(cbl, lo.y, hw >> 8, (unsigned short)sbits, v + 8);
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&sh->empty_i[islot]);
+      ++gi;
+      return true;
+    };
     for (int w = blockIdx.x; w < nwork; w += gridDim.x, ++it) {
       const int4 ch = a.chunks[w / a.T];
       const int tile = w % a.T;
       bool ok = !*abort;
-      for (int c = 0; c < nstage && ok; ++c, ++gi, ++ga) {
-        const int islot = gi % P2_ISTAGES, aslot = ga % P2_ASTAGES;
-        if (!mbar_wait(&sh->full_i[islot], (gi / P2_ISTAGES) & 1)) { ok = false; break; }
-        if (ga >= P2_ASTAGES && !mbar_wait(&sh->empty_a[aslot], ((ga / P2_ASTAGES) - 1) & 1)) { ok = false; break; }
+      // two register sets: a tcgen05.st reads its source registers asynchronously, so the set
+      // being stored stays untouched (and is kept live) until its tcgen05.wait::st
+      uint32_t va[16], vb[16];
+      if (ok) ok = decode_stage(0, va);
+      auto step = [&](int c, uint32_t* cur, uint32_t* nxt) {
+        const int aslot = ga % P2_ASTAGES;
+        if (ga >= P2_ASTAGES && !mbar_wait(&sh->empty_a[aslot], ((ga / P2_ASTAGES) - 1) & 1)) { ok = false; return; }
         tc_fence_after();
-        const uint32_t ip = smem_u32(I_t(islot));
-        uint32_t v[16];
-        if (PREC == VQ2_PREC_FP8) {             // one 64-group: 16 sub-vectors
-          const uint4 lo = lds128_v(ip + R * 32 + h * 16);
-          const uint32_t hw = lds32_v(ip + P2_IDX_HI + R * 8 + h * 4);
-          const uint32_t sbits = lds16_v(ip + P2_IDX_SC + R * 4 + h * 2);
-          decode16_fp8(cbl, lo, hw, __half2float(__ushort_as_half((unsigned short)sbits)), v);
-        } else {                                // half of a 64-group: 8 sub-vectors
-          const uint2 lo = lds64_v(ip + R * 16 + h * 8);
-          const uint32_t hw = lds16_v(ip + P2_IDX_HI + R * 8 + h * 2);
-          const uint32_t sbits = lds16_v(ip + P2_IDX_SC + R * 4 + (c & 1) * 2);
-          decode8_f16(cbl, lo, hw, __half2float(__ushort_as_half((unsigned short)sbits)), v);
-        }
-        tmem_st16(tmem + tlane + p2_a_col(aslot, t) + 16 * h, v);
+        tmem_st16(tmem + tlane + p2_a_col(aslot, t) + 16 * h, cur);
+        if (c + 1 < nstage && !decode_stage(c + 1, nxt)) ok = false;
         tmem_st_wait();
+        keep_live16(cur);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) {
-          mbar_arrive(&sh->full_a[aslot]);
-          mbar_arrive(&sh->empty_i[islot]);
-        }
+        if (lane == 0) mbar_arrive(&sh->full_a[aslot]);
+        ++ga;
+      };
+      for (int c = 0; c < nstage && ok; c += 2) {
+        step(c, va, vb);
+        if (c + 1 < nstage && ok) step(c + 1, vb, va);
       }
       if (!ok) *abort = 1;
       if (*abort) break;
@@ -414,33 +470,39 @@ prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const 
       const int ncol = ch.z >> 5;                          // 32-slot column groups
       if (GATEUP) {
         for (int cg = j; cg < ncol; cg += 4) {
-          float g[32], u[32];
-          tmem_ld32(tmem + tlane + p2_acc_col(0) + cg * 32, g);
-          tmem_ld32(tmem + tlane + p2_acc_col(1) + cg * 32, u);
           const int s0 = ch.y + cg * 32;
           const float myinv = a.inv_slot[s0 + lane];
           float* dst = a.inter + (size_t)s0 * a.I + tile * P2_ROWS + r;
+#pragma unroll 1
+          for (int hh = 0; hh < 4; ++hh) {          // 8 columns at a time (register budget)
+            float g[8], u[8];
+            tmem_ld8(tmem + tlane + p2_acc_col(0) + cg * 32 + hh * 8, g);
+            tmem_ld8(tmem + tlane + p2_acc_col(1) + cg * 32 + hh * 8, u);
 #pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const float inv = __shfl_sync(0xffffffffu, myinv, k);
-            const float gg = g[k] * inv, uu = u[k] * inv;
-            dst[(size_t)k * a.I] = gg / (1.f + __expf(-gg)) * uu;
+            for (int k = 0; k < 8; ++k) {
+              const float inv = __shfl_sync(0xffffffffu, myinv, hh * 8 + k);
+              const float gg = g[k] * inv, uu = u[k] * inv;
+              dst[(size_t)(hh * 8 + k) * a.I] = __fdividef(gg, 1.f + __expf(-gg)) * uu;
+            }
           }
         }
       } else {
         for (int u = j; u < P2_NT * ncol; u += 4) {
           const int tt = u & 1, cg = u >> 1;
-          float v[32];
-          tmem_ld32(tmem + tlane + p2_acc_col(tt) + cg * 32, v);
           const int s = ch.y + cg * 32 + lane;
           const int mytok = a.val[s] ? a.st[s] : -1;
           const float myw = mytok >= 0 ? a.topk_w[(size_t)mytok * a.topk + a.ss[s]] * a.inv_slot[s] : 0.f;
           float* col = a.out + tile * (P2_NT * P2_ROWS) + tt * P2_ROWS + r;
 #pragma unroll
-          for (int k = 0; k < 32; ++k) {
-            const int tok = __shfl_sync(0xffffffffu, mytok, k);
-            const float wk = __shfl_sync(0xffffffffu, myw, k);
-            if (tok >= 0) atomicAdd(col + (size_t)tok * a.H, v[k] * wk);
+          for (int hh = 0; hh < 2; ++hh) {          // 16 columns at a time (register budget)
+            float v[16];
+            tmem_ld16(tmem + tlane + p2_acc_col(tt) + cg * 32 + hh * 16, v);
+#pragma unroll
+            for (int k = 0; k < 16; ++k) {
+              const int tok = __shfl_sync(0xffffffffu, mytok, hh * 16 + k);
+              const float wk = __shfl_sync(0xffffffffu, myw, hh * 16 + k);
+              if (tok >= 0) atomicAdd(col + (size_t)tok * a.H, v[k] * wk);
+            }
           }
         }
       }
