@@ -411,6 +411,60 @@ def time_prefill(layers, dev, args, N=8192):
     return res
 
 
+STACK_LAYERS, STACK_TOKENS = 8, 65536
+
+
+def stack_flops(tokens=STACK_TOKENS, layers=STACK_LAYERS):
+    """Algorithmic FLOPs of the config-4 stack: per layer 2*M*H*2I + 2*M*I*H over M = tokens*top-k."""
+    M = tokens * K
+    return layers * (2.0 * M * H * 2 * I + 2.0 * M * I * H)
+
+
+def time_stack(dev, args, tokens=STACK_TOKENS):
+    """Config 4 on one GPU: 8 seeded layers (all 256 experts resident), 65,536 tokens, Zipf(1.1)
+    top-8 routing drawn per layer, fp8 prefill (the plugin's default), x = x + moe(x) in bf16.
+    One step = the whole stack; CUDA events around `reps` steps after one warm-up step."""
+    from vq2_vllm import synth
+    from vq2_vllm.kernels.ds4_vq2_cuda import vq2_moe_grouped_wmma
+    _, bf16_peak, src = peaks()
+    layers = [synth.make_layer(E, H, I, seed=4000 + l, device=dev) for l in range(STACK_LAYERS)]
+    routes = [synth.route_zipf(tokens, E, K, s=1.1, seed=4100 + l, device=dev) for l in range(STACK_LAYERS)]
+    x0 = synth.make_tokens(tokens, H, seed=4200, device=dev)
+    per_layer_ms = [0.0] * STACK_LAYERS
+    ev = [torch.cuda.Event(True) for _ in range(STACK_LAYERS + 1)]
+
+    def step(record):
+        x = x0
+        if record:
+            ev[0].record()
+        for l in range(STACK_LAYERS):
+            x = x + vq2_moe_grouped_wmma(x, *routes[l], *synth.layer_args(layers[l]), precision="fp8").to(x.dtype)
+            if record:
+                ev[l + 1].record()
+        return x
+
+    step(False)
+    torch.cuda.synchronize()
+    reps = max(1, min(args.steps, 3))
+    tot = 0.0
+    for _ in range(reps):
+        step(True)
+        ev[-1].synchronize()
+        for l in range(STACK_LAYERS):
+            per_layer_ms[l] += ev[l].elapsed_time(ev[l + 1]) / reps
+        tot += ev[0].elapsed_time(ev[-1]) / reps
+    fl = stack_flops(tokens) / STACK_LAYERS
+    peak = 2 * bf16_peak
+    out = {"workload": f"config4 stack on 1 GPU: {STACK_LAYERS} layers, {tokens} tokens, Zipf(1.1) top-8 per layer, fp8, residual",
+           "ms_per_stack": tot, "tok_per_s": tokens / (tot * 1e-3),
+           "per_layer_ms": [round(v, 3) for v in per_layer_ms],
+           "per_layer_tensor_frac": [round(fl / (v * 1e-3) / 1e12 / peak, 4) for v in per_layer_ms],
+           "tensor_frac_peak": f"2x {src} bf16 (fp8 dense rate is twice bf16)", "reps": reps}
+    del layers
+    torch.cuda.empty_cache()
+    return out
+
+
 def run_ours(args, rank, world):
     from vq2_vllm import synth
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", 0)))
@@ -438,33 +492,46 @@ def run_ours(args, rank, world):
     all_bytes = idx_bytes + u1 * SC_BYTES_PER_EXPERT + 2 * 8192
     achieved = idx_bytes / (ms1 * 1e-3) / 1e9
 
-    # e2e: the public host-buffer entry (vq2_moe_fused_10b_host -> vq2_decode_host): every step
-    # copies its token row, ids and routing weights from page-locked host memory to the device and
-    # the fp32 result back, inside the timed region
-    from vq2_vllm.kernels.vq2_kernel import vq2_moe_fused_10b_host
-    xh = [x.cpu().pin_memory() for x in [synth.make_tokens(1, H, seed=100 + j) for j in range(8)]]
-    rh = [(r[0].cpu().pin_memory(), r[1].cpu().pin_memory()) for r in
+    # e2e: the public host-buffer API (HostDecodeSession, one per layer): every step copies its
+    # token row, ids and routing weights from page-locked host memory to the device (one copy)
+    # and the fp32 result back, inside the timed region; the host waits on a slot's previous step
+    # before reusing it
+    from vq2_vllm.kernels.vq2_kernel import HostDecodeSession
+    xh = [x.cpu() for x in [synth.make_tokens(1, H, seed=100 + j) for j in range(8)]]
+    rh = [(r[0].cpu(), r[1].cpu()) for r in
           [make_routing(synth.make_tokens(1, H, seed=100 + j, device=dev), 200 + j) for j in range(8)]]
-    outh = [torch.empty(1, H, dtype=torch.float32).pin_memory() for _ in range(2)]
+    sessions = [HostDecodeSession(*synth.layer_args(L), N=1, k=K) for L in layers]
 
     def e2e_step(i):
-        L = layers[i % nlayers]
-        vq2_moe_fused_10b_host(xh[i % 8], rh[i % 8][0], rh[i % 8][1], *synth.layer_args(L), out=outh[i % 2])
+        sessions[i % nlayers].step(xh[i % 8], *rh[i % 8])
 
-    for i in range(3):
+    for i in range(8):
         e2e_step(i)
     torch.cuda.synchronize()
-    s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+    # the timed region ends with the last download: a device-wide event after all streams joined
+    t0 = time.perf_counter()
+    s = torch.cuda.Event(True)
     s.record()
     for i in range(args.steps):
         e2e_step(i)
+    for ss in sessions:
+        torch.cuda.current_stream().wait_stream(ss.s_out)
+    e = torch.cuda.Event(True)
     e.record()
     e.synchronize()
     e2e_ms = s.elapsed_time(e) / args.steps
-    h2d = H * 2 + K * 4 + K * 4
+    e2e_wall_ms = (time.perf_counter() - t0) * 1e3 / args.steps
+    h2d = sessions[0].nin                # one copy of the packed slot: x | ids | w (256-byte aligned parts)
+    del sessions
     d2h = H * 4
 
     prefill = time_prefill(layers, dev, args)
+    del layers
+    torch.cuda.empty_cache()
+    try:
+        stack = time_stack(dev, args)
+    except Exception as ex:  # a figure beside the headline must not cost the headline line
+        stack = {"error": f"{type(ex).__name__}: {ex}"[:300]}
     router = time_router(dev)
     try:
         shared = time_shared(dev, hbm)
@@ -511,8 +578,11 @@ def run_ours(args, rank, world):
             "cpu_baseline_prefill": {"value": cpu_pf, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
                                      "cpu_model": cpu_model(),
                                      "sample": cpu_pf_sample},
-            "e2e": {"value": e2e_ms * 1e3, "unit": "us/token", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "e2e": {"value": e2e_ms * 1e3, "unit": "us/token", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                    "host_wall_us_per_step": e2e_wall_ms * 1e3,
+                    "how": "HostDecodeSession: per step one upload (copy stream), the decode kernels, one download (second copy stream)"},
             "prefill": prefill,
+            "stack": stack,
             "gpu_launches": 2 * args.steps,
             "clocks": clocks}
     print(json.dumps(line), flush=True)

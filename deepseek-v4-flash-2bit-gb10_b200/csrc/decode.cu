@@ -823,6 +823,52 @@ extern "C" int vq2_decode_host(const vq2_moe_args* a, const void* h_x, const voi
   return cudaMemcpyAsync(h_out, b.out, ob, cudaMemcpyDeviceToHost, st) == cudaSuccess ? VQ2_OK : VQ2_ERR_CUDA;
 }
 
+// Pipelined variant for serving loops: the packed inputs (x | ids | w, at the offsets of
+// vq2_decode_host_offsets) are uploaded on `in_stream`, the kernels run on `stream` after the
+// upload (ev_in), and the result is downloaded on `out_stream` after the kernels (ev_done, then
+// ev_out marks the download), so the copies of neighbouring steps overlap this step's kernels.
+extern "C" void vq2_decode_host_offsets(int N, int topk, int H, int x_dtype, int ids_dtype, size_t* off_ids,
+                                        size_t* off_w, size_t* in_bytes) {
+  const size_t xb = (size_t)N * H * (x_dtype == VQ2_DT_F32 ? 4 : 2);
+  const size_t ib = (size_t)N * topk * (ids_dtype == VQ2_ID_I64 ? 8 : 4);
+  const size_t wb = (size_t)N * topk * 4;
+  *off_ids = stage_part(xb);
+  *off_w = stage_part(xb) + stage_part(ib);
+  *in_bytes = stage_part(xb) + stage_part(ib) + stage_part(wb);
+}
+
+extern "C" int vq2_decode_host_async(const vq2_moe_args* a, const void* h_in, float* h_out, void* d_in,
+                                     float* d_out, void* ws, size_t ws_bytes, void* stream, void* in_stream,
+                                     void* out_stream, void* ev_in, void* ev_done, void* ev_out) {
+  if (!a || !h_in || !h_out || !d_in || !d_out || !ev_in || !ev_done || !ev_out) return VQ2_ERR_NULL;
+  if (a->N <= 0 || a->topk <= 0 || a->H <= 0) return VQ2_ERR_SHAPE;
+  if (a->x_dtype < 0 || a->x_dtype > 2 || a->ids_dtype < 0 || a->ids_dtype > 1) return VQ2_ERR_DTYPE;
+  if (((uintptr_t)d_in & 255) != 0) return VQ2_ERR_ALIGN;
+  size_t off_i = 0, off_w = 0, nin = 0;
+  vq2_decode_host_offsets(a->N, a->topk, a->H, a->x_dtype, a->ids_dtype, &off_i, &off_w, &nin);
+  vq2_moe_args b = *a;
+  b.x = d_in;
+  b.topk_ids = (const uint8_t*)d_in + off_i;
+  b.topk_w = (const float*)((const uint8_t*)d_in + off_w);
+  b.out = d_out;
+  cudaStream_t s = (cudaStream_t)stream, si = (cudaStream_t)in_stream, so = (cudaStream_t)out_stream;
+  cudaEvent_t ei = (cudaEvent_t)ev_in, ed = (cudaEvent_t)ev_done, eo = (cudaEvent_t)ev_out;
+  // the events still mark this slot's previous step: its kernels must be done with d_in before
+  // the upload, and its download done with d_out before the kernels write it
+  if (cudaStreamWaitEvent(si, ed, 0) != cudaSuccess ||
+      cudaMemcpyAsync(d_in, h_in, nin, cudaMemcpyHostToDevice, si) != cudaSuccess ||
+      cudaEventRecord(ei, si) != cudaSuccess || cudaStreamWaitEvent(s, ei, 0) != cudaSuccess ||
+      cudaStreamWaitEvent(s, eo, 0) != cudaSuccess)
+    return VQ2_ERR_CUDA;
+  const int rc = vq2_decode(&b, ws, ws_bytes, stream);
+  if (rc) return rc;
+  if (cudaEventRecord(ed, s) != cudaSuccess || cudaStreamWaitEvent(so, ed, 0) != cudaSuccess ||
+      cudaMemcpyAsync(h_out, d_out, (size_t)a->N * a->H * sizeof(float), cudaMemcpyDeviceToHost, so) != cudaSuccess ||
+      cudaEventRecord(eo, so) != cudaSuccess)
+    return VQ2_ERR_CUDA;
+  return VQ2_OK;
+}
+
 static_assert(offsetof(vq2::DecodeShared, xs) % 16 == 0, "xs must be 16-byte aligned");
 static_assert(offsetof(vq2::DecodeShared, scratch) % 16 == 0, "bulk-copy destination must be 16-byte aligned");
 static_assert(offsetof(vq2::DecodeShared, ekey) % 16 == 0, "ekey is read as int4");

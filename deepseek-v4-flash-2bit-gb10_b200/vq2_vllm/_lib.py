@@ -38,6 +38,9 @@ _SIGS = {
     "vq2_decode_host": (ctypes.c_int, [ctypes.POINTER(Vq2MoeArgs), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
                                        ctypes.c_void_p, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p,
                                        ctypes.c_size_t, ctypes.c_void_p]),
+    "vq2_decode_host_offsets": (None, [ctypes.c_int] * 5 + [ctypes.POINTER(ctypes.c_size_t)] * 3),
+    "vq2_decode_host_async": (ctypes.c_int, [ctypes.POINTER(Vq2MoeArgs)] + [ctypes.c_void_p] * 5 + [ctypes.c_size_t]
+                              + [ctypes.c_void_p] * 6),
     "vq2_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(Vq2MoeArgs), ctypes.c_void_p]),
     "vq2_prefill_workspace_size": (ctypes.c_size_t, [ctypes.c_int] * 6),
     "vq2_prefill": (ctypes.c_int, [ctypes.POINTER(Vq2MoeArgs), ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t,

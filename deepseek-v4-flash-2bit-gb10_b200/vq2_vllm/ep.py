@@ -394,6 +394,51 @@ def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
         dist.barrier()
         return ms.item()
 
+    def run_stack(tokens_total=65536, nl=8, reps=2):
+        """Config 4: a stack of `nl` seeded layers over `tokens_total` tokens (tokens_total / W per
+        rank), Zipf(1.1) top-8 per layer (one expert popularity per layer, shared by the ranks),
+        x = x + moe(x) in bf16, NCCL all-to-all dispatch and combine, each rank's experts on the
+        grouped GEMM (fp8). Whole-stack time on the device, max over ranks."""
+        n = tokens_total // world
+        Ls = [synth.make_layer(per, H, I, seed=5000 + 100 * l + rank, device=dev) for l in range(nl)]
+        sfns = [cuda_expert_fn(L) for L in Ls]
+        x0 = synth.make_tokens(n, H, seed=6000 + rank, device=dev)
+        routes = [synth.route_zipf(n, E, K, s=1.1, seed=7000 + l, device=dev, draw_seed=7100 + 100 * l + rank)
+                  for l in range(nl)]
+        loads = []
+        for ids, _ in routes:           # pairs per owning rank, summed over the ranks
+            cnt = torch.bincount((ids.long() // per).flatten(), minlength=world).float()
+            dist.all_reduce(cnt)
+            loads.append((cnt.max() / cnt.mean()).item())
+
+        def stack_step():
+            x = x0
+            for l in range(nl):
+                x = x + ep_moe(x, *routes[l], sfns[l], E).to(x.dtype)
+            return x
+
+        stack_step()
+        torch.cuda.synchronize()
+        dist.barrier()
+        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+        s.record()
+        for _ in range(reps):
+            stack_step()
+        e.record()
+        e.synchronize()
+        ms = torch.tensor([s.elapsed_time(e) / reps], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        ms = ms.item()
+        flops = nl * (2.0 * tokens_total * K * H * 2 * I + 2.0 * tokens_total * K * I * H)
+        bf16 = peaks_fn()[1] if peaks_fn is not None else 1590.0
+        del Ls, sfns
+        torch.cuda.empty_cache()
+        return {"workload": f"config4: {nl} layers, {tokens_total} tokens ({n} per rank), Zipf(1.1) top-8, fp8, "
+                            f"residual, ep{world} (NCCL all-to-all)",
+                "ms_per_stack": ms, "tok_per_s": tokens_total / (ms * 1e-3),
+                "tensor_frac_per_gpu": flops / world / (ms * 1e-3) / 1e12 / (2 * bf16),
+                "expert_load_max_over_mean_per_layer": [round(v, 3) for v in loads], "reps": reps}
+
     def detail(per_rank, ms):
         """Per-GPU HBM rate on the index bytes of this rank's distinct experts (mean over ranks)
         and the exchange alone."""
@@ -451,6 +496,7 @@ def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
             m = run(total // world, max(3, args.steps // 4), 3)
             extra[f"config3_{total}_tokens"] = {"ms_per_step": m, "us_per_token": m * 1e3 / total,
                                                 **detail(total // world, m)}
+    stack = run_stack() if os.environ.get("VQ2_BENCH_STACK", "1") == "1" else None
     p2p_used = use_p2p and all(v is not None for v in exchanges.values())
     hbm, src = (peaks_fn()[0], peaks_fn()[2]) if peaks_fn is not None else (None, None)
     achieved = d1["local_idx_GBps_per_gpu"]
@@ -474,6 +520,7 @@ def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
                        "exchange": "nvlink peer memory (vq2_ep_dispatch / vq2_ep_combine)" if p2p_used
                        else "nccl all_gather + reduce_scatter"},
                 "cuda_graphs": {str(k): v for k, v in graphs_used.items()},
+                "stack": stack,
                 # this package's kernels per timed step: the two decode kernels, plus dispatch and
                 # combine with the peer-memory exchange (NCCL kernels are not counted)
                 "gpu_launches": (4 if p2p_used else 2) * args.steps}

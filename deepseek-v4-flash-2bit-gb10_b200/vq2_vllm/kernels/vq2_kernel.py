@@ -162,6 +162,97 @@ def vq2_moe_fused_10b_host(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, 
     return out
 
 
+class HostDecodeSession:
+    """Decode steps of one layer at a fixed batch shape whose inputs and result live in host
+    memory (extension; the reference's callers hold device tensors) — the shape of a serving loop
+    that receives token rows from the host and returns results to it.
+
+    ``slots`` staging slots each own page-locked host buffers (packed inputs x | topk_ids | topk_w,
+    and the fp32 result), device buffers and three events. A step is one library call
+    (vq2_decode_host_async): the upload runs on a copy stream, the decode kernels on the current
+    stream of the weights' device, the download on a second copy stream, so the copies of
+    neighbouring steps overlap this step's kernels. ``step`` first waits until the slot's previous
+    upload has read its host buffer; the returned host tensor is valid once ``done(slot)`` is true
+    (and stays valid until the slot is reused, ``slots`` steps later)."""
+
+    def __init__(self, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, N, k, x_dtype=torch.bfloat16, ids_dtype=torch.int32,
+                 slots=4, expert_base=0):
+        import ctypes
+        self._ctypes = ctypes
+        ws = [Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn]
+        want = (_F16, _U8, _U8, _F16, _F16, _U8, _U8, _F16)
+        for t, d in zip(ws, want):
+            if not _ok(t, d):
+                raise ValueError("HostDecodeSession: weights must be contiguous fp16 codebooks/scales and u8 planes")
+        _lib.require_cuda(*ws, device=lgu.get_device())
+        if x_dtype not in _lib.DT or ids_dtype not in _lib.ID:
+            raise ValueError("HostDecodeSession: x bf16/fp16/fp32, ids int32/int64")
+        if N * k > _lib.DECODE_MAX_PAIRS:
+            raise ValueError(f"HostDecodeSession: N*k = {N * k} above the decode limit {_lib.DECODE_MAX_PAIRS}")
+        dev = lgu.device
+        H = lgu.shape[2] * 4
+        I = lgu.shape[1] // 2
+        self.N, self.k, self.H, self.slots, self.dev = N, k, H, slots, dev
+        L = self._L = _lib.lib()
+        oi, ow, nin = ctypes.c_size_t(), ctypes.c_size_t(), ctypes.c_size_t()
+        L.vq2_decode_host_offsets(N, k, H, _lib.DT[x_dtype], _lib.ID[ids_dtype], ctypes.byref(oi), ctypes.byref(ow),
+                                  ctypes.byref(nin))
+        self.off_i, self.off_w, self.nin = oi.value, ow.value, nin.value
+        xe, ie = torch.empty(0, dtype=x_dtype).element_size(), torch.empty(0, dtype=ids_dtype).element_size()
+        self.xb, self.ib, self.wb = N * H * xe, N * k * ie, N * k * 4
+        self.nws = L.vq2_decode_workspace_size(N, k, H, I)
+        up = lambda v: (v + 255) & ~255
+        self.h_in = torch.empty(slots, up(self.nin), dtype=torch.uint8, pin_memory=True)
+        self.h_out = torch.empty(slots, N, H, dtype=_F32, pin_memory=True)
+        self.d_in = torch.empty(slots, up(self.nin), dtype=torch.uint8, device=dev)
+        self.d_out = torch.empty(slots, N, H, dtype=_F32, device=dev)
+        self.d_ws = torch.empty(slots, self.nws, dtype=torch.uint8, device=dev)
+        self.s_in, self.s_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+        self.ev = [[torch.cuda.Event() for _ in range(3)] for _ in range(slots)]   # in, done, out
+        with torch.cuda.device(dev):
+            for sl in range(slots):            # every event exists (recorded once) before first use
+                for e in self.ev[sl]:
+                    e.record()
+        torch.cuda.synchronize(dev)
+        a = self._args = _lib.Vq2MoeArgs()
+        a.N, a.H, a.I, a.E, a.topk = N, H, I, lgu.shape[0], k
+        a.x_dtype, a.ids_dtype, a.expert_base = _lib.DT[x_dtype], _lib.ID[ids_dtype], expert_base
+        a.w13_cb, a.w13_lo, a.w13_hi, a.w13_sc = Cgu.data_ptr(), lgu.data_ptr(), hgu.data_ptr(), sgu.data_ptr()
+        a.w2_cb, a.w2_lo, a.w2_hi, a.w2_sc = Cd.data_ptr(), ld.data_ptr(), hd.data_ptr(), sdn.data_ptr()
+        self._aref = ctypes.byref(a)
+        self._ptr = [(self.h_in[sl].data_ptr(), self.h_out[sl].data_ptr(), self.d_in[sl].data_ptr(),
+                      self.d_out[sl].data_ptr(), self.d_ws[sl].data_ptr()) + tuple(e.cuda_event for e in self.ev[sl])
+                     for sl in range(slots)]
+        self._streams = (self.s_in.cuda_stream, self.s_out.cuda_stream)
+        self.i = 0
+
+    def step(self, x, topk_ids, topk_w):
+        """Queue one step on host tensors x [N, H], topk_ids [N, k], topk_w [N, k] (fp32);
+        returns (slot, the slot's host result tensor)."""
+        sl = self.i % self.slots
+        self.i += 1
+        hin, hout, din, dout, dws, e_in, e_done, e_out = self._ptr[sl]
+        self.ev[sl][0].synchronize()             # the slot's previous upload has read h_in
+        mm = self._ctypes.memmove
+        mm(hin, x.data_ptr(), self.xb)
+        mm(hin + self.off_i, topk_ids.data_ptr(), self.ib)
+        mm(hin + self.off_w, topk_w.data_ptr(), self.wb)
+        rc = self._L.vq2_decode_host_async(self._aref, hin, hout, din, dout, dws, self.nws,
+                                           torch.cuda.current_stream(self.dev).cuda_stream, self._streams[0],
+                                           self._streams[1], e_in, e_done, e_out)
+        if rc:
+            _lib.check(rc, "HostDecodeSession")
+        return sl, self.h_out[sl]
+
+    def done(self, slot) -> bool:
+        return self.ev[slot][2].query()
+
+    def synchronize(self):
+        """Wait for every queued step's download."""
+        for sl in range(self.slots):
+            self.ev[sl][2].synchronize()
+
+
 # The packer lives beside the decode entry in the reference module (vq2_kernel.py:37-72, :160-167,
 # :501-505); its implementation here is kernels/vq2_pack.py.
 from .vq2_pack import pack_vq2, pack_vq2_experts, pack_vq2_experts_10b  # noqa: E402,F401

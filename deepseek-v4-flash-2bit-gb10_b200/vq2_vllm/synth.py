@@ -65,11 +65,15 @@ def route_softmax_topk(x: torch.Tensor, E: int, k: int, w_std: float, seed: int 
     return ti.to(torch.int32), tw.float()
 
 
-def route_zipf(N: int, E: int, k: int, s: float = 1.1, seed: int = 2, device="cpu"):
+def route_zipf(N: int, E: int, k: int, s: float = 1.1, seed: int = 2, device="cpu", draw_seed=None):
     """Zipf(s)-skewed top-k routing with distinct experts per token: p_e ~ 1/rank_e^s over a
-    seeded permutation of ranks; weights = softmax of N(0,1) over the k picks."""
+    seeded permutation of ranks; weights = softmax of N(0,1) over the k picks. ``draw_seed``
+    (optional) seeds the token draws separately from the popularity permutation, so several
+    sources (expert-parallel ranks) share one expert popularity but draw different tokens."""
     gen = torch.Generator(device="cpu").manual_seed(seed)
     ranks = torch.randperm(E, generator=gen).double() + 1.0
+    if draw_seed is not None:
+        gen = torch.Generator(device="cpu").manual_seed(draw_seed)
     p = ranks.pow(-s)
     p = (p / p.sum()).float()
     ids = torch.multinomial(p.expand(N, E), k, replacement=False, generator=gen).to(torch.int32)

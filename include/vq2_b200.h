@@ -81,6 +81,22 @@ size_t vq2_decode_host_stage_size(int N, int topk, int H, int x_dtype, int ids_d
 int vq2_decode_host(const vq2_moe_args* a, const void* h_x, const void* h_ids, const float* h_w, float* h_out,
                     void* stage, size_t stage_bytes, void* workspace, size_t ws_bytes, void* stream);
 
+/* Pipelined host-buffer decode step (no counterpart in the reference): h_in holds the step's
+ * inputs packed as x | ids | w at the offsets vq2_decode_host_offsets gives (each part 256-byte
+ * aligned; in_bytes in total); d_in is device memory of in_bytes (256-byte aligned), d_out the
+ * device result [N,H] f32. The upload runs on in_stream and records ev_in; `stream` waits for it
+ * and runs the decode kernels, then records ev_done; out_stream waits for that, downloads the
+ * result into h_out and records ev_out. Events (cudaEvent_t as void*, one set per staging slot,
+ * recorded at least once before the first use) and streams are the caller's; a slot's previous
+ * ev_done / ev_out order its new upload and kernels after that step's kernels and download. With
+ * separate upload and download streams the copies of neighbouring steps overlap the kernels.
+ * x, topk_ids, topk_w and out in `a` are ignored. Host buffers should be page-locked. */
+void vq2_decode_host_offsets(int N, int topk, int H, int x_dtype, int ids_dtype, size_t* off_ids, size_t* off_w,
+                             size_t* in_bytes);
+int vq2_decode_host_async(const vq2_moe_args* a, const void* h_in, float* h_out, void* d_in, float* d_out,
+                          void* workspace, size_t ws_bytes, void* stream, void* in_stream, void* out_stream,
+                          void* ev_in, void* ev_done, void* ev_out);
+
 /* Allocation-free decode: no counterpart in the reference. For callers that cannot allocate
  * device memory when they call (a memory pool that forbids new allocations, a driver callback, a
  * host runtime without a CUDA allocator): same result as vq2_decode, but the gate/up scratch is a

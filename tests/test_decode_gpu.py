@@ -173,3 +173,23 @@ def test_host_buffer_entry_matches_device_entry(big_layer, N, ids64):
         torch.cuda.synchronize()
         assert not got.is_cuda and got.dtype == torch.float32
         assert torch_ref.rel_l2(got, want.cpu()) < 1e-5
+
+
+def test_host_decode_session_matches_device_entry(big_layer):
+    """HostDecodeSession (per step one library call: upload on a copy stream, the decode kernels,
+    download on a second copy stream) gives the device entry's result, over more steps than it has
+    slots (slot reuse is ordered by the slot's events)."""
+    from vq2_vllm import synth
+    from vq2_vllm.kernels.vq2_kernel import HostDecodeSession
+    sess = HostDecodeSession(*synth.layer_args(big_layer), N=2, k=8, slots=2)
+    outs = []
+    for step in range(5):
+        x = synth.make_tokens(2, 4096, seed=300 + step, device="cuda")
+        ids, tw = synth.route_softmax_topk(x, 256, 8, w_std=0.02, seed=310 + step)
+        want = _moe()(x, ids, tw, *synth.layer_args(big_layer)).cpu()
+        sl, got = sess.step(x.cpu(), ids.cpu(), tw.cpu())
+        sess.synchronize()
+        assert sess.done(sl)
+        assert torch_ref.rel_l2(got, want) < 1e-5, step
+        outs.append(got.clone())
+    assert not torch.equal(outs[0], outs[1])

@@ -49,7 +49,11 @@ def _worker(rank, world, port, q):
                     out = ep.ep_moe_p2p(x, ids, w, fn, E, exch)
                 else:
                     out = (ep.ep_moe_gather if mode == "gather" else ep.ep_moe)(x, ids, w, fn, E)
-                res.append(torch_ref.rel_l2(out, torch_ref.moe_ref(x, ids, w, layer)))
+                # above the decode pair limit the local experts run the grouped GEMM, fp8 by
+                # default: its reference is the fp8 algorithm (3e-2); decode steps: fp32 (1e-2)
+                big = N * 8 > 512
+                ref = (torch_ref.moe_prefill_fp8_ref if big else torch_ref.moe_ref)(x, ids, w, layer)
+                res.append(torch_ref.rel_l2(out, ref) * (1e-2 / 3e-2 if big else 1.0))
         from vq2_vllm import _lib
         status = _lib.lib().vq2_device_status(1)
         exch.close()
@@ -74,4 +78,4 @@ def test_ep_two_gpus():
         p.join(timeout=60)
     for rank, status, val in res:
         assert status == "ok", val
-        assert val < 1e-2
+        assert val < 1e-2      # decode steps at 1e-2, fp8 steps at 3e-2 (scaled)
