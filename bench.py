@@ -690,7 +690,8 @@ def run_profile_case(case):
     """--profile-case: a small, self-contained invocation of one hot kernel for ncu captures (a few
     GB on the device at most, a handful of launches): "decode" = four config-1 decode layer calls
     at batch 1 over two layers; "prefill" = two fp8 grouped-GEMM calls, 2048 tokens over 64
-    experts, Zipf(1.1) top-8 (a small case of the config-2 kernels)."""
+    experts, Zipf(1.1) top-8 (a small case of the config-2 kernels); "prefill-config2" = three fp8
+    calls at config 2 (8192 tokens, 256 experts: 2.2 GB of weights, a launch-list capture only)."""
     from vq2_vllm import synth
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
@@ -701,6 +702,13 @@ def run_profile_case(case):
         ids, tw = make_routing(x, 2)
         for i in range(4):
             vq2_moe_fused_10b(x, ids, tw, *synth.layer_args(layers[i % 2]))
+    elif case == "prefill-config2":
+        from vq2_vllm.kernels.ds4_vq2_cuda import vq2_moe_grouped_wmma
+        L = synth.make_layer(E, H, I, seed=10, device=dev)
+        x = synth.make_tokens(8192, H, seed=300, device=dev)
+        ids, tw = synth.route_zipf(8192, E, K, s=1.1, seed=301, device=dev)
+        for _ in range(3):
+            vq2_moe_grouped_wmma(x, ids, tw, *synth.layer_args(L), precision="fp8")
     else:
         from vq2_vllm.kernels.ds4_vq2_cuda import vq2_moe_grouped_wmma
         L = synth.make_layer(64, H, I, seed=0, device=dev)
@@ -722,7 +730,7 @@ def main():
     ap.add_argument("--soak", type=float, default=0.6, help="untimed seconds before the timed decode steps")
     ap.add_argument("--ref-gpu", action="store_true",
                     help="time the reference's own GPU path (baseline/_ref) beside ours; one JSON line")
-    ap.add_argument("--profile-case", choices=["decode", "prefill"],
+    ap.add_argument("--profile-case", choices=["decode", "prefill", "prefill-config2"],
                     help="run a small invocation of one hot kernel (for ncu captures) and exit")
     args = ap.parse_args()
     if args.profile_case:
