@@ -40,7 +40,8 @@ __device__ void align_count_chunk(const void* ids, int dt, long M, int E, int ba
 }
 
 // counts[c][e] -> absolute destination base of chunk c's first pair of expert e; block_e table.
-__device__ void align_scan(int nchunks, int E, int BM, long Pmax, int* counts, int32_t* block_e, int* sh) {
+__device__ void align_scan(int nchunks, int E, int BM, long Pmax, int* counts, int32_t* block_e, int* sh,
+                           int2* ranges) {
   int* tot = sh;                     // [E] padded sizes, then offsets
   for (int e = threadIdx.x; e < E; e += blockDim.x) {
     int run = 0;
@@ -78,6 +79,7 @@ __device__ void align_scan(int nchunks, int E, int BM, long Pmax, int* counts, i
     const int b0 = tot[e] / BM;
     const int b1 = (e + 1 < E) ? tot[e + 1] / BM : used_blocks;
     for (int b = b0; b < b1; ++b) block_e[b] = e;
+    if (ranges) ranges[e] = make_int2(b0 * BM, (b1 - b0) * BM);   // expert e's padded slot range
   }
   for (long b = used_blocks + threadIdx.x; b < nblk; b += blockDim.x) block_e[b] = E - 1;
   for (int e = threadIdx.x; e < E; e += blockDim.x)
@@ -130,6 +132,7 @@ __device__ void zero_outputs(long Pmax, int32_t* st, int32_t* ss, uint8_t* val) 
 struct AlignArgs {
   const void* ids; int dt; long M; int k; int E; int BM; int base; int drop; long Pmax; int nchunks;
   int32_t* st; int32_t* ss; uint8_t* val; int32_t* be; int* counts;
+  int2* ranges;   // optional: per expert (first slot, padded slots)
 };
 
 __global__ void __launch_bounds__(ALIGN_THREADS) align_single_kernel(AlignArgs a) {
@@ -138,7 +141,7 @@ __global__ void __launch_bounds__(ALIGN_THREADS) align_single_kernel(AlignArgs a
   zero_outputs(a.Pmax, a.st, a.ss, a.val);
   for (int i = threadIdx.x; i < (blockDim.x / 32) * a.E; i += blockDim.x) sh_wc[i] = 0;
   align_count_chunk(a.ids, a.dt, a.M, a.E, a.base, a.drop, 0, a.counts, sh_a);
-  align_scan(1, a.E, a.BM, a.Pmax, a.counts, a.be, sh_a);
+  align_scan(1, a.E, a.BM, a.Pmax, a.counts, a.be, sh_a, a.ranges);
   align_place_chunk(a.ids, a.dt, a.M, a.k, a.E, a.base, a.drop, 0, a.counts, a.st, a.ss, a.val, sh_a, sh_wc);
 }
 
@@ -150,7 +153,7 @@ __global__ void __launch_bounds__(ALIGN_THREADS) align_count_kernel(AlignArgs a)
 
 __global__ void __launch_bounds__(ALIGN_THREADS) align_scan_kernel(AlignArgs a) {
   __shared__ int sh_a[ALIGN_MAX_E + 1];
-  align_scan(a.nchunks, a.E, a.BM, a.Pmax, a.counts, a.be, sh_a);
+  align_scan(a.nchunks, a.E, a.BM, a.Pmax, a.counts, a.be, sh_a, a.ranges);
 }
 
 __global__ void __launch_bounds__(ALIGN_THREADS) align_place_kernel(AlignArgs a) {
@@ -163,8 +166,9 @@ __global__ void __launch_bounds__(ALIGN_THREADS) align_place_kernel(AlignArgs a)
 
 // Host-side launcher shared with the prefill path. `counts` needs nchunks*E ints.
 int launch_align_ex(const void* ids, int dt, long N, int k, int E, int BM, int base, int drop, int32_t* st,
-                    int32_t* ss, uint8_t* val, int32_t* be, int* counts, cudaStream_t stream) {
+                    int32_t* ss, uint8_t* val, int32_t* be, int* counts, cudaStream_t stream, int2* ranges) {
   AlignArgs a;
+  a.ranges = ranges;
   a.ids = ids; a.dt = dt; a.M = N * k; a.k = k; a.E = E; a.BM = BM; a.base = base; a.drop = drop;
   a.Pmax = a.M + (long)min(a.M, (long)E) * BM;
   a.nchunks = (int)((a.M + ALIGN_CHUNK - 1) / ALIGN_CHUNK);
@@ -188,7 +192,7 @@ int launch_align_ex(const void* ids, int dt, long N, int k, int E, int BM, int b
 
 int launch_align(const void* ids, int dt, long N, int k, int E, int BM, int32_t* st, int32_t* ss,
                  uint8_t* val, int32_t* be, int* counts, cudaStream_t stream) {
-  return launch_align_ex(ids, dt, N, k, E, BM, 0, 0, st, ss, val, be, counts, stream);
+  return launch_align_ex(ids, dt, N, k, E, BM, 0, 0, st, ss, val, be, counts, stream, nullptr);
 }
 
 }  // namespace vq2

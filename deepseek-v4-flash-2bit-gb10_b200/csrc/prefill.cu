@@ -31,7 +31,7 @@
 namespace vq2 {
 
 int launch_align_ex(const void* ids, int dt, long N, int k, int E, int BM, int base, int drop, int32_t* st,
-                    int32_t* ss, uint8_t* val, int32_t* be, int* counts, cudaStream_t stream);
+                    int32_t* ss, uint8_t* val, int32_t* be, int* counts, cudaStream_t stream, int2* ranges);
 
 // ------------------------------------------------------------------ tcgen05 helpers
 // Shared-memory matrix descriptor: K-major, 128-byte swizzle, 8-row atoms 1024 B apart (stride
@@ -520,28 +520,23 @@ prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const 
 }
 
 // ------------------------------------------------------------------ work list
-// One CTA: the chunks of every expert's slot range (moe_align output with P2_BM-slot blocks;
-// each used block starts with a valid slot, the trailing unused blocks do not), at most
-// P2_CHUNK_BLOCKS blocks each, ordered by size, largest first.
-__global__ void __launch_bounds__(1024) build_chunks_kernel(const uint8_t* __restrict__ val, const int32_t* __restrict__ be,
-                                                            int nblk, int4* __restrict__ chunks, int* __restrict__ nchunks) {
+// One CTA, a thread per expert: the chunks of every expert's padded slot range (from moe_align),
+// at most P2_NMAX slots each, ordered by size, largest first.
+__global__ void __launch_bounds__(1024) build_chunks_kernel(const int2* __restrict__ ranges, int E,
+                                                            int4* __restrict__ chunks, int* __restrict__ nchunks) {
   __shared__ int cnt[P2_CHUNK_BLOCKS + 1], base[P2_CHUNK_BLOCKS + 1];
   if (threadIdx.x <= P2_CHUNK_BLOCKS) cnt[threadIdx.x] = 0;
   __syncthreads();
   for (int pass = 0; pass < 2; ++pass) {
-    for (int b0 = threadIdx.x; b0 < nblk; b0 += blockDim.x) {
-      if (!val[(size_t)b0 * P2_BM]) continue;
-      const int e = be[b0];
-      if (b0 > 0 && be[b0 - 1] == e) continue;           // not the first block of its expert
-      int nb = 1;
-      while (b0 + nb < nblk && be[b0 + nb] == e && val[(size_t)(b0 + nb) * P2_BM]) ++nb;
-      for (int k = 0; k < nb; k += P2_CHUNK_BLOCKS) {
-        const int size = min(P2_CHUNK_BLOCKS, nb - k);
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      const int2 rg = ranges[e];
+      for (int k = 0; k < rg.y; k += P2_NMAX) {
+        const int size = min(P2_NMAX, rg.y - k) / P2_BM;
         if (pass == 0) {
           atomicAdd(&cnt[size], 1);
         } else {
           const int pos = base[size] + atomicAdd(&cnt[size], 1);
-          chunks[pos] = make_int4(e, (b0 + k) * P2_BM, size * P2_BM, 0);
+          chunks[pos] = make_int4(e, rg.x + k, size * P2_BM, 0);
         }
       }
     }
@@ -670,7 +665,7 @@ static int encode_2d(CUtensorMap* m, const void* base, uint64_t inner_bytes, uin
 struct PfLayout {
   long M, Pmax, nblk, nchunks_align;
   size_t off_st, off_ss, off_val, off_be, off_counts, off_xq, off_invx, off_xs, off_invxs, off_inter, off_vb,
-      off_invvb, off_chunks, off_nchunks, total;
+      off_invvb, off_chunks, off_nchunks, off_ranges, total;
 };
 
 static size_t up256(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -697,6 +692,7 @@ static PfLayout pf_layout(int N, int k, int E, int H, int I, int prec) {
   L.off_invvb = o; o = up256(o + (size_t)L.Pmax * 4);
   L.off_chunks = o; o = up256(o + (size_t)L.nblk * 16);
   L.off_nchunks = o; o = up256(o + 4);
+  L.off_ranges = o; o = up256(o + (size_t)E * 8);
   L.total = o + 256;
   return L;
 }
@@ -742,6 +738,7 @@ extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_
   float* invvb = (float*)(w + L.off_invvb);
   int4* chunks = (int4*)(w + L.off_chunks);
   int* nchunks = (int*)(w + L.off_nchunks);
+  int2* ranges = (int2*)(w + L.off_ranges);
   cudaStream_t st_ = (cudaStream_t)stream;
 
   int dev = 0;
@@ -758,10 +755,10 @@ extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_
   const int nsm = device_sm_count();
   if (nsm <= 0) return VQ2_ERR_CUDA;
   int rc = launch_align_ex(a->topk_ids, a->ids_dtype, a->N, a->topk, a->E, P2_BM, a->expert_base, 1, st, ss, val,
-                           be, counts, st_);
+                           be, counts, st_, ranges);
   if (rc) return rc;
   if (cudaMemsetAsync(a->out, 0, (size_t)a->N * a->H * sizeof(float), st_) != cudaSuccess) return VQ2_ERR_CUDA;
-  build_chunks_kernel<<<1, 1024, 0, st_>>>(val, be, (int)L.nblk, chunks, nchunks);
+  build_chunks_kernel<<<1, 1024, 0, st_>>>(ranges, a->E, chunks, nchunks);
 
   P2Args g = {};
   g.chunks = chunks; g.nchunks = nchunks;
