@@ -90,7 +90,7 @@ __device__ void align_scan(int nchunks, int E, int BM, long Pmax, int* counts, i
 // stable placement of one chunk: rounds of blockDim pairs, in pair order
 __device__ void align_place_chunk(const void* ids, int dt, long M, int k, int E, int ebase, int drop, int chunk,
                                   const int* base,
-                                  int32_t* st, int32_t* ss, uint8_t* val, int* sh_run, int* sh_wc) {
+                                  int32_t* st, int32_t* ss, uint8_t* val, int* sh_run, int* sh_wc, int32_t* pslot) {
   const int nw = blockDim.x / 32, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int e = threadIdx.x; e < E; e += blockDim.x) sh_run[e] = base[(long)chunk * E + e];
   __syncthreads();
@@ -111,6 +111,9 @@ __device__ void align_place_chunk(const void* ids, int dt, long M, int k, int E,
       st[rank] = (int32_t)(m / k);
       ss[rank] = (int32_t)(m % k);
       val[rank] = 1;
+      if (pslot) pslot[m] = rank;
+    } else if (pslot && m < end) {
+      pslot[m] = -1;                      // pair owned by another device (dropped)
     }
     __syncthreads();
     if (act && leader) {
@@ -133,6 +136,7 @@ struct AlignArgs {
   const void* ids; int dt; long M; int k; int E; int BM; int base; int drop; long Pmax; int nchunks;
   int32_t* st; int32_t* ss; uint8_t* val; int32_t* be; int* counts;
   int2* ranges;   // optional: per expert (first slot, padded slots)
+  int32_t* pslot; // optional: per pair, its slot (-1 if dropped)
 };
 
 __global__ void __launch_bounds__(ALIGN_THREADS) align_single_kernel(AlignArgs a) {
@@ -142,7 +146,7 @@ __global__ void __launch_bounds__(ALIGN_THREADS) align_single_kernel(AlignArgs a
   for (int i = threadIdx.x; i < (blockDim.x / 32) * a.E; i += blockDim.x) sh_wc[i] = 0;
   align_count_chunk(a.ids, a.dt, a.M, a.E, a.base, a.drop, 0, a.counts, sh_a);
   align_scan(1, a.E, a.BM, a.Pmax, a.counts, a.be, sh_a, a.ranges);
-  align_place_chunk(a.ids, a.dt, a.M, a.k, a.E, a.base, a.drop, 0, a.counts, a.st, a.ss, a.val, sh_a, sh_wc);
+  align_place_chunk(a.ids, a.dt, a.M, a.k, a.E, a.base, a.drop, 0, a.counts, a.st, a.ss, a.val, sh_a, sh_wc, a.pslot);
 }
 
 __global__ void __launch_bounds__(ALIGN_THREADS) align_count_kernel(AlignArgs a) {
@@ -161,14 +165,16 @@ __global__ void __launch_bounds__(ALIGN_THREADS) align_place_kernel(AlignArgs a)
   extern __shared__ int sh_wc[];
   for (int i = threadIdx.x; i < (blockDim.x / 32) * a.E; i += blockDim.x) sh_wc[i] = 0;
   __syncthreads();
-  align_place_chunk(a.ids, a.dt, a.M, a.k, a.E, a.base, a.drop, blockIdx.x, a.counts, a.st, a.ss, a.val, sh_a, sh_wc);
+  align_place_chunk(a.ids, a.dt, a.M, a.k, a.E, a.base, a.drop, blockIdx.x, a.counts, a.st, a.ss, a.val, sh_a, sh_wc, a.pslot);
 }
 
 // Host-side launcher shared with the prefill path. `counts` needs nchunks*E ints.
 int launch_align_ex(const void* ids, int dt, long N, int k, int E, int BM, int base, int drop, int32_t* st,
-                    int32_t* ss, uint8_t* val, int32_t* be, int* counts, cudaStream_t stream, int2* ranges) {
+                    int32_t* ss, uint8_t* val, int32_t* be, int* counts, cudaStream_t stream, int2* ranges,
+                    int32_t* pslot) {
   AlignArgs a;
   a.ranges = ranges;
+  a.pslot = pslot;
   a.ids = ids; a.dt = dt; a.M = N * k; a.k = k; a.E = E; a.BM = BM; a.base = base; a.drop = drop;
   a.Pmax = a.M + (long)min(a.M, (long)E) * BM;
   a.nchunks = (int)((a.M + ALIGN_CHUNK - 1) / ALIGN_CHUNK);
@@ -192,7 +198,7 @@ int launch_align_ex(const void* ids, int dt, long N, int k, int E, int BM, int b
 
 int launch_align(const void* ids, int dt, long N, int k, int E, int BM, int32_t* st, int32_t* ss,
                  uint8_t* val, int32_t* be, int* counts, cudaStream_t stream) {
-  return launch_align_ex(ids, dt, N, k, E, BM, 0, 0, st, ss, val, be, counts, stream, nullptr);
+  return launch_align_ex(ids, dt, N, k, E, BM, 0, 0, st, ss, val, be, counts, stream, nullptr, nullptr);
 }
 
 }  // namespace vq2

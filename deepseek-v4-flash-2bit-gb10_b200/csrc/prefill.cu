@@ -191,35 +191,41 @@ __device__ __forceinline__ void umma_tmem_a(uint32_t tmem_d, uint32_t tmem_a, ui
                  ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc));
 }
 
-// ------------------------------------------------------------------ grouped GEMM kernel
-// Persistent; one CTA per SM walks the work list w = blockIdx.x, blockIdx.x + gridDim.x, ...
-// (w -> chunk w / T, row tile w % T; chunks heaviest first). A work item is one chunk of up to
-// P2_NMAX consecutive slots of one expert (its tokens, padded to P2_BM) against P2_NT x 128
-// weight rows: GATEUP = 128 gate rows and the 128 matching up rows of tile t; otherwise 256
-// down rows. Per 128-byte K stage the decoder warps write the decoded rows into tensor memory
-// (the MMA's A operand, one 128-lane tile per 128 rows), warp 0 loads the chunk's activation rows
-// by TMA (B operand), warp 2 issues M=128 x N=slots MMAs into one TMEM accumulator per row tile.
-// The epilogue reads the accumulators (lane = weight row, column = slot): gate/up writes
+// ------------------------------------------------------------------ grouped GEMM kernel (CTA pairs)
+// Persistent; the CTAs run as pairs (clusters of 2) and pair p walks the work list
+// w = p, p + npairs, ... (w -> chunk w / T, row tile w % T; chunks heaviest first). A work item is
+// one chunk of up to P2_NMAX consecutive slots of one expert (its tokens, padded to P2_BM) against
+// 256 weight rows: 128 per CTA of the pair (GATEUP: 64 gate rows and the 64 matching up rows of
+// the pair's 128 intermediate columns; otherwise 128 down rows). Per 128-byte K stage each CTA's
+// decoder warps write its 128 decoded rows into its tensor memory (the A operand, M = 256 over the
+// pair), each CTA loads half of the slots of every accumulator by TMA (the B operand, N split over
+// the pair), and the first CTA's MMA lane issues cta_group::2 MMAs (M = 256, N <= 192) into two
+// accumulators per CTA (up to 384 slots per item). The pair shares every activation tile, so the
+// activation traffic per weight row is half that of one CTA holding 256 rows, and each decoded
+// weight serves up to 384 slots. The epilogue reads each CTA's accumulators (lane = weight row,
+// column = slot): gate/up pairs the gate and up lanes (adjacent lanes) by shuffles and writes
 // inter[slot][i] = silu(g * inv) * (u * inv) (reference vq2_grouped.cu:255-264); down adds
 // acc * w * inv_vb into out[token] with fp32 reductions.
-constexpr int P2_ROWS = 128;                 // weight rows per A tile (MMA M)
-constexpr int P2_NT = 2;                     // A tiles per work item
-constexpr int P2_NMAX = 192;                 // slots per chunk (MMA N at most)
+constexpr int P2_ROWS = 128;                 // weight rows per CTA (half of the pair's MMA M)
+constexpr int P2_NACC = 2;                   // accumulators per CTA
+constexpr int P2_NSUB = 192;                 // slots per accumulator (MMA N at most)
+constexpr int P2_NMAX = P2_NACC * P2_NSUB;   // slots per chunk
 constexpr int P2_BM = 32;                    // per-expert slot padding (moe_align block)
 constexpr int P2_CHUNK_BLOCKS = P2_NMAX / P2_BM;
-constexpr int P2_BSTAGES = 2, P2_ISTAGES = 3, P2_ASTAGES = 2;
-constexpr int P2_DEC_WARPS = 16;            // 4 per TMEM lane quarter: row tile x K half
+constexpr int P2_BSTAGES = 3, P2_ISTAGES = 4, P2_ASTAGES = 4;
+constexpr int P2_DEC_WARPS = 16;             // 4 per TMEM lane quarter: K quarter
 constexpr int P2_THREADS = (3 + P2_DEC_WARPS) * 32;
-constexpr int P2_BTILE = P2_NMAX * 128;      // one B stage: 192 slot rows x 128 bytes (SW128)
+constexpr int P2_BHALF = (P2_NSUB / 2) * 128;          // one CTA's half of one accumulator's B: 96 rows
+constexpr int P2_BTILE = P2_NACC * P2_BHALF;           // one B stage of one CTA
 constexpr int P2_CB_COPIES = 16;
 constexpr int P2_CB_BYTES = 1024 * 8 * P2_CB_COPIES;
-constexpr int P2_IDX = 11264;                // index planes of one stage: lo 256 x 32, hi 256 x 8, sc 256 x 4
-constexpr int P2_IDX_HI = 8192, P2_IDX_SC = 10240;
+constexpr int P2_IDX = 5632;                 // index planes of one stage: lo 128 x 32, hi 128 x 8, sc 128 x 4
+constexpr int P2_IDX_HI = 4096, P2_IDX_SC = 5120;
 constexpr uint32_t P2_TMEM_COLS = 512;
-// TMEM columns: accumulator of tile 0 at 0 (N <= 192), A stage 0 at 192 (2 tiles x 32 columns),
-// accumulator of tile 1 at 256, A stage 1 at 448.
-__host__ __device__ constexpr uint32_t p2_acc_col(int t) { return t ? 256u : 0u; }
-__host__ __device__ constexpr uint32_t p2_a_col(int s, int t) { return (s ? 448u : 192u) + 32u * t; }
+// TMEM columns: accumulator 0 at 0 (N <= 192), A stages 0-1 at 192 and 224, accumulator 1 at 256,
+// A stages 2-3 at 448 and 480 (32 columns each: 128 bytes of K).
+__host__ __device__ constexpr uint32_t p2_acc_col(int j) { return j ? 256u : 0u; }
+__host__ __device__ constexpr uint32_t p2_a_col(int s) { return s < 2 ? 192u + 32u * s : 448u + 32u * (s - 2); }
 
 struct P2Shared {
   uint64_t full_b[P2_BSTAGES], empty_b[P2_BSTAGES];
@@ -250,15 +256,82 @@ struct P2Args {
   int K;                     // input width (elements)
   int R;                     // weight rows per expert (2I or H)
   int I, H, topk;
-  int T;                     // row tiles per chunk
+  int T;                     // row tiles (pair items) per chunk
 };
 
-// weight row of A tile t, lane r, for row tile `tile` of expert e
-template <bool GATEUP>
-__device__ __forceinline__ long p2_weight_row(const P2Args& a, int e, int tile, int t, int r) {
-  if (GATEUP) return (long)e * a.R + (long)t * a.I + tile * P2_ROWS + r;
-  return (long)e * a.R + (long)tile * (P2_NT * P2_ROWS) + t * P2_ROWS + r;
+// ---- cluster-pair helpers
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
 }
+// the address of this CTA's shared variable `p` in CTA `cta` of the cluster
+__device__ __forceinline__ uint32_t peer_smem(const void* p, uint32_t cta) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(cta));
+  return r;
+}
+// Arrive on a barrier of another CTA of the cluster (default release semantics at CTA scope;
+// tensor-memory writes are ordered by the tcgen05 fences around the barrier, as the pair leader's
+// MMA lane issues tcgen05.fence::after_thread_sync after its wait).
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+               : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire (for barriers the peer CTA arrives on).
+__device__ __forceinline__ bool mbar_wait_cluster(uint64_t* bar, uint32_t parity) {
+  for (uint32_t i = 0; i < VQ2_WAIT_LIMIT; ++i)
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+  set_status(VQ2_ERR_TIMEOUT);
+  return false;
+}
+__device__ __forceinline__ void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n barrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// 2-D TMA load into this CTA's shared memory whose completion is counted on the pair leader's
+// barrier (`bar_cluster`: a shared::cluster address).
+__device__ __forceinline__ void tma_load_2d_pair(void* dst, const CUtensorMap* map, int x, int y, uint32_t bar_cluster) {
+  asm volatile("cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];"
+               ::"r"(smem_u32(dst)), "l"(map), "r"(x), "r"(y), "r"(bar_cluster) : "memory");
+}
+template <int PREC>
+__device__ __forceinline__ void umma_pair(uint32_t tmem_d, uint32_t tmem_a, uint64_t db, uint32_t idesc, uint32_t acc) {
+  if (PREC == VQ2_PREC_FP8)
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                 " tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], [%1], %2, %3, p;\n}"
+                 ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc));
+  else
+    asm volatile("{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+                 " tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n}"
+                 ::"r"(tmem_d), "r"(tmem_a), "l"(db), "r"(idesc), "r"(acc));
+}
+// arrives on the barrier at this offset in both CTAs once every prior MMA of the pair completed
+__device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;"
+               ::"r"(smem_u32(bar)), "h"((unsigned short)3) : "memory");
+}
+
+// Weight row of row R (0..127) of this CTA's index stage in pair item `tile` of expert e (rank:
+// the CTA in the pair). GATEUP: R < 64 are the gate rows of the CTA's 64 intermediate columns,
+// R >= 64 the matching up rows; otherwise 128 consecutive down rows.
+template <bool GATEUP>
+__device__ __forceinline__ long p2_weight_row(const P2Args& a, int e, int tile, int rank, int R) {
+  if (GATEUP) {
+    const int i = tile * P2_ROWS + rank * (P2_ROWS / 2) + (R & 63);     // intermediate column
+    return (long)e * a.R + (R < 64 ? i : a.I + i);
+  }
+  return (long)e * a.R + (long)tile * (2 * P2_ROWS) + rank * P2_ROWS + R;
+}
+// Index-stage row decoded into TMEM lane r. GATEUP interleaves gate and up: lane 2m holds the gate
+// row and lane 2m + 1 the up row of intermediate column m, so the epilogue pairs them with a lane
+// shuffle.
+template <bool GATEUP>
+__device__ __forceinline__ int p2_stage_row(int r) { return GATEUP ? (r & 1) * 64 + (r >> 1) : r; }
 
 template <int PREC, bool GATEUP>
 __global__ void __launch_bounds__(P2_THREADS, 1)
@@ -270,6 +343,9 @@ prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const 
   uint8_t* itiles = btiles + P2_BSTAGES * P2_BTILE;
   P2Shared* sh = (P2Shared*)(itiles + P2_ISTAGES * P2_IDX);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_rank();
+  const bool leader = rank == 0;
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
   constexpr int elem = PREC == VQ2_PREC_FP8 ? 1 : 2;
   constexpr int KE = 128 / elem;               // K elements per stage (128 bytes)
   constexpr int LOB = KE / 4;                  // lo bytes per row per stage
@@ -282,9 +358,9 @@ prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const 
   if (threadIdx.x == 0) {
     for (int s = 0; s < P2_BSTAGES; ++s) { mbar_init(&sh->full_b[s], 1); mbar_init(&sh->empty_b[s], 1); }
     for (int s = 0; s < P2_ISTAGES; ++s) { mbar_init(&sh->full_i[s], 33); mbar_init(&sh->empty_i[s], P2_DEC_WARPS); }
-    for (int s = 0; s < P2_ASTAGES; ++s) { mbar_init(&sh->full_a[s], P2_DEC_WARPS); mbar_init(&sh->empty_a[s], 1); }
+    for (int s = 0; s < P2_ASTAGES; ++s) { mbar_init(&sh->full_a[s], 2 * P2_DEC_WARPS); mbar_init(&sh->empty_a[s], 1); }
     mbar_init(&sh->done, 1);
-    mbar_init(&sh->acc_empty, P2_DEC_WARPS);
+    mbar_init(&sh->acc_empty, 2 * P2_DEC_WARPS);
     mbar_init(&sh->cbbar, 1);
     mbar_init(&sh->drain, 1);
     sh->abort = 0;
@@ -292,10 +368,10 @@ prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const 
     mbar_arrive_expect_tx(&sh->cbbar, 1024 * 8);
     bulk_g2s(B_t(0), a.cb, 1024 * 8, &sh->cbbar);     // the codebook lands in a B stage first
   }
-  if (warp == 0) {
-    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;"
+  if (warp == 0) {   // the same warp in both CTAs of the pair (a collective allocation)
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;"
                  ::"r"(smem_u32(&sh->tmem_base)), "r"(P2_TMEM_COLS) : "memory");
-    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
   }
   __syncthreads();
   if (!mbar_wait(&sh->cbbar, 0)) sh->abort = 1;
@@ -308,61 +384,66 @@ prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const 
   }
   tc_fence_before();
   __syncthreads();                                     // codebook ready, B stage 0 free again
+  cluster_sync();                                      // both CTAs' barriers initialised
   tc_fence_after();
   const uint32_t tmem = sh->tmem_base;
   volatile int* abort = &sh->abort;
 
   if (warp == 0) {
-    // ---------------- activation loader (lane 0): B stages of each item by TMA
+    // ---------------- activation loader (lane 0): this CTA's halves of the item's B stages
     if (lane == 0) {
       int gb = 0;
-      for (int w = blockIdx.x; w < nwork && !*abort; w += gridDim.x) {
+      for (int w = pair; w < nwork && !*abort; w += npairs) {
         const int4 ch = a.chunks[w / a.T];
+        const int n0 = min(ch.z, P2_NSUB), n1 = ch.z - n0;     // slots of the two accumulators
+        const int nacc = n1 > 0 ? 2 : 1;
         for (int c = 0; c < nstage; ++c, ++gb) {
           const int slot = gb % P2_BSTAGES;
           if (gb >= P2_BSTAGES && !mbar_wait(&sh->empty_b[slot], ((gb / P2_BSTAGES) - 1) & 1)) { *abort = 1; break; }
-          mbar_arrive_expect_tx(&sh->full_b[slot], P2_BTILE);
-          tma_load_2d(B_t(slot), &tm_act, c * 128, ch.y, &sh->full_b[slot]);
+          const uint32_t fb = peer_smem(&sh->full_b[slot], 0);
+          if (leader) mbar_arrive_expect_tx(&sh->full_b[slot], 2u * nacc * P2_BHALF);
+          tma_load_2d_pair(B_t(slot), &tm_act, c * 128, ch.y + (int)rank * (n0 >> 1), fb);
+          if (nacc == 2) tma_load_2d_pair(B_t(slot) + P2_BHALF, &tm_act, c * 128, ch.y + P2_NSUB + (int)rank * (n1 >> 1), fb);
         }
       }
-      // every issued load has landed before the CTA can exit
-      for (int q = max(0, gb - P2_BSTAGES); q < gb; ++q) mbar_wait(&sh->full_b[q % P2_BSTAGES], (q / P2_BSTAGES) & 1);
+      // both CTAs' loads of the last stages complete on the leader's barriers: the leader waits
+      // for them (bounded) so no copy is in flight when the pair exits
+      if (leader)
+        for (int q = max(0, gb - P2_BSTAGES); q < gb; ++q) mbar_wait_cluster(&sh->full_b[q % P2_BSTAGES], (q / P2_BSTAGES) & 1);
     }
   } else if (warp == 1) {
-    // ---------------- index loader: lo plane by TMA (two 128-row boxes), hi / scale planes by cp.async
+    // ---------------- index loader: lo plane by TMA (two 64-row boxes), hi / scale planes by cp.async
     int gi = 0;
-    for (int w = blockIdx.x; w < nwork && !*abort; w += gridDim.x) {
+    for (int w = pair; w < nwork && !*abort; w += npairs) {
       const int e = a.chunks[w / a.T].x, tile = w % a.T;
-      // this lane's rows are lane + 32 i (i < 4: tile 0, else tile 1); hi / scale row pointers
-      // are formed from one base per tile
-      const long wr0 = p2_weight_row<GATEUP>(a, e, tile, 0, lane), wr1 = p2_weight_row<GATEUP>(a, e, tile, 1, lane);
-      const uint8_t* hi_b0 = a.hi + wr0 * (nsub / 4);
-      const uint8_t* hi_b1 = a.hi + wr1 * (nsub / 4);
-      const uint8_t* sc_b0 = (const uint8_t*)(a.sc + wr0 * ngk);
-      const uint8_t* sc_b1 = (const uint8_t*)(a.sc + wr1 * ngk);
-      const long hi_step = 32L * (nsub / 4), sc_step = 32L * ngk * 2;
-      const int row0 = (int)p2_weight_row<GATEUP>(a, e, tile, 0, 0);
-      const int row1 = (int)p2_weight_row<GATEUP>(a, e, tile, 1, 0);
+      const int row0 = (int)p2_weight_row<GATEUP>(a, e, tile, rank, 0);
+      const int row1 = (int)p2_weight_row<GATEUP>(a, e, tile, rank, 64);
+      const uint8_t* hi_r[4];
+      const uint8_t* sc_r[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const long wr = p2_weight_row<GATEUP>(a, e, tile, rank, lane + 32 * i);
+        hi_r[i] = a.hi + wr * (nsub / 4);
+        sc_r[i] = (const uint8_t*)(a.sc + wr * ngk);
+      }
       for (int c = 0; c < nstage; ++c, ++gi) {
         const int slot = gi % P2_ISTAGES;
         if (gi >= P2_ISTAGES && !mbar_wait(&sh->empty_i[slot], ((gi / P2_ISTAGES) - 1) & 1)) { *abort = 1; break; }
         const uint32_t ibase = smem_u32(I_t(slot));
         if (lane == 0) {
-          mbar_arrive_expect_tx(&sh->full_i[slot], P2_NT * P2_ROWS * LOB);
+          mbar_arrive_expect_tx(&sh->full_i[slot], P2_ROWS * LOB);
           tma_load_2d(I_t(slot), &tm_lo, c * LOB, row0, &sh->full_i[slot]);
-          tma_load_2d(I_t(slot) + P2_ROWS * LOB, &tm_lo, c * LOB, row1, &sh->full_i[slot]);
+          tma_load_2d(I_t(slot) + 64 * LOB, &tm_lo, c * LOB, row1, &sh->full_i[slot]);
         }
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
+        for (int i = 0; i < 4; ++i) {
           const int R = lane + 32 * i;
-          const uint8_t* hi_r = (i < 4 ? hi_b0 : hi_b1) + (i & 3) * hi_step;
-          const uint8_t* sc_r = (i < 4 ? sc_b0 : sc_b1) + (i & 3) * sc_step;
           if (PREC == VQ2_PREC_FP8) {          // hi: 8 bytes (32 sub-vectors); scales of 2 groups
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(ibase + P2_IDX_HI + R * 8), "l"(hi_r + c * 8) : "memory");
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + P2_IDX_SC + R * 4), "l"(sc_r + c * 4) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 8;" ::"r"(ibase + P2_IDX_HI + R * 8), "l"(hi_r[i] + c * 8) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + P2_IDX_SC + R * 4), "l"(sc_r[i] + c * 4) : "memory");
           } else {                             // hi: 4 bytes (16 sub-vectors); the scale pair holding this group
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + P2_IDX_HI + R * 8), "l"(hi_r + c * 4) : "memory");
-            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + P2_IDX_SC + R * 4), "l"(sc_r + (c & ~1) * 2) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + P2_IDX_HI + R * 8), "l"(hi_r[i] + c * 4) : "memory");
+            asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(ibase + P2_IDX_SC + R * 4), "l"(sc_r[i] + (c & ~1) * 2) : "memory");
           }
         }
         asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(&sh->full_i[slot])) : "memory");
@@ -372,90 +453,98 @@ prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const 
     if (lane == 0)   // the lo-plane TMA loads of the last stages have landed
       for (int q = max(0, gi - P2_ISTAGES); q < gi; ++q) mbar_wait(&sh->full_i[q % P2_ISTAGES], (q / P2_ISTAGES) & 1);
   } else if (warp == 2) {
-    // ---------------- MMA issuer (lane 0)
-    if (lane == 0) {
+    // ---------------- MMA issuer (lane 0 of the pair's first CTA)
+    if (lane == 0 && leader) {
       int gb = 0, ga = 0, it = 0;
-      for (int w = blockIdx.x; w < nwork && !*abort; w += gridDim.x, ++it) {
+      for (int w = pair; w < nwork && !*abort; w += npairs, ++it) {
         const int ns = a.chunks[w / a.T].z;
-        const uint32_t idesc = (1u << 4) | ((uint32_t)(ns >> 3) << 17) | ((uint32_t)(P2_ROWS >> 4) << 24);
-        if (it > 0 && !mbar_wait(&sh->acc_empty, (it - 1) & 1)) { *abort = 1; break; }
+        const int n0 = min(ns, P2_NSUB), n1 = ns - n0;
+        const uint32_t id0 = (1u << 4) | ((uint32_t)(n0 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+        const uint32_t id1 = (1u << 4) | ((uint32_t)(n1 >> 3) << 17) | ((uint32_t)(256 >> 4) << 24);
+        if (it > 0 && !mbar_wait_cluster(&sh->acc_empty, (it - 1) & 1)) { *abort = 1; break; }
         tc_fence_after();
         bool ok = true;
         for (int c = 0; c < nstage; ++c, ++gb, ++ga) {
           const int bslot = gb % P2_BSTAGES, aslot = ga % P2_ASTAGES;
-          if (!mbar_wait(&sh->full_b[bslot], (gb / P2_BSTAGES) & 1) ||
-              !mbar_wait(&sh->full_a[aslot], (ga / P2_ASTAGES) & 1)) { ok = false; break; }
+          if (!mbar_wait_cluster(&sh->full_b[bslot], (gb / P2_BSTAGES) & 1) ||
+              !mbar_wait_cluster(&sh->full_a[aslot], (ga / P2_ASTAGES) & 1)) { ok = false; break; }
           tc_fence_after();
           const uint32_t bbase = smem_u32(B_t(bslot));
 #pragma unroll
-          for (int t = 0; t < P2_NT; ++t)
+          for (int ks = 0; ks < 4; ++ks)
+            umma_pair<PREC>(tmem + p2_acc_col(0), tmem + p2_a_col(aslot) + 8 * ks, umma_desc_sw128(bbase + ks * 32), id0,
+                            (c | ks) != 0);
+          if (n1 > 0) {
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks)
-              umma_tmem_a<PREC>(tmem + p2_acc_col(t), tmem + p2_a_col(aslot, t) + 8 * ks,
-                                umma_desc_sw128(bbase + ks * 32), idesc, (c | ks) != 0);
-          umma_commit(&sh->empty_b[bslot]);
-          umma_commit(&sh->empty_a[aslot]);
+              umma_pair<PREC>(tmem + p2_acc_col(1), tmem + p2_a_col(aslot) + 8 * ks,
+                              umma_desc_sw128(bbase + P2_BHALF + ks * 32), id1, (c | ks) != 0);
+          }
+          umma_commit_pair(&sh->empty_b[bslot]);
+          umma_commit_pair(&sh->empty_a[aslot]);
         }
-        umma_commit(&sh->done);       // arrives once every MMA issued so far has completed
+        umma_commit_pair(&sh->done);   // both CTAs: every MMA issued so far has completed
         if (!ok) { *abort = 1; break; }
       }
-      umma_commit(&sh->drain);        // nothing of ours still reads TMEM or shared memory after this
+      umma_commit_pair(&sh->drain);    // nothing of ours still reads TMEM or shared memory after this
       mbar_wait(&sh->drain, 0);
     }
   } else {
-    // ---------------- decoders (16 warps): warp -> TMEM lane quarter q, row tile t, K half h
+    // ---------------- decoders (16 warps): warp -> TMEM lane quarter q, K quarter kq
     // Software-pipelined by one stage: the tensor-memory store of stage c is issued, then stage
     // c + 1's index planes are read and decoded into registers, and only then is the store of
-    // stage c waited for and the stage handed to the MMA warp, so the store latency does not sit
-    // on the decode chain.
-    const int q = warp & 3, j = (warp - 3) >> 2, t = j >> 1, h = j & 1;
-    const int r = q * 32 + lane, R = t * P2_ROWS + r;
+    // stage c waited for and the stage handed to the MMA lane (the pair leader's barrier), so
+    // the store latency does not sit on the decode chain.
+    const int q = warp & 3, kq = (warp - 3) >> 2;
+    const int r = q * 32 + lane;                           // TMEM lane
+    const int R = p2_stage_row<GATEUP>(r);                 // its row of the index stage
     const uint32_t cbl = smem_u32(cbs) + (lane & (P2_CB_COPIES - 1)) * 8;
     const uint32_t tlane = (uint32_t)(q * 32) << 16;
     int gi = 0, ga = 0, it = 0;
-    // stage gi of the index ring -> 16 decoded words (this thread's row, K half), then frees the
-    // slot (after the decode consumed every lane's loads of it: the next writer is the loader's
-    // TMA / cp.async)
+    // stage gi of the index ring -> 8 decoded words (this thread's row, K quarter), then frees
+    // the slot (after the decode consumed every lane's loads of it: the next writer is the
+    // loader's TMA / cp.async)
     auto decode_stage = [&](int c, uint32_t* v) -> bool {
       const int islot = gi % P2_ISTAGES;
       if (!mbar_wait(&sh->full_i[islot], (gi / P2_ISTAGES) & 1)) return false;
       const uint32_t ip = smem_u32(I_t(islot));
-      if (PREC == VQ2_PREC_FP8) {             // one 64-group: 16 sub-vectors
-        const uint4 lo = lds128_v(ip + R * 32 + h * 16);
-        const uint32_t hw = lds32_v(ip + P2_IDX_HI + R * 8 + h * 4);
-        const uint32_t sbits = lds16_v(ip + P2_IDX_SC + R * 4 + h * 2);
-        decode16_fp8(cbl, lo, hw, (unsigned short)sbits, v);
-      } else {                                // half of a 64-group: 8 sub-vectors
-        const uint2 lo = lds64_v(ip + R * 16 + h * 8);
-        const uint32_t hw = lds16_v(ip + P2_IDX_HI + R * 8 + h * 2);
+      if (PREC == VQ2_PREC_FP8) {             // 8 sub-vectors, a quarter of the 128-element stage
+        const uint2 lo = lds64_v(ip + R * 32 + kq * 8);
+        const uint32_t hw = lds16_v(ip + P2_IDX_HI + R * 8 + kq * 2);
+        const uint32_t sbits = lds16_v(ip + P2_IDX_SC + R * 4 + (kq >> 1) * 2);
+        decode8_fp8(cbl, lo, hw, (unsigned short)sbits, v);
+      } else {                                // 4 sub-vectors, a quarter of the 64-element stage
+        const uint32_t lo = lds32_v(ip + R * 16 + kq * 4);
+        const uint32_t hw = lds8_v(ip + P2_IDX_HI + R * 8 + kq);
         const uint32_t sbits = lds16_v(ip + P2_IDX_SC + R * 4 + (c & 1) * 2);
-        decode4_f16(cbl, lo.x, hw, (unsigned short)sbits, v);
-        decode4_f16(cbl, lo.y, hw >> 8, (unsigned short)sbits, v + 8);
+        decode4_f16(cbl, lo, hw, (unsigned short)sbits, v);
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&sh->empty_i[islot]);
       ++gi;
       return true;
     };
-    for (int w = blockIdx.x; w < nwork; w += gridDim.x, ++it) {
+    const uint32_t full_a0 = peer_smem(&sh->full_a[0], 0), acc_empty0 = peer_smem(&sh->acc_empty, 0);
+    const uint32_t full_a_step = (uint32_t)((uintptr_t)&sh->full_a[1] - (uintptr_t)&sh->full_a[0]);
+    for (int w = pair; w < nwork; w += npairs, ++it) {
       const int4 ch = a.chunks[w / a.T];
       const int tile = w % a.T;
       bool ok = !*abort;
       // two register sets: a tcgen05.st reads its source registers asynchronously, so the set
       // being stored stays untouched (and is kept live) until its tcgen05.wait::st
-      uint32_t va[16], vb[16];
+      uint32_t va[8], vb[8];
       if (ok) ok = decode_stage(0, va);
       auto step = [&](int c, uint32_t* cur, uint32_t* nxt) {
         const int aslot = ga % P2_ASTAGES;
         if (ga >= P2_ASTAGES && !mbar_wait(&sh->empty_a[aslot], ((ga / P2_ASTAGES) - 1) & 1)) { ok = false; return; }
         tc_fence_after();
-        tmem_st16(tmem + tlane + p2_a_col(aslot, t) + 16 * h, cur);
+        tmem_st8(tmem + tlane + p2_a_col(aslot) + 8 * kq, cur);
         if (c + 1 < nstage && !decode_stage(c + 1, nxt)) ok = false;
         tmem_st_wait();
-        keep_live16(cur);
+        keep_live8(cur);
         tc_fence_before();
         __syncwarp();
-        if (lane == 0) mbar_arrive(&sh->full_a[aslot]);
+        if (lane == 0) mbar_arrive_remote(full_a0 + aslot * full_a_step);
         ++ga;
       };
       for (int c = 0; c < nstage && ok; c += 2) {
@@ -467,55 +556,67 @@ prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const 
       // ---------------- epilogue of the item out of TMEM (lane = weight row, column = slot)
       if (!mbar_wait(&sh->done, it & 1)) { *abort = 1; break; }
       tc_fence_after();
-      const int ncol = ch.z >> 5;                          // 32-slot column groups
+      const int n0 = min(ch.z, P2_NSUB);
+      const int ncol = ch.z >> 5;                           // 32-slot column groups over both accumulators
       if (GATEUP) {
-        for (int cg = j; cg < ncol; cg += 4) {
-          const int s0 = ch.y + cg * 32;
+        // lane 2m holds gate and lane 2m + 1 up of intermediate column m; for each column pair
+        // (k, k + 1) the even lane finishes slot k and the odd lane slot k + 1
+        const bool odd = lane & 1;
+        float* dst = a.inter + tile * P2_ROWS + rank * (P2_ROWS / 2) + (r >> 1);
+        for (int cg = kq; cg < ncol; cg += 4) {
+          const int j = cg * 32 >= n0 ? 1 : 0;
+          const int col = cg * 32 - j * P2_NSUB;             // column within accumulator j
+          const int s0 = ch.y + j * P2_NSUB + col;           // slot of that column
           const float myinv = a.inv_slot[s0 + lane];
-          float* dst = a.inter + (size_t)s0 * a.I + tile * P2_ROWS + r;
 #pragma unroll 1
-          for (int hh = 0; hh < 4; ++hh) {          // 8 columns at a time (register budget)
-            float g[8], u[8];
-            tmem_ld8(tmem + tlane + p2_acc_col(0) + cg * 32 + hh * 8, g);
-            tmem_ld8(tmem + tlane + p2_acc_col(1) + cg * 32 + hh * 8, u);
+          for (int hh = 0; hh < 2; ++hh) {
+            float v[16];
+            tmem_ld16(tmem + tlane + p2_acc_col(j) + col + hh * 16, v);
 #pragma unroll
-            for (int k = 0; k < 8; ++k) {
-              const float inv = __shfl_sync(0xffffffffu, myinv, hh * 8 + k);
-              const float gg = g[k] * inv, uu = u[k] * inv;
-              dst[(size_t)(hh * 8 + k) * a.I] = __fdividef(gg, 1.f + __expf(-gg)) * uu;
+            for (int k = 0; k < 16; k += 2) {
+              // even lane keeps column k, odd lane column k + 1; each sends the other column
+              const float send = odd ? v[k] : v[k + 1];
+              const float recv = __shfl_xor_sync(0xffffffffu, send, 1);
+              const float g = odd ? recv : v[k], u = odd ? v[k + 1] : recv;
+              const int kk = hh * 16 + k + (odd ? 1 : 0);
+              const float inv = __shfl_sync(0xffffffffu, myinv, kk);
+              const float gg = g * inv, uu = u * inv;
+              dst[(size_t)(s0 + kk) * a.I] = __fdividef(gg, 1.f + __expf(-gg)) * uu;
             }
           }
         }
       } else {
-        for (int u = j; u < P2_NT * ncol; u += 4) {
-          const int tt = u & 1, cg = u >> 1;
-          const int s = ch.y + cg * 32 + lane;
+        float* col_out = a.out + tile * (2 * P2_ROWS) + rank * P2_ROWS + r;
+        for (int cg = kq; cg < ncol; cg += 4) {
+          const int j = cg * 32 >= n0 ? 1 : 0;
+          const int col = cg * 32 - j * P2_NSUB;
+          const int s = ch.y + j * P2_NSUB + col + lane;
           const int mytok = a.val[s] ? a.st[s] : -1;
           const float myw = mytok >= 0 ? a.topk_w[(size_t)mytok * a.topk + a.ss[s]] * a.inv_slot[s] : 0.f;
-          float* col = a.out + tile * (P2_NT * P2_ROWS) + tt * P2_ROWS + r;
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {          // 16 columns at a time (register budget)
+#pragma unroll 1
+          for (int hh = 0; hh < 2; ++hh) {
             float v[16];
-            tmem_ld16(tmem + tlane + p2_acc_col(tt) + cg * 32 + hh * 16, v);
+            tmem_ld16(tmem + tlane + p2_acc_col(j) + col + hh * 16, v);
 #pragma unroll
             for (int k = 0; k < 16; ++k) {
               const int tok = __shfl_sync(0xffffffffu, mytok, hh * 16 + k);
               const float wk = __shfl_sync(0xffffffffu, myw, hh * 16 + k);
-              if (tok >= 0) atomicAdd(col + (size_t)tok * a.H, v[k] * wk);
+              if (tok >= 0) atomicAdd(col_out + (size_t)tok * a.H, v[k] * wk);   // 32 consecutive rows: one line
             }
           }
         }
       }
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&sh->acc_empty);
+      if (lane == 0) mbar_arrive_remote(acc_empty0);
     }
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync();                                      // the pair's MMAs and TMEM reads are done
   if (warp == 0) {
     tc_fence_after();
-    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P2_TMEM_COLS) : "memory");
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(P2_TMEM_COLS) : "memory");
   }
 }
 
@@ -555,11 +656,14 @@ __global__ void __launch_bounds__(1024) build_chunks_kernel(const int2* __restri
 // lane + 32 of each group), then fp8: s = 448 / max(amax, 1e-6), q = e4m3(y * s), inv = 1 / s
 // (reference quant_fp8_rows, ds4_vq2_cuda.py:11-23, applied to had_act_batch output as at
 // ds4_vq2_cuda.py:94 and :106); f16: s = the power of two with amax * s <= 2^15, q = f16(y * s).
-// Rows with valid[row] == 0 are written as zeros with inv = 0. cols <= 4096.
+// Rows with valid[row] == 0 are written as zeros with inv = 0. cols <= 4096. With `pslot`, row n
+// is a token whose quantised row (and inverse scale) is written to each of its slots
+// pslot[n * k + j] >= 0 instead of row n of `out` (the slot gather fused into the quantisation).
 template <int PREC>
 __global__ void __launch_bounds__(256) had_quant_rows_kernel(const void* __restrict__ x, int in_dt,
                                                              const uint8_t* __restrict__ valid, int cols,
-                                                             uint8_t* __restrict__ out, float* __restrict__ inv) {
+                                                             uint8_t* __restrict__ out, float* __restrict__ inv,
+                                                             const int32_t* __restrict__ pslot, int k) {
   __shared__ float red[33];
   const long row = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -606,36 +710,103 @@ __global__ void __launch_bounds__(256) had_quant_rows_kernel(const void* __restr
       s = ldexpf(1.f, max(-100, min(100, ex - 1)));
     }
   }
-  if (threadIdx.x == 0) inv[row] = 1.0f / s;
+  const float is = 1.0f / s;
+  const int ndst = pslot ? k : 1;
+  for (int jd = 0; jd < ndst; ++jd) {
+    long dst = row;
+    if (pslot) {
+      dst = pslot[row * k + jd];
+      if (dst < 0) continue;                    // pair owned by another device
+    }
+    uint8_t* orow_d = out + dst * (size_t)cols * elem;
+    if (threadIdx.x == 0) inv[dst] = is;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int g = warp + 8 * i;
-    if (g < ng) {
-      if (PREC == VQ2_PREC_FP8) {
-        orow[g * 64 + lane] = (uint8_t)__nv_cvt_float_to_fp8(va[i] * s, __NV_SATFINITE, __NV_E4M3);
-        orow[g * 64 + 32 + lane] = (uint8_t)__nv_cvt_float_to_fp8(vb[i] * s, __NV_SATFINITE, __NV_E4M3);
-      } else {
-        ((__half*)orow)[g * 64 + lane] = __float2half_rn(va[i] * s);
-        ((__half*)orow)[g * 64 + 32 + lane] = __float2half_rn(vb[i] * s);
+    for (int i = 0; i < 8; ++i) {
+      const int g = warp + 8 * i;
+      if (g < ng) {
+        if (PREC == VQ2_PREC_FP8) {
+          orow_d[g * 64 + lane] = (uint8_t)__nv_cvt_float_to_fp8(va[i] * s, __NV_SATFINITE, __NV_E4M3);
+          orow_d[g * 64 + 32 + lane] = (uint8_t)__nv_cvt_float_to_fp8(vb[i] * s, __NV_SATFINITE, __NV_E4M3);
+        } else {
+          ((__half*)orow_d)[g * 64 + lane] = __float2half_rn(va[i] * s);
+          ((__half*)orow_d)[g * 64 + 32 + lane] = __float2half_rn(vb[i] * s);
+        }
       }
     }
   }
 }
 
-// Quantised token rows into slot order (padding slots zero) with their inverse scales, so the
-// activation rows of a chunk are one contiguous 2-D TMA box.
-__global__ void __launch_bounds__(256) gather_slot_rows_kernel(const uint8_t* __restrict__ src,
-                                                              const float* __restrict__ inv_tok,
-                                                              const int32_t* __restrict__ st,
-                                                              const uint8_t* __restrict__ val, int row_bytes,
-                                                              uint8_t* __restrict__ dst, float* __restrict__ inv_slot) {
-  const long p = blockIdx.x;
-  uint4* d = (uint4*)(dst + p * (size_t)row_bytes);
-  const bool ok = val[p] != 0;
-  const int tok = ok ? st[p] : 0;
-  const uint4* s = (const uint4*)(src + (size_t)tok * row_bytes);
-  for (int i = threadIdx.x; i < row_bytes / 16; i += blockDim.x) d[i] = ok ? s[i] : make_uint4(0, 0, 0, 0);
-  if (threadIdx.x == 0) inv_slot[p] = ok ? inv_tok[tok] : 0.f;
+// Warp-per-row variant for fp32 rows of at most 2048 columns (the intermediate rows of the down
+// projection): one warp holds its whole row in registers (lane: elements lane and lane + 32 of
+// every 64-group, all loads issued together), rotates every group with the shuffle FWHT, takes
+// the row absmax with a warp reduction and writes the quantised row; same arithmetic and outputs
+// as had_quant_rows_kernel. 8 rows per 256-thread CTA.
+template <int PREC>
+__global__ void __launch_bounds__(256) had_quant_rows_warp_kernel(const float* __restrict__ x,
+                                                                  const uint8_t* __restrict__ valid, long rows,
+                                                                  int cols, uint8_t* __restrict__ out,
+                                                                  float* __restrict__ inv) {
+  constexpr int NG = 32;                          // groups per row at most (2048 columns)
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const long row = (long)blockIdx.x * 8 + warp;
+  if (row >= rows) return;
+  const int ng = cols / 64;
+  const int elem = PREC == VQ2_PREC_FP8 ? 1 : 2;
+  uint8_t* orow = out + row * (size_t)cols * elem;
+  if (!valid[row]) {
+    for (int c = lane; c < cols * elem / 4; c += 32) ((uint32_t*)orow)[c] = 0u;
+    if (lane == 0) inv[row] = 0.f;
+    return;
+  }
+  const float* xr = x + row * (size_t)cols;
+  float va[NG], vb[NG];
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    va[g] = g < ng ? __ldcs(xr + g * 64 + lane) : 0.f;       // read once: streaming loads
+    vb[g] = g < ng ? __ldcs(xr + g * 64 + 32 + lane) : 0.f;
+  }
+  float amax = 0.f;
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    float a = va[g], b = vb[g];
+    const float t = a + b;
+    b = a - b;
+    a = t;
+#pragma unroll
+    for (int len = 16; len >= 1; len >>= 1) {
+      const float pa = __shfl_xor_sync(0xffffffffu, a, len), pb = __shfl_xor_sync(0xffffffffu, b, len);
+      a = (lane & len) ? (pa - a) : (a + pa);
+      b = (lane & len) ? (pb - b) : (b + pb);
+    }
+    va[g] = a * 0.125f;
+    vb[g] = b * 0.125f;
+    amax = fmaxf(amax, fmaxf(fabsf(va[g]), fabsf(vb[g])));
+  }
+  amax = warp_max(amax);
+  float s;
+  if (PREC == VQ2_PREC_FP8) {
+    s = 448.0f / fmaxf(amax, 1e-6f);
+  } else {
+    s = 1.f;
+    if (amax > 0.f) {
+      int ex;
+      frexpf(32768.f / amax, &ex);
+      s = ldexpf(1.f, max(-100, min(100, ex - 1)));
+    }
+  }
+  if (lane == 0) inv[row] = 1.0f / s;
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    if (g < ng) {
+      if (PREC == VQ2_PREC_FP8) {
+        orow[g * 64 + lane] = (uint8_t)__nv_cvt_float_to_fp8(va[g] * s, __NV_SATFINITE, __NV_E4M3);
+        orow[g * 64 + 32 + lane] = (uint8_t)__nv_cvt_float_to_fp8(vb[g] * s, __NV_SATFINITE, __NV_E4M3);
+      } else {
+        ((__half*)orow)[g * 64 + lane] = __float2half_rn(va[g] * s);
+        ((__half*)orow)[g * 64 + 32 + lane] = __float2half_rn(vb[g] * s);
+      }
+    }
+  }
 }
 
 // ------------------------------------------------------------------ host
@@ -664,8 +835,8 @@ static int encode_2d(CUtensorMap* m, const void* base, uint64_t inner_bytes, uin
 
 struct PfLayout {
   long M, Pmax, nblk, nchunks_align;
-  size_t off_st, off_ss, off_val, off_be, off_counts, off_xq, off_invx, off_xs, off_invxs, off_inter, off_vb,
-      off_invvb, off_chunks, off_nchunks, off_ranges, total;
+  size_t off_st, off_ss, off_val, off_be, off_counts, off_xs, off_invxs, off_inter, off_vb,
+      off_invvb, off_chunks, off_nchunks, off_ranges, off_pslot, total;
 };
 
 static size_t up256(size_t v) { return (v + 255) & ~(size_t)255; }
@@ -683,8 +854,6 @@ static PfLayout pf_layout(int N, int k, int E, int H, int I, int prec) {
   L.off_val = o; o = up256(o + L.Pmax);
   L.off_be = o; o = up256(o + L.nblk * 4);
   L.off_counts = o; o = up256(o + L.nchunks_align * E * 4);
-  L.off_xq = o; o = up256(o + (size_t)N * H * elem);
-  L.off_invx = o; o = up256(o + (size_t)N * 4);
   L.off_xs = o; o = up256(o + (size_t)L.Pmax * H * elem);
   L.off_invxs = o; o = up256(o + (size_t)L.Pmax * 4);
   L.off_inter = o; o = up256(o + (size_t)L.Pmax * I * 4);
@@ -693,11 +862,13 @@ static PfLayout pf_layout(int N, int k, int E, int H, int I, int prec) {
   L.off_chunks = o; o = up256(o + (size_t)L.nblk * 16);
   L.off_nchunks = o; o = up256(o + 4);
   L.off_ranges = o; o = up256(o + (size_t)E * 8);
+  L.off_pslot = o; o = up256(o + (size_t)L.M * 4);
   L.total = o + 256;
   return L;
 }
 
 static bool g_pf_attr[64];
+static int g_pf_pairs[64];   // resident CTA pairs of the GEMM kernels, per device
 
 }  // namespace vq2
 
@@ -729,9 +900,7 @@ extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_
   uint8_t* val = w + L.off_val;
   int32_t* be = (int32_t*)(w + L.off_be);
   int* counts = (int*)(w + L.off_counts);
-  uint8_t* xq = w + L.off_xq;
   uint8_t* xs = w + L.off_xs;
-  float* invx = (float*)(w + L.off_invx);
   float* invxs = (float*)(w + L.off_invxs);
   float* inter = (float*)(w + L.off_inter);
   uint8_t* vb = w + L.off_vb;
@@ -739,6 +908,7 @@ extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_
   int4* chunks = (int4*)(w + L.off_chunks);
   int* nchunks = (int*)(w + L.off_nchunks);
   int2* ranges = (int2*)(w + L.off_ranges);
+  int32_t* pslot = (int32_t*)(w + L.off_pslot);
   cudaStream_t st_ = (cudaStream_t)stream;
 
   int dev = 0;
@@ -753,9 +923,9 @@ extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_
     g_pf_attr[dev] = true;
   }
   const int nsm = device_sm_count();
-  if (nsm <= 0) return VQ2_ERR_CUDA;
+  if (nsm < 2) return VQ2_ERR_CUDA;
   int rc = launch_align_ex(a->topk_ids, a->ids_dtype, a->N, a->topk, a->E, P2_BM, a->expert_base, 1, st, ss, val,
-                           be, counts, st_, ranges);
+                           be, counts, st_, ranges, pslot);
   if (rc) return rc;
   if (cudaMemsetAsync(a->out, 0, (size_t)a->N * a->H * sizeof(float), st_) != cudaSuccess) return VQ2_ERR_CUDA;
   build_chunks_kernel<<<1, 1024, 0, st_>>>(ranges, a->E, chunks, nchunks);
@@ -764,33 +934,65 @@ extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_
   g.chunks = chunks; g.nchunks = nchunks;
   g.st = st; g.ss = ss; g.val = val; g.topk_w = a->topk_w; g.inter = inter; g.out = a->out;
   g.I = a->I; g.H = a->H; g.topk = a->topk;
+  // Hadamard + per-token quantisation, each token row written to its slots (padding slots are
+  // left as they are: their columns of the GEMMs are never combined into the output)
   if (prec == VQ2_PREC_FP8)
-    had_quant_rows_kernel<VQ2_PREC_FP8><<<a->N, 256, 0, st_>>>(a->x, a->x_dtype, nullptr, a->H, xq, invx);
+    had_quant_rows_kernel<VQ2_PREC_FP8><<<a->N, 256, 0, st_>>>(a->x, a->x_dtype, nullptr, a->H, xs, invxs, pslot, a->topk);
   else
-    had_quant_rows_kernel<VQ2_PREC_F16><<<a->N, 256, 0, st_>>>(a->x, a->x_dtype, nullptr, a->H, xq, invx);
+    had_quant_rows_kernel<VQ2_PREC_F16><<<a->N, 256, 0, st_>>>(a->x, a->x_dtype, nullptr, a->H, xs, invxs, pslot, a->topk);
   const int elem = prec == VQ2_PREC_FP8 ? 1 : 2;
   const int lob = 128 / elem / 4;
-  gather_slot_rows_kernel<<<(unsigned)L.Pmax, 256, 0, st_>>>(xq, invx, st, val, a->H * elem, xs, invxs);
   CUtensorMap tm_x, tm_v, tm_l13, tm_l2;
-  if (encode_2d(&tm_x, xs, (uint64_t)a->H * elem, L.Pmax, 128, P2_NMAX, true) ||
-      encode_2d(&tm_v, vb, (uint64_t)a->I * elem, L.Pmax, 128, P2_NMAX, true) ||
-      encode_2d(&tm_l13, a->w13_lo, a->H / 4, (uint64_t)a->E * 2 * a->I, lob, P2_ROWS, false) ||
-      encode_2d(&tm_l2, a->w2_lo, a->I / 4, (uint64_t)a->E * a->H, lob, P2_ROWS, false))
+  if (encode_2d(&tm_x, xs, (uint64_t)a->H * elem, L.Pmax, 128, P2_NSUB / 2, true) ||
+      encode_2d(&tm_v, vb, (uint64_t)a->I * elem, L.Pmax, 128, P2_NSUB / 2, true) ||
+      encode_2d(&tm_l13, a->w13_lo, a->H / 4, (uint64_t)a->E * 2 * a->I, lob, 64, false) ||
+      encode_2d(&tm_l2, a->w2_lo, a->I / 4, (uint64_t)a->E * a->H, lob, 64, false))
     return VQ2_ERR_CUDA;
+  // CTA pairs (clusters of 2), one CTA per SM: as many pairs as can be resident at once
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)(nsm & ~1));
+  cfg.blockDim = dim3(P2_THREADS);
+  cfg.dynamicSmemBytes = P2_SMEM;
+  cfg.stream = st_;
+  cudaLaunchAttribute cattr[1];
+  cattr[0].id = cudaLaunchAttributeClusterDimension;
+  cattr[0].val.clusterDim.x = 2;
+  cattr[0].val.clusterDim.y = 1;
+  cattr[0].val.clusterDim.z = 1;
+  cfg.attrs = cattr;
+  cfg.numAttrs = 1;
+  if (!g_pf_pairs[dev]) {
+    int nc = 0;
+    if (cudaOccupancyMaxActiveClusters(&nc, (void*)prefill_gemm_kernel<VQ2_PREC_FP8, true>, &cfg) != cudaSuccess || nc < 1)
+      nc = nsm / 2;
+    g_pf_pairs[dev] = std::min(nc, nsm / 2);
+  }
+  cfg.gridDim = dim3((unsigned)(2 * g_pf_pairs[dev]));
   // gate/up: row tiles of 128 gate + 128 up rows
   g.inv_slot = invxs; g.lo = a->w13_lo; g.hi = a->w13_hi; g.sc = a->w13_sc; g.cb = a->w13_cb;
   g.K = a->H; g.R = 2 * a->I; g.T = a->I / P2_ROWS;
-  if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, true><<<nsm, P2_THREADS, P2_SMEM, st_>>>(g, tm_x, tm_l13);
-  else prefill_gemm_kernel<VQ2_PREC_F16, true><<<nsm, P2_THREADS, P2_SMEM, st_>>>(g, tm_x, tm_l13);
+  cudaError_t le = prec == VQ2_PREC_FP8 ? cudaLaunchKernelEx(&cfg, prefill_gemm_kernel<VQ2_PREC_FP8, true>, g, tm_x, tm_l13)
+                                        : cudaLaunchKernelEx(&cfg, prefill_gemm_kernel<VQ2_PREC_F16, true>, g, tm_x, tm_l13);
+  if (le != cudaSuccess) return VQ2_ERR_CUDA;
   // inter -> Hadamard -> quantised activation of the down projection
-  if (prec == VQ2_PREC_FP8)
-    had_quant_rows_kernel<VQ2_PREC_FP8><<<(unsigned)L.Pmax, 256, 0, st_>>>(inter, VQ2_DT_F32, val, a->I, vb, invvb);
-  else
-    had_quant_rows_kernel<VQ2_PREC_F16><<<(unsigned)L.Pmax, 256, 0, st_>>>(inter, VQ2_DT_F32, val, a->I, vb, invvb);
+  if (a->I <= 2048) {
+    const unsigned nb = (unsigned)((L.Pmax + 7) / 8);
+    if (prec == VQ2_PREC_FP8)
+      had_quant_rows_warp_kernel<VQ2_PREC_FP8><<<nb, 256, 0, st_>>>(inter, val, L.Pmax, a->I, vb, invvb);
+    else
+      had_quant_rows_warp_kernel<VQ2_PREC_F16><<<nb, 256, 0, st_>>>(inter, val, L.Pmax, a->I, vb, invvb);
+  } else if (prec == VQ2_PREC_FP8) {
+    had_quant_rows_kernel<VQ2_PREC_FP8><<<(unsigned)L.Pmax, 256, 0, st_>>>(inter, VQ2_DT_F32, val, a->I, vb, invvb,
+                                                                            nullptr, 1);
+  } else {
+    had_quant_rows_kernel<VQ2_PREC_F16><<<(unsigned)L.Pmax, 256, 0, st_>>>(inter, VQ2_DT_F32, val, a->I, vb, invvb,
+                                                                            nullptr, 1);
+  }
   // down + combine: row tiles of 256 output rows
   g.inv_slot = invvb; g.lo = a->w2_lo; g.hi = a->w2_hi; g.sc = a->w2_sc; g.cb = a->w2_cb;
-  g.K = a->I; g.R = a->H; g.T = a->H / (P2_NT * P2_ROWS);
-  if (prec == VQ2_PREC_FP8) prefill_gemm_kernel<VQ2_PREC_FP8, false><<<nsm, P2_THREADS, P2_SMEM, st_>>>(g, tm_v, tm_l2);
-  else prefill_gemm_kernel<VQ2_PREC_F16, false><<<nsm, P2_THREADS, P2_SMEM, st_>>>(g, tm_v, tm_l2);
+  g.K = a->I; g.R = a->H; g.T = a->H / (2 * P2_ROWS);
+  le = prec == VQ2_PREC_FP8 ? cudaLaunchKernelEx(&cfg, prefill_gemm_kernel<VQ2_PREC_FP8, false>, g, tm_v, tm_l2)
+                            : cudaLaunchKernelEx(&cfg, prefill_gemm_kernel<VQ2_PREC_F16, false>, g, tm_v, tm_l2);
+  if (le != cudaSuccess) return VQ2_ERR_CUDA;
   return cudaGetLastError() == cudaSuccess ? VQ2_OK : VQ2_ERR_CUDA;
 }
