@@ -139,6 +139,27 @@ __device__ __forceinline__ void decode16_fp8(uint32_t cbl, uint4 lo, uint32_t hw
   decode8_fp8(cbl, make_uint2(lo.z, lo.w), hw >> 16, sb, v + 8);
 }
 
+// fp8 from an fp32 codebook (entries 128 bytes apart: 8 copies of 16 bytes, lane l reads copy
+// l mod 8, so each 8-lane phase of a warp's 16-byte gathers is conflict-free): one gather gives
+// the four fp32 values, two packed multiplies give the exact products, then e4m3 as above.
+__device__ __forceinline__ void decode8_fp8_f32cb(uint32_t cbl, uint2 lo, uint32_t hw, float scf, uint32_t* v) {
+  const float2 s2 = make_float2(scf, scf);
+#pragma unroll
+  for (int q = 0; q < 2; ++q) {
+    uint32_t ids[2];
+    unpack_ids4(q ? lo.y : lo.x, (hw >> (8 * q)) & 0xFFu, ids[0], ids[1]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t id = (j & 2) ? (ids[j & 1] >> 16) : (ids[j & 1] & 0xFFFFu);
+      float4 c;
+      asm("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(c.x), "=f"(c.y), "=f"(c.z), "=f"(c.w) : "r"(cbl + (id << 7)));
+      const __nv_fp8x2_storage_t p0 = __nv_cvt_float2_to_fp8x2(fmul2(make_float2(c.x, c.y), s2), __NV_SATFINITE, __NV_E4M3);
+      const __nv_fp8x2_storage_t p1 = __nv_cvt_float2_to_fp8x2(fmul2(make_float2(c.z, c.w), s2), __NV_SATFINITE, __NV_E4M3);
+      v[4 * q + j] = (uint32_t)p0 | ((uint32_t)p1 << 16);
+    }
+  }
+}
+
 // f16: 4 sub-vectors of a row (lo: 4 low index bytes, hw: 1 hi byte) -> 8 words of 2 f16 values,
 // C[id] * sc in fp16.
 __device__ __forceinline__ void decode4_f16(uint32_t cbl, uint32_t lo, uint32_t hw, unsigned short sb, uint32_t* v) {
@@ -375,7 +396,14 @@ prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const 
   }
   __syncthreads();
   if (!mbar_wait(&sh->cbbar, 0)) sh->abort = 1;
-  {  // replicate: entry e of copy c at e * 128 + c * 8; consecutive 16-byte stores
+  if (PREC == VQ2_PREC_FP8) {  // fp32 entries: entry e of copy c at e * 128 + c * 16
+    const uint2* src = (const uint2*)B_t(0);
+    for (int idx = threadIdx.x; idx < 1024 * 8; idx += blockDim.x) {
+      const uint2 v = src[idx >> 3];
+      const float2 a = __half22float2(*(const __half2*)&v.x), b = __half22float2(*(const __half2*)&v.y);
+      *(float4*)(cbs + idx * 16) = make_float4(a.x, a.y, b.x, b.y);
+    }
+  } else {  // fp16 entries: entry e of copy c at e * 128 + c * 8; consecutive 16-byte stores
     const uint2* src = (const uint2*)B_t(0);
     for (int idx = threadIdx.x; idx < 1024 * (P2_CB_COPIES / 2); idx += blockDim.x) {
       const uint2 v = src[idx / (P2_CB_COPIES / 2)];
@@ -498,7 +526,8 @@ prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const 
     const int q = warp & 3, kq = (warp - 3) >> 2;
     const int r = q * 32 + lane;                           // TMEM lane
     const int R = p2_stage_row<GATEUP>(r);                 // its row of the index stage
-    const uint32_t cbl = smem_u32(cbs) + (lane & (P2_CB_COPIES - 1)) * 8;
+    const uint32_t cbl = PREC == VQ2_PREC_FP8 ? smem_u32(cbs) + (lane & 7) * 16      // fp32 codebook: 8 copies
+                                              : smem_u32(cbs) + (lane & (P2_CB_COPIES - 1)) * 8;
     const uint32_t tlane = (uint32_t)(q * 32) << 16;
     int gi = 0, ga = 0, it = 0;
     // stage gi of the index ring -> 8 decoded words (this thread's row, K quarter), then frees
@@ -512,7 +541,7 @@ prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const 
         const uint2 lo = lds64_v(ip + R * 32 + kq * 8);
         const uint32_t hw = lds16_v(ip + P2_IDX_HI + R * 8 + kq * 2);
         const uint32_t sbits = lds16_v(ip + P2_IDX_SC + R * 4 + (kq >> 1) * 2);
-        decode8_fp8(cbl, lo, hw, (unsigned short)sbits, v);
+        decode8_fp8_f32cb(cbl, lo, hw, __half2float(__ushort_as_half((unsigned short)sbits)), v);
       } else {                                // 4 sub-vectors, a quarter of the 64-element stage
         const uint32_t lo = lds32_v(ip + R * 16 + kq * 4);
         const uint32_t hw = lds8_v(ip + P2_IDX_HI + R * 8 + kq);
