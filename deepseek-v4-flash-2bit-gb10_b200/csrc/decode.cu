@@ -146,6 +146,84 @@ __device__ __forceinline__ void consumer_sync() {
   asm volatile("bar.sync 1, %0;" ::"r"(DEC_NW * 32) : "memory");
 }
 
+// ------------------------------------------------------------------ fused expert-parallel exchange
+// With `world` > 0 the two kernels also carry the decode step's token exchange between the ranks of
+// an expert-parallel group (one exchange region per rank, mapped by every peer; field pointers per
+// rank in `peers`, EP_FIELDS each): the gate/up kernel pushes this rank's rows, ids (as i32) and
+// weights into slot `rank` of every rank's region and waits (bounded) until every rank's have
+// arrived, and the kernels then run on the gathered rows (world x N tokens, this rank's experts);
+// the down kernel adds its results with fp32 atomics straight into the owning rank's COMB rows over
+// NVLink, and its last CTA releases a completion flag to every rank. ep_finish_kernel waits for all
+// ranks' flags, copies COMB out and re-zeroes it. Steps are numbered by EPOCH in the region.
+struct DecEp {
+  const uint64_t* peers;    // [world][EP_FIELDS] field addresses of every rank's region
+  int world, rank, N;       // N: tokens per rank
+  int row_x, ids_i64, k;
+  const uint8_t* x_local;   // this rank's N rows, ids and weights
+  const void* ids_local;
+  const float* w_local;
+  const unsigned* dflag;    // this rank's DFLAG [world][VQ2_EP_CTAS] and step counter
+  const unsigned* epoch;
+  unsigned* count;          // this rank's completion counter (the down kernel's CTAs)
+};
+
+// Step number of the current call (EPOCH is advanced by the finish kernel of the previous step).
+__device__ __forceinline__ unsigned ep_step(const DecEp& ep) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(ep.epoch) : "memory");
+  return v + 1;
+}
+
+// Every thread: wait until all world x C dispatch flags here reached `step`, then a CTA barrier.
+__device__ __forceinline__ void ep_wait_dispatch(const DecEp& ep, unsigned step) {
+  const int C = ep_slices((size_t)ep.N * ep.row_x);
+  for (int f = threadIdx.x; f < ep.world * C; f += blockDim.x) ep_wait_flag(ep.dflag + f, step);
+  __syncthreads();
+}
+
+// All threads of every CTA: the (destination, slice) items b = blockIdx.x, + gridDim.x, ...: push
+// slice c of this rank's rows, ids and weights into slot `rank` of destination p's region and
+// release flag [rank][c] there; then wait for every rank's slices here.
+__device__ __forceinline__ void ep_dispatch_and_wait(const DecEp& ep, unsigned step) {
+  const int C = ep_slices((size_t)ep.N * ep.row_x);
+  const size_t xb = (size_t)ep.N * ep.row_x, ib = (size_t)ep.N * ep.k * 4;
+  for (int b = blockIdx.x; b < ep.world * C; b += gridDim.x) {
+    const int p = b / C, c = b % C;
+    size_t xb0, xb1, ib0, ib1;
+    ep_slice(xb, c, C, 16, xb0, xb1);
+    ep_slice(ib, c, C, 4, ib0, ib1);
+    const uint64_t* t = ep.peers + p * EP_FIELDS;
+    uint8_t* dx = (uint8_t*)t[EP_X] + ep.rank * xb;
+    for (size_t i = xb0 / 16 + threadIdx.x; i < xb1 / 16; i += blockDim.x)
+      ((uint4*)dx)[i] = ((const uint4*)ep.x_local)[i];
+    int32_t* di = (int32_t*)((uint8_t*)t[EP_IDS] + ep.rank * ib);
+    float* dw = (float*)((uint8_t*)t[EP_WT] + ep.rank * ib);
+    for (size_t i = ib0 / 4 + threadIdx.x; i < ib1 / 4; i += blockDim.x) {
+      di[i] = ep.ids_i64 ? (int32_t)((const long long*)ep.ids_local)[i] : ((const int32_t*)ep.ids_local)[i];
+      dw[i] = ep.w_local[i];
+    }
+    __syncthreads();                     // every thread's stores precede the release below
+    if (threadIdx.x == 0) st_release_sys((unsigned*)t[EP_DFLAG] + ep.rank * C + c, step);
+  }
+  ep_wait_dispatch(ep, step);
+}
+
+// Consumer threads, after the down phase: the CTA's atomics are complete; the CTA that completes
+// the count releases this rank's completion flag [rank] at every rank.
+__device__ __forceinline__ void ep_release_done(const DecEp& ep, unsigned step) {
+  consumer_sync();
+  if (threadIdx.x == 0) {
+    __threadfence_system();
+    unsigned prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ep.count) : "memory");
+    if (prev == gridDim.x - 1) {
+      *ep.count = 0;
+      for (int p = 0; p < ep.world; ++p)
+        st_release_sys((unsigned*)ep.peers[p * EP_FIELDS + EP_CFLAG] + ep.rank, step);
+    }
+  }
+}
+
 // Consumers replicate the codebook (landed in sh->cbstage by one bulk copy) 16x — entry e of
 // copy c at byte e*128 + c*8 — and record max |C| into sh->cmax. Ends with a consumer barrier.
 __device__ __forceinline__ void fill_codebook(uint8_t* cbs, DecodeShared* sh) {
@@ -409,7 +487,7 @@ __device__ __forceinline__ void gateup_rows(const uint8_t* st, int rr0, int rste
 template <int R>
 __device__ __forceinline__ void down_rows(const uint8_t* st, int rr0, int rstep, int n, int g, bool gv, int nsub,
                                           int ng, uint32_t lo_b, uint32_t hi_b, const uint8_t* cbl,
-                                          const uint32_t (*xr)[32], float wsc, int tok, int H, int h0, float* out) {
+                                          const uint32_t (*xr)[32], float wsc, int h0, float* orow) {
   uint4 lo[R];
   uint32_t hw[R];
   float sc[R];
@@ -433,7 +511,7 @@ __device__ __forceinline__ void down_rows(const uint8_t* st, int rr0, int rstep,
   const int lane = threadIdx.x & 31;
   const int r = reduce_index<R>(lane);
   const int rr = rr0 + r * rstep;
-  if ((lane & (32 / R - 1)) == 0 && rr < n) atomicAdd(&out[(size_t)tok * H + h0 + rr], tot);
+  if ((lane & (32 / R - 1)) == 0 && rr < n) atomicAdd(&orow[h0 + rr], tot);
 }
 
 // ------------------------------------------------------------------ phases
@@ -502,7 +580,7 @@ struct GateupPre {
   float va[STAGE_GPW], vb[STAGE_GPW];
   int m = -1;
 };
-__device__ __forceinline__ void gateup_pre(const vq2_moe_args& a, const DecSmem& d, GateupPre& pre) {
+__device__ __forceinline__ void gateup_pre(const vq2_moe_args& a, const DecSmem& d, GateupPre& pre, bool zero_out) {
   DecodeShared* sh = d.sh;
   const ChunkIter it0((long)sh->nunits * a.I, a.I, DEC_SA);
   if (it0.left > 0) {
@@ -512,6 +590,7 @@ __device__ __forceinline__ void gateup_pre(const vq2_moe_args& a, const DecSmem&
     const int xdt = a.x_dtype;
     stage_load([&](int i) { return load_act(xp, xdt, xrow + i); }, a.H / 64, pre.va, pre.vb);
   }
+  if (!zero_out) return;
   const long tot = (long)a.N * a.H;
   for (long i = (long)blockIdx.x * DEC_NW * 32 + threadIdx.x; i < tot; i += (long)gridDim.x * DEC_NW * 32)
     a.out[i] = 0.f;
@@ -578,7 +657,7 @@ __device__ __forceinline__ void gateup_consume(const vq2_moe_args& a, const DecS
 // d.cbs and every CTA's gate/up partials visible.
 template <int KH>
 __device__ __forceinline__ void down_consume(const vq2_moe_args& a, const DecSmem& d, const float* __restrict__ part,
-                                             int khA, int& c) {
+                                             int khA, const DecEp& ep, int& c) {
   DecodeShared* sh = d.sh;
   const int H = a.H, I = a.I, nsub = I / 4, ng = I / 64;
   constexpr int S = down_rows_per_stage(KH);
@@ -590,7 +669,8 @@ __device__ __forceinline__ void down_consume(const vq2_moe_args& a, const DecSme
   const uint8_t* cbl = d.cbs + (lane & (CB_COPIES - 1)) * 8;
   uint32_t xr[1][32];
   float wsc = 0.f;
-  int tok = -1, ucur = -1;
+  float* orow = nullptr;
+  int ucur = -1;
   ChunkIter it((long)sh->nunits * H, H, S);
   // Units of this CTA's row range: when all of their activations fit the staging buffer they are
   // staged together before the loop (a range that crosses a unit boundary then pays one staging).
@@ -629,7 +709,10 @@ __device__ __forceinline__ void down_consume(const vq2_moe_args& a, const DecSme
     if (u != ucur) {
       ucur = u;
       const int m = sh->unit_m[u][0];
-      tok = m / a.topk;
+      const int tok = m / a.topk;
+      // the token's output row: here, or (expert parallelism) in its owner's COMB over NVLink
+      orow = ep.world > 0 ? (float*)ep.peers[(tok / ep.N) * EP_FIELDS + EP_COMB] + (size_t)(tok % ep.N) * H
+                          : a.out + (size_t)tok * H;
       int gi = g;                      // this lane's group in the staging buffer
       if (all_at_once) gi += (u - ub) * ng;
       else stage_units(u - ub, 1);
@@ -640,16 +723,16 @@ __device__ __forceinline__ void down_consume(const vq2_moe_args& a, const DecSme
     const uint8_t* st = d.stages + slot * DEC_STAGE_BYTES;
     if (S / rstep >= 8) {
       for (int rr0 = rsub; rr0 < n; rr0 += 8 * rstep)
-        down_rows<8>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, tok, H, h0, a.out);
+        down_rows<8>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, h0, orow);
     } else if (S / rstep >= 4) {
       for (int rr0 = rsub; rr0 < n; rr0 += 4 * rstep)
-        down_rows<4>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, tok, H, h0, a.out);
+        down_rows<4>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, h0, orow);
     } else {
       for (int rr0 = rsub; rr0 < n; rr0 += 2 * rstep) {
         if (rr0 + rstep < n)     // both rows of the pass exist
-          down_rows<2>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, tok, H, h0, a.out);
+          down_rows<2>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, h0, orow);
         else                     // ragged end of a chunk: one row
-          down_rows<1>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, tok, H, h0, a.out);
+          down_rows<1>(st, rr0, rstep, n, g, gv, nsub, ng, lo_b, hi_b, cbl, xr, wsc, h0, orow);
       }
     }
     __syncwarp();
@@ -661,7 +744,7 @@ __device__ __forceinline__ void down_consume(const vq2_moe_args& a, const DecSme
 // ------------------------------------------------------------------ kernel A: gate/up partials
 template <int KH>
 __global__ void __launch_bounds__(DEC_THREADS, 1)
-decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
+decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part, DecEp ep) {
   extern __shared__ __align__(128) uint8_t smem[];
   const DecSmem d = dec_smem(smem);
   // Launched with programmatic dependent launch: the CTA becomes resident and issues the
@@ -671,6 +754,8 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
   // it then no longer hides the activation loads below.)
   dec_init(a.w13_cb, d);
   pdl_wait();
+  // expert parallelism: gather every rank's rows, ids and weights first (the plan reads them)
+  if (ep.world > 0) ep_dispatch_and_wait(ep, ep_step(ep));
   // dependents (the down kernel) may launch now: everything this grid waited for is complete
   pdl_launch_dependents();
   build_plan(a.topk_ids, a.ids_dtype, a.topk_w, a.N * a.topk, a.E, a.expert_base, d.sh);
@@ -683,7 +768,7 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
     return;
   }
   GateupPre pre;
-  gateup_pre(a, d, pre);
+  gateup_pre(a, d, pre, ep.world == 0);
   fill_codebook(d.cbs, d.sh);         // overlaps the activation loads of gateup_pre
   gateup_consume<KH>(a, d, part, pre, c);
 }
@@ -691,12 +776,16 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part) {
 // ------------------------------------------------------------------ kernel B: down + combine
 template <int KH>
 __global__ void __launch_bounds__(DEC_THREADS, 1)
-decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
+decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA, DecEp ep) {
   extern __shared__ __align__(128) uint8_t smem[];
   const DecSmem d = dec_smem(smem);
   // the next call's gate/up kernel may launch now: before its own grid-dependency wait it only
   // initialises barriers and copies its codebook into its shared memory
   pdl_launch_dependents();
+  // expert parallelism: the gathered ids the plan reads were written by the peers (their arrival
+  // flags are set by now; the acquire makes the data visible to this CTA)
+  const unsigned step = ep.world > 0 ? ep_step(ep) : 0u;
+  if (ep.world > 0) ep_wait_dispatch(ep, step);
   dec_prologue(a, a.w2_cb, d);
   int c = 0;
   if (threadIdx.x >> 5 == DEC_NW) {   // producer warp: the weights do not depend on the gate/up grid
@@ -708,7 +797,34 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA) {
   }
   fill_codebook(d.cbs, d.sh);
   pdl_wait();   // the gate/up partials and the zeroed output come from the previous grid
-  down_consume<KH>(a, d, part, khA, c);
+  down_consume<KH>(a, d, part, khA, ep, c);
+  if (ep.world > 0) ep_release_done(ep, step);
+}
+
+// ------------------------------------------------------------------ expert parallelism: finish
+// Waits for every rank's completion flag of this step, copies this rank's COMB rows ([N][H] fp32,
+// summed by all ranks' atomics) to `out` and re-zeroes them; the CTA that completes the count
+// advances EPOCH. Runs in stream order after the down kernel.
+__global__ void __launch_bounds__(512) ep_finish_kernel(float* comb, const unsigned* cflag, int world,
+                                                        unsigned* epoch, unsigned* count, int n4,
+                                                        float* __restrict__ out) {
+  const unsigned step = *epoch + 1;
+  for (int f = threadIdx.x; f < world; f += blockDim.x) ep_wait_flag(cflag + f, step);
+  __syncthreads();
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
+    ((float4*)out)[i] = __ldcg((const float4*)comb + i);
+    ((float4*)comb)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  __threadfence_system();                // the zeros precede the next step's dispatch release
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned prev;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(count) : "memory");
+    if (prev == gridDim.x - 1) {
+      *count = 0;
+      *epoch = step;
+    }
+  }
 }
 
 static size_t decode_smem_bytes(size_t stage_bytes) {
@@ -734,7 +850,8 @@ extern "C" size_t vq2_decode_workspace_size(int N, int topk, int H, int I) {
   return (size_t)N * topk * khA_of(H) * 2 * I * sizeof(float) + 256;
 }
 
-extern "C" int vq2_decode(const vq2_moe_args* a, void* ws, size_t ws_bytes, void* stream) {
+// Validation and the two launches; `ep` (world 0: none) selects the fused expert-parallel exchange.
+static int decode_launch(const vq2_moe_args* a, void* ws, size_t ws_bytes, void* stream, const DecEp& ep) {
   if (!a || !a->x || !a->topk_ids || !a->topk_w || !a->out || !a->w13_cb || !a->w13_lo || !a->w13_hi ||
       !a->w13_sc || !a->w2_cb || !a->w2_lo || !a->w2_hi || !a->w2_sc)
     return VQ2_ERR_NULL;
@@ -770,8 +887,8 @@ extern "C" int vq2_decode(const vq2_moe_args* a, void* ws, size_t ws_bytes, void
   cfg.blockDim = dim3(DEC_THREADS);
   cfg.dynamicSmemBytes = sm;
   cfg.stream = (cudaStream_t)stream;
-  void (*ka)(vq2_moe_args, float*) = khA == 1 ? decode_gateup_kernel<1> : decode_gateup_kernel<2>;
-  void (*kb)(vq2_moe_args, const float*, int) = khB == 1 ? decode_down_kernel<1> : decode_down_kernel<2>;
+  void (*ka)(vq2_moe_args, float*, DecEp) = khA == 1 ? decode_gateup_kernel<1> : decode_gateup_kernel<2>;
+  void (*kb)(vq2_moe_args, const float*, int, DecEp) = khB == 1 ? decode_down_kernel<1> : decode_down_kernel<2>;
   // both kernels use programmatic dependent launch (each waits for its predecessor with
   // griddepcontrol.wait before touching anything the predecessor may produce or still read)
   cudaLaunchAttribute attr[1];
@@ -779,9 +896,68 @@ extern "C" int vq2_decode(const vq2_moe_args* a, void* ws, size_t ws_bytes, void
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, ka, args, part) != cudaSuccess) return VQ2_ERR_CUDA;
-  if (cudaLaunchKernelEx(&cfg, kb, args, (const float*)part, khA) != cudaSuccess) return VQ2_ERR_CUDA;
+  if (cudaLaunchKernelEx(&cfg, ka, args, part, ep) != cudaSuccess) return VQ2_ERR_CUDA;
+  if (cudaLaunchKernelEx(&cfg, kb, args, (const float*)part, khA, ep) != cudaSuccess) return VQ2_ERR_CUDA;
   return VQ2_OK;
+}
+
+extern "C" int vq2_decode(const vq2_moe_args* a, void* ws, size_t ws_bytes, void* stream) {
+  return decode_launch(a, ws, ws_bytes, stream, DecEp{});
+}
+
+// ------------------------------------------------------------------ expert-parallel decode step
+extern "C" size_t vq2_ep_decode_workspace_size(int world, int N, int topk, int H, int I) {
+  return vq2_decode_workspace_size(world * N, topk, H, I);
+}
+
+extern "C" int vq2_ep_decode(const vq2_moe_args* a, const uint64_t* peers, int world, int rank, void* my_region,
+                             const vq2_ep_layout* lay, void* ws, size_t ws_bytes, void* stream) {
+  if (!a || !peers || !my_region || !lay || !a->x || !a->topk_ids || !a->topk_w || !a->out) return VQ2_ERR_NULL;
+  if (world < 1 || world > 64 || rank < 0 || rank >= world || a->N <= 0 || a->topk <= 0) return VQ2_ERR_SHAPE;
+  if ((long)world * a->N * a->topk > VQ2_DECODE_MAX_PAIRS) return VQ2_ERR_TOO_MANY_PAIRS;
+  if (a->x_dtype < 0 || a->x_dtype > 2 || a->ids_dtype < 0 || a->ids_dtype > 1) return VQ2_ERR_DTYPE;
+  const size_t offs[] = {lay->off_x, lay->off_ids, lay->off_w, lay->off_comb, lay->off_dflag, lay->off_cflag,
+                         lay->off_epoch, lay->off_count};
+  for (size_t o : offs)
+    if (o & 15) return VQ2_ERR_ALIGN;
+  if (!aligned16(a->x) || !aligned16(a->out) || ((uintptr_t)a->topk_ids & 3) || ((uintptr_t)a->topk_w & 3))
+    return VQ2_ERR_ALIGN;
+  uint8_t* r = (uint8_t*)my_region;
+  const int row_x = a->H * (a->x_dtype == VQ2_DT_F32 ? 4 : 2);
+  DecEp ep = {};
+  ep.peers = peers;
+  ep.world = world;
+  ep.rank = rank;
+  ep.N = a->N;
+  ep.row_x = row_x;
+  ep.ids_i64 = a->ids_dtype == VQ2_ID_I64;
+  ep.k = a->topk;
+  ep.x_local = (const uint8_t*)a->x;
+  ep.ids_local = a->topk_ids;
+  ep.w_local = a->topk_w;
+  ep.dflag = (const unsigned*)(r + lay->off_dflag);
+  ep.epoch = (const unsigned*)(r + lay->off_epoch);
+  ep.count = (unsigned*)(r + lay->off_count);
+  // the kernels run on the gathered rows of all ranks (region fields, i32 ids)
+  vq2_moe_args g = *a;
+  g.N = world * a->N;
+  g.x = r + lay->off_x;
+  g.topk_ids = r + lay->off_ids;
+  g.ids_dtype = VQ2_ID_I32;
+  g.topk_w = (const float*)(r + lay->off_w);
+  g.out = (float*)(r + lay->off_comb);   // not written: results go to the owners' COMB rows
+  int rc = decode_launch(&g, ws, ws_bytes, stream, ep);
+  if (rc) return rc;
+  const int n4 = a->N * a->H / 4;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const int nsm = g_dec_cache[dev].nsm > 0 ? g_dec_cache[dev].nsm : 148;
+  const int grid = min(nsm, max(1, (n4 + 511) / 512));
+  ep_finish_kernel<<<grid, 512, 0, (cudaStream_t)stream>>>((float*)(r + lay->off_comb),
+                                                          (const unsigned*)(r + lay->off_cflag), world,
+                                                          (unsigned*)(r + lay->off_epoch),
+                                                          (unsigned*)(r + lay->off_count) + 1, n4, a->out);
+  return cudaGetLastError() == cudaSuccess ? VQ2_OK : VQ2_ERR_CUDA;
 }
 // ------------------------------------------------------------------ decode from host buffers
 // One call per decode step for a caller whose inputs and result live in host memory: the three

@@ -25,31 +25,6 @@
 namespace vq2 {
 
 
-// Ordering: every thread of the CTA stores its share of the data, the CTA barrier orders those
-// stores before the signalling thread's next operations, and the signalling thread's release
-// store at system scope (a fence.acq_rel.sys plus the store) makes everything ordered before it
-// visible to a peer thread whose acquire load reads the flag (causality is transitive through
-// the barrier). No separate sequentially-consistent fence is needed (measured: it cost ~2 us
-// per handshake).
-__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-// Bounded wait until the flag has reached step `ep` (wrap-safe comparison).
-__device__ __forceinline__ bool ep_wait_flag(const unsigned* f, unsigned ep) {
-  for (uint32_t i = 0; i < VQ2_WAIT_LIMIT; ++i) {
-    if ((int)(ld_acquire_sys(f) - ep) >= 0) return true;
-    __nanosleep(32);
-  }
-  set_status(VQ2_ERR_TIMEOUT);
-  return false;
-}
-
 // CTA-wide copy of `bytes` (a multiple of 16, both ends 16-byte aligned) to peer memory.
 __device__ __forceinline__ void ep_copy16(uint8_t* dst, const uint8_t* src, size_t bytes) {
   const size_t n = bytes / 16;
@@ -59,22 +34,6 @@ __device__ __forceinline__ void ep_copy16(uint8_t* dst, const uint8_t* src, size
 __device__ __forceinline__ void ep_copy4(uint8_t* dst, const uint8_t* src, size_t bytes) {
   const size_t n = bytes / 4;
   for (size_t i = threadIdx.x; i < n; i += blockDim.x) ((uint32_t*)dst)[i] = ((const uint32_t*)src)[i];
-}
-
-enum { EP_X = 0, EP_IDS = 1, EP_WT = 2, EP_COMB = 3, EP_DFLAG = 4, EP_CFLAG = 5, EP_FIELDS = 6 };
-
-// Slice [c * chunk, (c + 1) * chunk) of `bytes`, chunk a multiple of `align` (16 or 4).
-__device__ __forceinline__ void ep_slice(size_t bytes, int c, int C, size_t align, size_t& b, size_t& e) {
-  const size_t chunk = ((bytes + C - 1) / C + align - 1) / align * align;
-  b = min(bytes, (size_t)c * chunk);
-  e = min(bytes, b + chunk);
-}
-
-// Slices per destination: about one per 32 KB pushed, 1..VQ2_EP_CTAS. Every rank derives the same
-// count from the same N, so senders and receivers agree on the number of flags.
-__host__ __device__ __forceinline__ int ep_slices(size_t bytes_per_dest) {
-  const size_t s = (bytes_per_dest + 32767) / 32768;
-  return s < 1 ? 1 : (s > VQ2_EP_CTAS ? VQ2_EP_CTAS : (int)s);
 }
 
 // grid: C = ep_slices(N * row_x) CTAs. CTA c pushes slice c of this rank's rows, ids (narrowed to

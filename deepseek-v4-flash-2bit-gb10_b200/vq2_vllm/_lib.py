@@ -31,6 +31,12 @@ class Vq2MoeArgs(ctypes.Structure):
                 ("w2_sc", ctypes.c_void_p), ("out", ctypes.c_void_p)]
 
 
+
+class Vq2EpLayout(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_size_t) for n in ("off_x", "off_ids", "off_w", "off_comb", "off_dflag", "off_cflag",
+                                               "off_epoch", "off_count")]
+
+
 _SIGS = {
     "vq2_decode_workspace_size": (ctypes.c_size_t, [ctypes.c_int] * 4),
     "vq2_decode": (ctypes.c_int, [ctypes.POINTER(Vq2MoeArgs), ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
@@ -64,6 +70,10 @@ _SIGS = {
     "vq2_ep_combine": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_int,
                                       ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_size_t, ctypes.c_size_t,
                                       ctypes.c_void_p, ctypes.c_void_p]),
+    "vq2_ep_decode_workspace_size": (ctypes.c_size_t, [ctypes.c_int] * 5),
+    "vq2_ep_decode": (ctypes.c_int, [ctypes.POINTER(Vq2MoeArgs), ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
+                                     ctypes.c_void_p, ctypes.POINTER(Vq2EpLayout), ctypes.c_void_p, ctypes.c_size_t,
+                                     ctypes.c_void_p]),
     "vq2_router_workspace_size": (ctypes.c_size_t, [ctypes.c_int] * 3),
     "vq2_router_topk": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_int,
                                        ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,

@@ -158,6 +158,7 @@ class P2PExchange:
         lay = self.layout(W, n_max, H, k, self.row_x)
         self.off_x, self.off_ids, self.off_w, self.off_comb = lay["x"], lay["ids"], lay["w"], lay["comb"]
         self.off_dflag, self.off_cflag, self.off_epoch = lay["dflag"], lay["cflag"], lay["epoch"]
+        self.off_count = lay["count"]
         self.nbytes = lay["bytes"]
         dev = torch.device("cuda", torch.cuda.current_device())
         p = ctypes.c_void_p()
@@ -199,7 +200,7 @@ class P2PExchange:
         256-byte aligned, and the region size."""
         sizes = (("x", world * n_max * row_x), ("ids", world * n_max * k * 4), ("w", world * n_max * k * 4),
                  ("comb", world * n_max * H * 4), ("dflag", world * EP_CTAS * 4), ("cflag", world * EP_CTAS * 4),
-                 ("epoch", 4))
+                 ("epoch", 16), ("count", 16))
         out, o = {}, 0
         for name, size in sizes:
             out[name] = o
@@ -243,6 +244,34 @@ class P2PExchange:
             self.off_cflag, self.off_epoch, out.data_ptr(), self._lib.stream_ptr()), "vq2_ep_combine")
         return out
 
+    def decode(self, x, topk_ids, topk_w, local: dict, E: int):
+        """One decode step with the exchange fused into the decode kernels (vq2_ep_decode): this
+        rank's rows go to every rank, this rank's experts (``local``, experts
+        [rank*E/W, (rank+1)*E/W) of an E-expert layer) run on all ranks' rows, and every result
+        is added into its owner's output over NVLink. Returns fp32 [N, H] for this rank's tokens."""
+        from . import synth
+        from .kernels.vq2_kernel import _prep
+        L = self._lib.lib()
+        N, k = x.shape[0], topk_ids.shape[1]
+        if N > self.n_max or x.dtype != self.x_dtype or x.shape[1] != self.H or k != self.k:
+            raise ValueError("vq2 ep: step does not fit the exchange region")
+        if E % self.world:
+            raise ValueError(f"vq2 ep: {E} experts do not split evenly over {self.world} ranks")
+        per = E // self.world
+        t = _prep(x, topk_ids, topk_w, *synth.layer_args(local))
+        t[0] = self._aligned(t[0])
+        out = torch.empty(N, self.H, dtype=torch.float32, device=x.device)
+        a = self._lib.moe_args(*t, out, expert_base=self.rank * per, E=per)
+        if not hasattr(self, "_lay"):
+            self._lay = self._lib.Vq2EpLayout(self.off_x, self.off_ids, self.off_w, self.off_comb, self.off_dflag,
+                                              self.off_cflag, self.off_epoch, self.off_count)
+        stream = self._lib.stream_ptr()
+        nb = L.vq2_ep_decode_workspace_size(self.world, N, k, a.H, a.I)
+        ws = self._lib.workspace(nb, x.device, stream)
+        self._lib.check(L.vq2_ep_decode(a, self.peers.data_ptr(), self.world, self.rank, self.base, self._lay,
+                                        ws.data_ptr(), ws.numel(), stream), "vq2_ep_decode")
+        return out
+
     def close(self):
         torch.cuda.synchronize()
         L = self._lib.lib()
@@ -266,6 +295,11 @@ def ep_moe_p2p(x, topk_ids, topk_w, expert_fn, E: int, exch: P2PExchange):
     xa, ia, wa = exch.dispatch(x, topk_ids, topk_w)
     part = expert_fn(xa, ia, wa, rank * per, per)
     return exch.combine(part, N)
+
+
+def ep_moe_p2p_fused(x, topk_ids, topk_w, local: dict, E: int, exch: P2PExchange):
+    """ep_moe_p2p with the exchange inside the decode kernels (P2PExchange.decode)."""
+    return exch.decode(x, topk_ids, topk_w, local, E)
 
 
 def local_layer(layer: dict, rank: int, world: int) -> dict:
@@ -325,6 +359,11 @@ def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
     graphs_used = {}
     use_p2p = os.environ.get("VQ2_EP_P2P", "1") != "0"
     exchanges = {}
+    # the decode-sized steps run the exchange fused into the decode kernels (vq2_ep_decode) unless
+    # VQ2_EP_FUSED=0; the stand-alone dispatch / combine path still times the exchange alone
+    use_fused = use_p2p and os.environ.get("VQ2_EP_FUSED", "1") != "0"
+    fexchanges = {}
+    fused_used = {}
     idx_bytes_per_expert = 3 * H * I // 4 + 3 * H * I // 16      # lo + hi planes, gate/up/down
 
     def local_distinct(per_rank):
@@ -352,7 +391,15 @@ def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
             exch = exchanges[per_rank]
             if exch is not None:
                 moe = lambda x, ids, w, fn, E_: ep_moe_p2p(x, ids, w, fn, E_, exch)
-        if collective_only:      # the same exchange with an expert function that does no work
+        fexch = None
+        if use_fused and not collective_only and per_rank * world * K <= 512 and exchanges.get(per_rank):
+            if per_rank not in fexchanges:
+                fexchanges[per_rank] = P2PExchange(per_rank, H, K)
+            fexch = fexchanges[per_rank]
+            fused_used[per_rank] = True
+        if fexch is not None:
+            step = lambda i: fexch.decode(xs[i % 8], rs[i % 8][0], rs[i % 8][1], layers[i % nlayers], E)
+        elif collective_only:      # the same exchange with an expert function that does no work
             zero = lambda x, ids, w, base, El: torch.zeros(x.shape[0], H, device=x.device)
             step = lambda i: moe(xs[i % 8], rs[i % 8][0], rs[i % 8][1], zero, E)
         else:
@@ -466,12 +513,15 @@ def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
           for j in range(8)]
     outh = torch.empty(1, H, dtype=torch.float32).pin_memory()
     exch1 = exchanges.get(1)
+    fexch1 = fexchanges.get(1)
 
     def e2e_step(i):
         x = xh[i % 8].to(dev, non_blocking=True)
         ids = rh[i % 8][0].to(dev, non_blocking=True)
         w = rh[i % 8][1].to(dev, non_blocking=True)
-        if exch1 is not None:
+        if fexch1 is not None:
+            out = fexch1.decode(x, ids, w, layers[i % nlayers], E)
+        elif exch1 is not None:
             out = ep_moe_p2p(x, ids, w, fns[i % nlayers], E, exch1)
         else:
             out = ep_moe_gather(x, ids, w, fns[i % nlayers], E)
@@ -517,15 +567,19 @@ def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
                              "peak_source": f"{src} (MEASURED_PEAKS.json hbm_gbs)" if src == "measured" else src},
                 "clocks": clocks,
                 "ep": {"one_token_per_rank": d1, **extra,
-                       "exchange": "nvlink peer memory (vq2_ep_dispatch / vq2_ep_combine)" if p2p_used
-                       else "nccl all_gather + reduce_scatter"},
+                       "exchange": ("nvlink peer memory, fused into the decode kernels (vq2_ep_decode)"
+                                    if fused_used.get(1) else
+                                    "nvlink peer memory (vq2_ep_dispatch / vq2_ep_combine)" if p2p_used
+                                    else "nccl all_gather + reduce_scatter"),
+                       "exchange_only_us_is": "the stand-alone dispatch + combine with no expert work"},
                 "cuda_graphs": {str(k): v for k, v in graphs_used.items()},
                 "stack": stack,
-                # this package's kernels per timed step: the two decode kernels, plus dispatch and
-                # combine with the peer-memory exchange (NCCL kernels are not counted)
-                "gpu_launches": (4 if p2p_used else 2) * args.steps}
+                # this package's kernels per timed step: the two decode kernels, plus the finish
+                # kernel (fused exchange) or dispatch and combine (stand-alone peer-memory
+                # exchange); NCCL kernels are not counted
+                "gpu_launches": (3 if fused_used.get(1) else 4 if p2p_used else 2) * args.steps}
         print(json.dumps(line), flush=True)
-    for ex in exchanges.values():
+    for ex in list(exchanges.values()) + list(fexchanges.values()):
         if ex is not None:
             ex.close()
     dist.barrier()

@@ -1,7 +1,8 @@
-"""Expert-parallel decode and prefill on 2 GPUs (skipped with fewer) against the fp32 oracle of the
-same full layer: NCCL gather and all-to-all modes, and the NVLink peer-memory exchange (several
-consecutive steps through one region, with different token counts). NVLS is off
-(NCCL_NVLS_ENABLE=0) in the child ranks."""
+"""Expert-parallel decode and prefill against the fp32 oracle of the same full layer: NCCL gather and
+all-to-all modes, the NVLink peer-memory exchange and the exchange fused into the decode kernels
+(several consecutive steps through one region, with different token counts and id dtypes), as one
+rank on one GPU and as two ranks on 2 GPUs (skipped with fewer). NVLS is off (NCCL_NVLS_ENABLE=0)
+in the child ranks."""
 import os
 import socket
 
@@ -41,12 +42,16 @@ def _worker(rank, world, port, q):
         fn = ep.cuda_expert_fn(local)
         res = []
         exch = ep.P2PExchange(4, H, 8)
-        for N, mode in ((4, "gather"), (4, "a2a"), (300, "a2a"), (4, "p2p"), (1, "p2p"), (3, "p2p")):
-            for rep in range(2 if mode == "p2p" else 1):       # p2p: consecutive steps reuse the region
+        fexch = ep.P2PExchange(4, H, 8)      # the fused step keeps its own region
+        for N, mode in ((4, "gather"), (4, "a2a"), (300, "a2a"), (4, "p2p"), (1, "p2p"), (3, "p2p"),
+                        (4, "fused"), (1, "fused"), (3, "fused")):
+            for rep in range(1 if mode in ("gather", "a2a") else 3):   # consecutive steps reuse the region
                 x = synth.make_tokens(N, H, seed=10 + rank + rep, device=dev)
                 ids, w = synth.route_uniform(N, E, 8, seed=20 + rank + rep, device=dev)
                 if mode == "p2p":
                     out = ep.ep_moe_p2p(x, ids, w, fn, E, exch)
+                elif mode == "fused":
+                    out = ep.ep_moe_p2p_fused(x, ids.long() if rep == 1 else ids, w, local, E, fexch)
                 else:
                     out = (ep.ep_moe_gather if mode == "gather" else ep.ep_moe)(x, ids, w, fn, E)
                 # above the decode pair limit the local experts run the grouped GEMM, fp8 by
@@ -57,6 +62,7 @@ def _worker(rank, world, port, q):
         from vq2_vllm import _lib
         status = _lib.lib().vq2_device_status(1)
         exch.close()
+        fexch.close()
         if status != 0:
             raise RuntimeError(f"device status {status}")
         q.put((rank, "ok", max(res)))
@@ -65,17 +71,30 @@ def _worker(rank, world, port, q):
         q.put((rank, "error", repr(ex)))
 
 
-@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-def test_ep_two_gpus():
+def _run(world):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _port()
-    ps = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    ps = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in ps:
         p.start()
-    res = sorted(q.get(timeout=300) for _ in range(2))
+    res = sorted(q.get(timeout=300) for _ in range(world))
     for p in ps:
         p.join(timeout=60)
+    return res
+
+
+def test_ep_one_rank():
+    """Every exchange mode, the fused one included, as a group of one rank on one GPU (the region
+    is this rank's only; the flags, counters and COMB reset are exercised over consecutive steps)."""
+    for rank, status, val in _run(1):
+        assert status == "ok", val
+        assert val < 1e-2
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_ep_two_gpus():
+    res = _run(2)
     for rank, status, val in res:
         assert status == "ok", val
         assert val < 1e-2      # decode steps at 1e-2, fp8 steps at 3e-2 (scaled)
