@@ -149,9 +149,10 @@ __device__ __forceinline__ void consumer_sync() {
 // ------------------------------------------------------------------ fused expert-parallel exchange
 // With `world` > 0 the two kernels also carry the decode step's token exchange between the ranks of
 // an expert-parallel group (one exchange region per rank, mapped by every peer; field pointers per
-// rank in `peers`, EP_FIELDS each): the gate/up kernel pushes this rank's rows, ids (as i32) and
-// weights into slot `rank` of every rank's region and waits (bounded) until every rank's have
-// arrived, and the kernels then run on the gathered rows (world x N tokens, this rank's experts);
+// rank in `peers`, EP_FIELDS each): a small push kernel ahead of them stores this rank's rows, ids
+// (as i32) and weights into slot `rank` of every rank's region, the gate/up kernel waits (bounded)
+// until every rank's have arrived, and the kernels then run on the gathered rows (world x N
+// tokens, this rank's experts);
 // the down kernel adds its results with fp32 atomics straight into the owning rank's COMB rows over
 // NVLink, and its last CTA releases a completion flag to every rank. ep_finish_kernel waits for all
 // ranks' flags, copies COMB out and re-zeroes it. Steps are numbered by EPOCH in the region.
@@ -181,13 +182,19 @@ __device__ __forceinline__ void ep_wait_dispatch(const DecEp& ep, unsigned step)
   __syncthreads();
 }
 
-// All threads of every CTA: the (destination, slice) items b = blockIdx.x, + gridDim.x, ...: push
-// slice c of this rank's rows, ids and weights into slot `rank` of destination p's region and
-// release flag [rank][c] there; then wait for every rank's slices here.
-__device__ __forceinline__ void ep_dispatch_and_wait(const DecEp& ep, unsigned step) {
+// grid: world x C CTAs (C = ep_slices(N * row_x)), launched ahead of the gate/up kernel: CTA
+// (p, c) pushes slice c of this rank's rows, ids (as i32) and weights into slot `rank` of rank p's
+// region and releases flag [rank][c] there. The kernel is small, so the gate/up kernel (launched
+// behind it with programmatic dependent launch) becomes resident while the rows cross NVLink; the
+// gate/up kernel then waits for every rank's flags.
+__global__ void __launch_bounds__(512) ep_push_kernel(DecEp ep) {
+  pdl_wait();                  // the previous step (whose finish kernel precedes) is complete
+  pdl_launch_dependents();
+  const unsigned step = ep_step(ep);
   const int C = ep_slices((size_t)ep.N * ep.row_x);
   const size_t xb = (size_t)ep.N * ep.row_x, ib = (size_t)ep.N * ep.k * 4;
-  for (int b = blockIdx.x; b < ep.world * C; b += gridDim.x) {
+  {
+    const int b = blockIdx.x;
     const int p = b / C, c = b % C;
     size_t xb0, xb1, ib0, ib1;
     ep_slice(xb, c, C, 16, xb0, xb1);
@@ -205,7 +212,6 @@ __device__ __forceinline__ void ep_dispatch_and_wait(const DecEp& ep, unsigned s
     __syncthreads();                     // every thread's stores precede the release below
     if (threadIdx.x == 0) st_release_sys((unsigned*)t[EP_DFLAG] + ep.rank * C + c, step);
   }
-  ep_wait_dispatch(ep, step);
 }
 
 // Consumer threads, after the down phase: the CTA's atomics are complete; the CTA that completes
@@ -754,8 +760,8 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part, DecEp ep) {
   // it then no longer hides the activation loads below.)
   dec_init(a.w13_cb, d);
   pdl_wait();
-  // expert parallelism: gather every rank's rows, ids and weights first (the plan reads them)
-  if (ep.world > 0) ep_dispatch_and_wait(ep, ep_step(ep));
+  // expert parallelism: every rank's rows, ids and weights must have arrived (the plan reads them)
+  if (ep.world > 0) ep_wait_dispatch(ep, ep_step(ep));
   // dependents (the down kernel) may launch now: everything this grid waited for is complete
   pdl_launch_dependents();
   build_plan(a.topk_ids, a.ids_dtype, a.topk_w, a.N * a.topk, a.E, a.expert_base, d.sh);
@@ -815,9 +821,9 @@ __global__ void __launch_bounds__(512) ep_finish_kernel(float* comb, const unsig
     ((float4*)out)[i] = __ldcg((const float4*)comb + i);
     ((float4*)comb)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
-  __threadfence_system();                // the zeros precede the next step's dispatch release
   __syncthreads();
   if (threadIdx.x == 0) {
+    __threadfence_system();              // the CTA's zeros precede the next step's dispatch release
     unsigned prev;
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(count) : "memory");
     if (prev == gridDim.x - 1) {
@@ -938,6 +944,18 @@ extern "C" int vq2_ep_decode(const vq2_moe_args* a, const uint64_t* peers, int w
   ep.dflag = (const unsigned*)(r + lay->off_dflag);
   ep.epoch = (const unsigned*)(r + lay->off_epoch);
   ep.count = (unsigned*)(r + lay->off_count);
+  {
+    cudaLaunchConfig_t pc = {};
+    pc.gridDim = dim3(world * ep_slices((size_t)a->N * row_x));
+    pc.blockDim = dim3(512);
+    pc.stream = (cudaStream_t)stream;
+    cudaLaunchAttribute pa[1];
+    pa[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    pa[0].val.programmaticStreamSerializationAllowed = 1;
+    pc.attrs = pa;
+    pc.numAttrs = 1;
+    if (cudaLaunchKernelEx(&pc, ep_push_kernel, ep) != cudaSuccess) return VQ2_ERR_CUDA;
+  }
   // the kernels run on the gathered rows of all ranks (region fields, i32 ids)
   vq2_moe_args g = *a;
   g.N = world * a->N;

@@ -359,9 +359,11 @@ def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
     graphs_used = {}
     use_p2p = os.environ.get("VQ2_EP_P2P", "1") != "0"
     exchanges = {}
-    # the decode-sized steps run the exchange fused into the decode kernels (vq2_ep_decode) unless
-    # VQ2_EP_FUSED=0; the stand-alone dispatch / combine path still times the exchange alone
-    use_fused = use_p2p and os.environ.get("VQ2_EP_FUSED", "1") != "0"
+    # the headline steps use the stand-alone peer-memory exchange (dispatch / decode / combine),
+    # measured faster on the device than the exchange fused into the decode kernels
+    # (vq2_ep_decode); VQ2_EP_FUSED=1 makes the fused step the headline. The fused step is timed
+    # beside it either way.
+    use_fused = use_p2p and os.environ.get("VQ2_EP_FUSED", "0") != "0"
     fexchanges = {}
     fused_used = {}
     idx_bytes_per_expert = 3 * H * I // 4 + 3 * H * I // 16      # lo + hi planes, gate/up/down
@@ -377,7 +379,8 @@ def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
             tot += torch.unique(mine).numel()
         return tot / 8
 
-    def run(per_rank, steps, warmup, collective_only=False):
+    def run(per_rank, steps, warmup, collective_only=False, fused=None):
+        fused = use_fused if fused is None else fused
         xs = [synth.make_tokens(per_rank, H, seed=50 + 97 * rank + j, device=dev) for j in range(8)]
         rs = [synth.route_uniform(per_rank, E, K, seed=500 + 97 * rank + j, device=dev) for j in range(8)]
         gather = per_rank * world <= 512
@@ -392,11 +395,12 @@ def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
             if exch is not None:
                 moe = lambda x, ids, w, fn, E_: ep_moe_p2p(x, ids, w, fn, E_, exch)
         fexch = None
-        if use_fused and not collective_only and per_rank * world * K <= 512 and exchanges.get(per_rank):
+        if fused and not collective_only and per_rank * world * K <= 512 and exchanges.get(per_rank):
             if per_rank not in fexchanges:
                 fexchanges[per_rank] = P2PExchange(per_rank, H, K)
             fexch = fexchanges[per_rank]
-            fused_used[per_rank] = True
+            if fused == use_fused:
+                fused_used[per_rank] = True
         if fexch is not None:
             step = lambda i: fexch.decode(xs[i % 8], rs[i % 8][0], rs[i % 8][1], layers[i % nlayers], E)
         elif collective_only:      # the same exchange with an expert function that does no work
@@ -505,6 +509,9 @@ def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
         ms1 = run(1, args.steps, max(args.warmup, 3))
         clocks = None
     d1 = detail(1, ms1)
+    if use_p2p and exchanges.get(1) is not None:    # the other exchange variant of the same step
+        d1["fused_exchange_ms_per_step" if not use_fused else "standalone_exchange_ms_per_step"] = run(
+            1, args.steps, max(args.warmup, 3), fused=not use_fused)
 
     # e2e: the public call (ep_moe_p2p / ep_moe_gather) with this rank's token row, ids and
     # weights copied in from pinned host memory and its output copied back, every step
@@ -513,7 +520,7 @@ def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
           for j in range(8)]
     outh = torch.empty(1, H, dtype=torch.float32).pin_memory()
     exch1 = exchanges.get(1)
-    fexch1 = fexchanges.get(1)
+    fexch1 = fexchanges.get(1) if use_fused else None
 
     def e2e_step(i):
         x = xh[i % 8].to(dev, non_blocking=True)

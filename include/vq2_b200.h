@@ -177,8 +177,9 @@ typedef struct vq2_ep_layout {
    dispatch + vq2_decode on the gathered rows + combine; the reference's decode call
    vq2_vllm/kernels/vq2_kernel.py:569-594 runs on one device). `a` is this rank's call: x, topk_ids,
    topk_w of its N tokens (global expert ids), `out` f32 [N][H], and this rank's experts (a->E
-   experts from a->expert_base). The gate/up kernel pushes the rows to every rank and waits for
-   every rank's; both kernels run over the world*N gathered tokens; the down kernel adds each
+   experts from a->expert_base). A small push kernel stores the rows into every rank's region;
+   the gate/up kernel waits for every rank's; both decode kernels run over the world*N gathered
+   tokens; the down kernel adds each
    result into its owner's COMB rows with fp32 atomics over NVLink (so the sum order over ranks
    is not fixed); a finish kernel waits for every rank's completion flag, writes `out` and re-zeroes
    COMB. Every rank calls it once per step with the same N; world*N*topk <= VQ2_DECODE_MAX_PAIRS.
