@@ -240,7 +240,7 @@ constexpr int P2_BHALF = (P2_NSUB / 2) * 128;          // one CTA's half of one 
 constexpr int P2_BTILE = P2_NACC * P2_BHALF;           // one B stage of one CTA
 constexpr int P2_CB_COPIES = 16;
 constexpr int P2_CB_BYTES = 1024 * 8 * P2_CB_COPIES;
-constexpr int P2_IDX = 5632;                 // index planes of one stage: lo 128 x 32, hi 128 x 8, sc 128 x 4
+constexpr int P2_IDX = 5632;                 // index planes of one stage: lo [LOB/16][128][16], hi 128 x 8, sc 128 x 4
 constexpr int P2_IDX_HI = 4096, P2_IDX_SC = 5120;
 constexpr uint32_t P2_TMEM_COLS = 512;
 // TMEM columns: accumulator 0 at 0 (N <= 192), A stages 0-1 at 192 and 224, accumulator 1 at 256,
@@ -460,8 +460,13 @@ prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const 
         const uint32_t ibase = smem_u32(I_t(slot));
         if (lane == 0) {
           mbar_arrive_expect_tx(&sh->full_i[slot], P2_ROWS * LOB);
-          tma_load_2d(I_t(slot), &tm_lo, c * LOB, row0, &sh->full_i[slot]);
-          tma_load_2d(I_t(slot) + 64 * LOB, &tm_lo, c * LOB, row1, &sh->full_i[slot]);
+          // 16-byte-wide boxes: [16-byte column h][row 0..127][16 bytes] (fp8: two columns), so a
+          // decoder warp's 8-byte reads of 32 rows stride 16 bytes instead of LOB
+#pragma unroll
+          for (int h = 0; h < LOB / 16; ++h) {
+            tma_load_2d(I_t(slot) + h * (P2_ROWS * 16), &tm_lo, c * LOB + h * 16, row0, &sh->full_i[slot]);
+            tma_load_2d(I_t(slot) + h * (P2_ROWS * 16) + 64 * 16, &tm_lo, c * LOB + h * 16, row1, &sh->full_i[slot]);
+          }
         }
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -538,7 +543,7 @@ prefill_gemm_kernel(P2Args a, const __grid_constant__ CUtensorMap tm_act, const 
       if (!mbar_wait(&sh->full_i[islot], (gi / P2_ISTAGES) & 1)) return false;
       const uint32_t ip = smem_u32(I_t(islot));
       if (PREC == VQ2_PREC_FP8) {             // 8 sub-vectors, a quarter of the 128-element stage
-        const uint2 lo = lds64_v(ip + R * 32 + kq * 8);
+        const uint2 lo = lds64_v(ip + (kq >> 1) * (P2_ROWS * 16) + R * 16 + (kq & 1) * 8);
         const uint32_t hw = lds16_v(ip + P2_IDX_HI + R * 8 + kq * 2);
         const uint32_t sbits = lds16_v(ip + P2_IDX_SC + R * 4 + (kq >> 1) * 2);
         decode8_fp8_f32cb(cbl, lo, hw, __half2float(__ushort_as_half((unsigned short)sbits)), v);
@@ -970,12 +975,11 @@ extern "C" int vq2_prefill(const vq2_moe_args* a, int prec, void* ws, size_t ws_
   else
     had_quant_rows_kernel<VQ2_PREC_F16><<<a->N, 256, 0, st_>>>(a->x, a->x_dtype, nullptr, a->H, xs, invxs, pslot, a->topk);
   const int elem = prec == VQ2_PREC_FP8 ? 1 : 2;
-  const int lob = 128 / elem / 4;
   CUtensorMap tm_x, tm_v, tm_l13, tm_l2;
   if (encode_2d(&tm_x, xs, (uint64_t)a->H * elem, L.Pmax, 128, P2_NSUB / 2, true) ||
       encode_2d(&tm_v, vb, (uint64_t)a->I * elem, L.Pmax, 128, P2_NSUB / 2, true) ||
-      encode_2d(&tm_l13, a->w13_lo, a->H / 4, (uint64_t)a->E * 2 * a->I, lob, 64, false) ||
-      encode_2d(&tm_l2, a->w2_lo, a->I / 4, (uint64_t)a->E * a->H, lob, 64, false))
+      encode_2d(&tm_l13, a->w13_lo, a->H / 4, (uint64_t)a->E * 2 * a->I, 16, 64, false) ||
+      encode_2d(&tm_l2, a->w2_lo, a->I / 4, (uint64_t)a->E * a->H, 16, 64, false))
     return VQ2_ERR_CUDA;
   // CTA pairs (clusters of 2), one CTA per SM: as many pairs as can be resident at once
   cudaLaunchConfig_t cfg = {};
