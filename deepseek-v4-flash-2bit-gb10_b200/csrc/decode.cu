@@ -58,6 +58,7 @@ struct DecodeShared {
   uint64_t cbbar;
   int nunits;
   int abort;
+  int ep_last;                              // expert parallelism: this CTA completed the down grid
   float cmax;
   float red[32];
   float ginv[DEC_MAXG];                     // per 64-group: 2^-scale / 8 of the staged activation
@@ -154,8 +155,8 @@ __device__ __forceinline__ void consumer_sync() {
 // until every rank's have arrived, and the kernels then run on the gathered rows (world x N
 // tokens, this rank's experts);
 // the down kernel adds its results with fp32 atomics straight into the owning rank's COMB rows over
-// NVLink, and its last CTA releases a completion flag to every rank. ep_finish_kernel waits for all
-// ranks' flags, copies COMB out and re-zeroes it. Steps are numbered by EPOCH in the region.
+// NVLink; its last CTA releases a completion flag to every rank, waits for every rank's flag,
+// copies this rank's COMB rows out and re-zeroes them. Steps are numbered by EPOCH in the region.
 struct DecEp {
   const uint64_t* peers;    // [world][EP_FIELDS] field addresses of every rank's region
   int world, rank, N;       // N: tokens per rank
@@ -164,8 +165,12 @@ struct DecEp {
   const void* ids_local;
   const float* w_local;
   const unsigned* dflag;    // this rank's DFLAG [world][VQ2_EP_CTAS] and step counter
-  const unsigned* epoch;
+  unsigned* epoch;
   unsigned* count;          // this rank's completion counter (the down kernel's CTAs)
+  const unsigned* cflag;    // this rank's CFLAG [world]
+  float* comb;              // this rank's COMB rows [N][H] (summed by every rank's down kernel)
+  float* out;               // this rank's result [N][H]
+  int H;
 };
 
 // Step number of the current call (EPOCH is advanced by the finish kernel of the previous step).
@@ -214,19 +219,36 @@ __global__ void __launch_bounds__(512) ep_push_kernel(DecEp ep) {
   }
 }
 
-// Consumer threads, after the down phase: the CTA's atomics are complete; the CTA that completes
-// the count releases this rank's completion flag [rank] at every rank.
-__device__ __forceinline__ void ep_release_done(const DecEp& ep, unsigned step) {
+// Consumer threads, after the down phase: the CTA's atomics are complete. The CTA that completes
+// the count releases this rank's completion flag [rank] at every rank, waits (bounded) for every
+// rank's flag here, copies this rank's COMB rows to `out`, re-zeroes them and advances EPOCH
+// (every CTA of the grid read EPOCH before it counted itself).
+__device__ __forceinline__ void ep_release_done(const DecEp& ep, unsigned step, int* last_flag) {
   consumer_sync();
   if (threadIdx.x == 0) {
     __threadfence_system();
     unsigned prev;
     asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(ep.count) : "memory");
-    if (prev == gridDim.x - 1) {
+    *last_flag = prev == gridDim.x - 1;
+    if (*last_flag) {
       *ep.count = 0;
       for (int p = 0; p < ep.world; ++p)
         st_release_sys((unsigned*)ep.peers[p * EP_FIELDS + EP_CFLAG] + ep.rank, step);
     }
+  }
+  consumer_sync();
+  if (!*last_flag) return;
+  for (int f = threadIdx.x; f < ep.world; f += DEC_NW * 32) ep_wait_flag(ep.cflag + f, step);
+  consumer_sync();
+  const int n4 = ep.N * ep.H / 4;
+  for (int i = threadIdx.x; i < n4; i += DEC_NW * 32) {
+    ((float4*)ep.out)[i] = __ldcg((const float4*)ep.comb + i);
+    ((float4*)ep.comb)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+  consumer_sync();
+  if (threadIdx.x == 0) {
+    __threadfence();   // the zeros reach this GPU's L2 (where the peers' atomics land) first
+    *ep.epoch = step;
   }
 }
 
@@ -759,9 +781,12 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part, DecEp ep) {
   // kernel may still be using. (Replicating the codebook before the wait was measured slower:
   // it then no longer hides the activation loads below.)
   dec_init(a.w13_cb, d);
-  pdl_wait();
-  // expert parallelism: every rank's rows, ids and weights must have arrived (the plan reads them)
+  // expert parallelism: every rank's rows, ids and weights must have arrived (the plan reads them;
+  // their flags order them, and the push kernel ahead starts only after the previous step's
+  // finish kernel, which waited for every rank's down kernel, so no grid-dependency wait is
+  // needed). Otherwise the call's inputs may come from the previous kernel.
   if (ep.world > 0) ep_wait_dispatch(ep, ep_step(ep));
+  else pdl_wait();
   // dependents (the down kernel) may launch now: everything this grid waited for is complete
   pdl_launch_dependents();
   build_plan(a.topk_ids, a.ids_dtype, a.topk_w, a.N * a.topk, a.E, a.expert_base, d.sh);
@@ -804,34 +829,9 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA, DecE
   fill_codebook(d.cbs, d.sh);
   pdl_wait();   // the gate/up partials and the zeroed output come from the previous grid
   down_consume<KH>(a, d, part, khA, ep, c);
-  if (ep.world > 0) ep_release_done(ep, step);
+  if (ep.world > 0) ep_release_done(ep, step, &d.sh->ep_last);
 }
 
-// ------------------------------------------------------------------ expert parallelism: finish
-// Waits for every rank's completion flag of this step, copies this rank's COMB rows ([N][H] fp32,
-// summed by all ranks' atomics) to `out` and re-zeroes them; the CTA that completes the count
-// advances EPOCH. Runs in stream order after the down kernel.
-__global__ void __launch_bounds__(512) ep_finish_kernel(float* comb, const unsigned* cflag, int world,
-                                                        unsigned* epoch, unsigned* count, int n4,
-                                                        float* __restrict__ out) {
-  const unsigned step = *epoch + 1;
-  for (int f = threadIdx.x; f < world; f += blockDim.x) ep_wait_flag(cflag + f, step);
-  __syncthreads();
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += gridDim.x * blockDim.x) {
-    ((float4*)out)[i] = __ldcg((const float4*)comb + i);
-    ((float4*)comb)[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();              // the CTA's zeros precede the next step's dispatch release
-    unsigned prev;
-    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], 1;" : "=r"(prev) : "l"(count) : "memory");
-    if (prev == gridDim.x - 1) {
-      *count = 0;
-      *epoch = step;
-    }
-  }
-}
 
 static size_t decode_smem_bytes(size_t stage_bytes) {
   return CB_BYTES + ((sizeof(DecodeShared) + 127) / 128) * 128 + (size_t)DEC_STAGES * stage_bytes;
@@ -942,8 +942,12 @@ extern "C" int vq2_ep_decode(const vq2_moe_args* a, const uint64_t* peers, int w
   ep.ids_local = a->topk_ids;
   ep.w_local = a->topk_w;
   ep.dflag = (const unsigned*)(r + lay->off_dflag);
-  ep.epoch = (const unsigned*)(r + lay->off_epoch);
+  ep.epoch = (unsigned*)(r + lay->off_epoch);
   ep.count = (unsigned*)(r + lay->off_count);
+  ep.cflag = (const unsigned*)(r + lay->off_cflag);
+  ep.comb = (float*)(r + lay->off_comb);
+  ep.out = a->out;
+  ep.H = a->H;
   {
     cudaLaunchConfig_t pc = {};
     pc.gridDim = dim3(world * ep_slices((size_t)a->N * row_x));
@@ -964,18 +968,7 @@ extern "C" int vq2_ep_decode(const vq2_moe_args* a, const uint64_t* peers, int w
   g.ids_dtype = VQ2_ID_I32;
   g.topk_w = (const float*)(r + lay->off_w);
   g.out = (float*)(r + lay->off_comb);   // not written: results go to the owners' COMB rows
-  int rc = decode_launch(&g, ws, ws_bytes, stream, ep);
-  if (rc) return rc;
-  const int n4 = a->N * a->H / 4;
-  int dev = 0;
-  cudaGetDevice(&dev);
-  const int nsm = g_dec_cache[dev].nsm > 0 ? g_dec_cache[dev].nsm : 148;
-  const int grid = min(nsm, max(1, (n4 + 511) / 512));
-  ep_finish_kernel<<<grid, 512, 0, (cudaStream_t)stream>>>((float*)(r + lay->off_comb),
-                                                          (const unsigned*)(r + lay->off_cflag), world,
-                                                          (unsigned*)(r + lay->off_epoch),
-                                                          (unsigned*)(r + lay->off_count) + 1, n4, a->out);
-  return cudaGetLastError() == cudaSuccess ? VQ2_OK : VQ2_ERR_CUDA;
+  return decode_launch(&g, ws, ws_bytes, stream, ep);
 }
 // ------------------------------------------------------------------ decode from host buffers
 // One call per decode step for a caller whose inputs and result live in host memory: the three

@@ -581,7 +581,7 @@ def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
                        "exchange_only_us_is": "the stand-alone dispatch + combine with no expert work"},
                 "cuda_graphs": {str(k): v for k, v in graphs_used.items()},
                 "stack": stack,
-                # this package's kernels per timed step: the two decode kernels, plus the finish
+                # this package's kernels per timed step: the two decode kernels, plus the push
                 # kernel (fused exchange) or dispatch and combine (stand-alone peer-memory
                 # exchange); NCCL kernels are not counted
                 "gpu_launches": (3 if fused_used.get(1) else 4 if p2p_used else 2) * args.steps}

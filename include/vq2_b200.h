@@ -145,7 +145,7 @@ int vq2_hadamard_rows(const void* x, int in_dtype, void* y, int out_dtype, long 
      COMB [world][N][H] f32   partial outputs pushed back by each rank, for this rank's tokens
      DFLAG[world][VQ2_EP_CTAS] u32, CFLAG[world][VQ2_EP_CTAS] u32   per-(source, slice) step flags
      EPOCH u32   this rank's step
-     COUNT u32[2]   completion counters of the fused step (vq2_ep_decode)
+     COUNT u32[2]   completion counter of the fused step's down kernel (vq2_ep_decode)
    `peers` is a device array [world][6] of u64 addresses (X, IDS, WT, COMB, DFLAG, CFLAG) of every
    rank's region, this rank's included. Every rank calls dispatch / combine once per step with the
    same N. Waits are bounded: a peer that never arrives makes vq2_device_status report
@@ -179,11 +179,10 @@ typedef struct vq2_ep_layout {
    topk_w of its N tokens (global expert ids), `out` f32 [N][H], and this rank's experts (a->E
    experts from a->expert_base). A small push kernel stores the rows into every rank's region;
    the gate/up kernel waits for every rank's; both decode kernels run over the world*N gathered
-   tokens; the down kernel adds each
-   result into its owner's COMB rows with fp32 atomics over NVLink (so the sum order over ranks
-   is not fixed); a finish kernel waits for every rank's completion flag, writes `out` and re-zeroes
-   COMB. Every rank calls it once per step with the same N; world*N*topk <= VQ2_DECODE_MAX_PAIRS.
-   Four launches, no host synchronisation. Do not mix with dispatch / combine on one region. */
+   tokens; the down kernel adds each result into its owner's COMB rows with fp32 atomics over
+   NVLink (so the sum order over ranks is not fixed), and its last CTA waits for every rank's
+   completion flag, writes `out` and re-zeroes COMB. Every rank calls it once per step with the
+   same N; world*N*topk <= VQ2_DECODE_MAX_PAIRS. Three launches, no host synchronisation. Do not mix with dispatch / combine on one region. */
 size_t vq2_ep_decode_workspace_size(int world, int N, int topk, int H, int I);
 int vq2_ep_decode(const vq2_moe_args* a, const uint64_t* peers, int world, int rank, void* my_region,
                   const vq2_ep_layout* layout, void* ws, size_t ws_bytes, void* stream);
