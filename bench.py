@@ -276,6 +276,54 @@ def time_pack(dev):
     return res
 
 
+def time_routed_plus_shared(layers, dev):
+    """Config 1, batch 1: the routed decode plus the shared expert per layer call, (a) one after
+    the other on one stream and (b) co-scheduled by vq2_decode_with_shared (the shared expert's
+    kernels on a partition of the SMs, concurrently with the routed ones). Four routed layers and
+    four shared-weight copies cycled; 8 calls per CUDA graph, 25 replays (us per call)."""
+    from vq2_vllm import synth
+    from vq2_vllm.kernels.shared_expert import moe_with_shared_expert, shared_expert_fused
+    from vq2_vllm.kernels.vq2_kernel import vq2_moe_fused_10b
+    g = torch.Generator(device=dev).manual_seed(41)
+    sh = [((torch.randn(2 * I, H, generator=g, device=dev) * 0.02).bfloat16(),
+           (torch.randn(H, I, generator=g, device=dev) * 0.02).bfloat16()) for _ in range(4)]
+    xs = [synth.make_tokens(1, H, seed=100 + j, device=dev) for j in range(8)]
+    routes = [make_routing(xs[j], seed=200 + j) for j in range(8)]
+    nl = len(layers)
+
+    def timed(step):
+        for i in range(8):
+            step(i)
+        torch.cuda.synchronize()
+        gr = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(gr):
+            for i in range(8):
+                step(i)
+        for _ in range(3):
+            gr.replay()
+        torch.cuda.synchronize()
+        st, en = torch.cuda.Event(True), torch.cuda.Event(True)
+        st.record()
+        for _ in range(25):
+            gr.replay()
+        en.record()
+        en.synchronize()
+        return st.elapsed_time(en) * 1e3 / 200
+
+    def seq(i):
+        o = vq2_moe_fused_10b(xs[i % 8], *routes[i % 8], *synth.layer_args(layers[i % nl]))
+        shared_expert_fused(xs[i % 8], *sh[i % 4], out=o)
+
+    res = {"workload": "config1 batch 1: routed layer + shared expert (bf16 [4096, 4096] + [4096, 2048])",
+           "sequential_us": timed(seq),
+           "coscheduled_us": timed(lambda i: moe_with_shared_expert(
+               xs[i % 8], *routes[i % 8], *synth.layer_args(layers[i % nl]), *sh[i % 4])),
+           "shared_sms": "library default (VQ2_SHARED_SMS_DEFAULT)"}
+    del sh
+    torch.cuda.empty_cache()
+    return res
+
+
 def time_shared(dev, hbm):
     """The config-1 shared expert (bf16 gate/up [4096, 4096], down [4096, 2048]) for batch 1 and
     3: four copies of its weights (201 MB > L2) cycled, one call per copy captured in a CUDA
@@ -526,6 +574,10 @@ def run_ours(args, rank, world):
     d2h = H * 4
 
     prefill = time_prefill(layers, dev, args)
+    try:
+        with_shared = time_routed_plus_shared(layers, dev)
+    except Exception as ex:  # a figure beside the headline must not cost the headline line
+        with_shared = {"error": f"{type(ex).__name__}: {ex}"[:300]}
     del layers
     torch.cuda.empty_cache()
     try:
@@ -557,6 +609,7 @@ def run_ours(args, rank, world):
                        "distinct_experts_per_step": u1},
             "router": {**router, "workload": "top-8 of softmax(x @ W_r), x [1, 4096], W_r [4096, 256], graph replay"},
             "shared_expert": {**shared, "workload": "config1 shared expert, bf16 gate/up [4096, 4096] + down [4096, 2048], 4 weight copies cycled (> L2)"},
+            "routed_plus_shared": with_shared,
             "pack": {**pack, "workload": "VQ packer on 8 experts of the gate/up tensor, 8 x 4096 x 4096 bf16"},
             "decode_graph": {"us_per_token": ms_graph * 1e3,
                              "how": "the same batch-1 steps replayed from CUDA graphs"},

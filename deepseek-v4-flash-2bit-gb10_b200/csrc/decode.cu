@@ -171,6 +171,7 @@ struct DecEp {
   float* comb;              // this rank's COMB rows [N][H] (summed by every rank's down kernel)
   float* out;               // this rank's result [N][H]
   int H;
+  int keep_out;             // (world 0) the output already holds values to add to: do not zero it
 };
 
 // Step number of the current call (EPOCH is advanced by the finish kernel of the previous step).
@@ -799,7 +800,7 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part, DecEp ep) {
     return;
   }
   GateupPre pre;
-  gateup_pre(a, d, pre, ep.world == 0);
+  gateup_pre(a, d, pre, ep.world == 0 && !ep.keep_out);
   fill_codebook(d.cbs, d.sh);         // overlaps the activation loads of gateup_pre
   gateup_consume<KH>(a, d, part, pre, c);
 }
@@ -857,7 +858,9 @@ extern "C" size_t vq2_decode_workspace_size(int N, int topk, int H, int I) {
 }
 
 // Validation and the two launches; `ep` (world 0: none) selects the fused expert-parallel exchange.
-static int decode_launch(const vq2_moe_args* a, void* ws, size_t ws_bytes, void* stream, const DecEp& ep) {
+// ctas > 0 runs the persistent grids on that many CTAs (one per SM) instead of one per SM.
+static int decode_launch(const vq2_moe_args* a, void* ws, size_t ws_bytes, void* stream, const DecEp& ep,
+                         int ctas = 0) {
   if (!a || !a->x || !a->topk_ids || !a->topk_w || !a->out || !a->w13_cb || !a->w13_lo || !a->w13_hi ||
       !a->w13_sc || !a->w2_cb || !a->w2_lo || !a->w2_hi || !a->w2_sc)
     return VQ2_ERR_NULL;
@@ -889,7 +892,7 @@ static int decode_launch(const vq2_moe_args* a, void* ws, size_t ws_bytes, void*
   const int khA = khA_of(a->H), khB = khA_of(a->I);
   vq2_moe_args args = *a;
   cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3(lc.nsm);
+  cfg.gridDim = dim3(ctas > 0 && ctas < lc.nsm ? ctas : lc.nsm);
   cfg.blockDim = dim3(DEC_THREADS);
   cfg.dynamicSmemBytes = sm;
   cfg.stream = (cudaStream_t)stream;

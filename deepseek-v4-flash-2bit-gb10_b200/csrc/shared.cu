@@ -202,8 +202,13 @@ __global__ void __launch_bounds__(SE_THREADS, SE_CTAS_PER_SM) shared_down_kernel
         const float as = warp_sum(a[n]), bs = warp_sum(b[n]);
         if (lane == 0) {
           float* o = out + (size_t)n * H + 2 * unit;
-          o[0] = accumulate ? o[0] + as : as;
-          o[1] = accumulate ? o[1] + bs : bs;
+          if (accumulate == 2) {          // concurrent with other writers of `out`: fp32 atomics
+            atomicAdd(o, as);
+            atomicAdd(o + 1, bs);
+          } else {
+            o[0] = accumulate ? o[0] + as : as;
+            o[1] = accumulate ? o[1] + bs : bs;
+          }
         }
       }
     }
@@ -212,31 +217,30 @@ __global__ void __launch_bounds__(SE_THREADS, SE_CTAS_PER_SM) shared_down_kernel
 
 constexpr int SE_SMEM_CAP = 200 * 1024;   // dynamic shared memory of either kernel (x or inter as fp32)
 
-inline int se_grid(long long warps) {
+// grid of a kernel whose warps take `warps` row units: at most SE_CTAS_PER_SM CTAs per SM of the
+// `sms` SMs it may use (all of them when sms <= 0)
+inline int se_grid(long long warps, int sms = 0) {
   const long long b = (warps + SE_WARPS - 1) / SE_WARPS;
-  const long long nsm = std::max(device_sm_count(), 1);
+  const long long nsm = sms > 0 ? sms : std::max(device_sm_count(), 1);
   return (int)std::min<long long>(std::max<long long>(b, 1), nsm * SE_CTAS_PER_SM);
 }
 
-}  // namespace vq2
-
-using namespace vq2;
-
-extern "C" size_t vq2_shared_expert_workspace_size(int N, int Is) {
-  if (N <= 0 || Is <= 0) return 0;
-  return (size_t)N * Is * sizeof(float) + 256;
-}
-
-extern "C" int vq2_shared_expert(const void* x, int x_dtype, const void* w13, const void* w2, int N, int H, int Is,
-                                 float* out, int accumulate, void* ws, size_t ws_bytes, void* stream) {
+// Validation of a shared-expert call (0 if it can run).
+inline int se_check(const void* x, int x_dtype, const void* w13, const void* w2, int N, int H, int Is,
+                    const float* out) {
   if (!x || !w13 || !w2 || !out) return VQ2_ERR_NULL;
   if (N <= 0 || N > SE_MAX_N || H <= 0 || Is <= 0 || H % 256 || Is % 256 || H % 2) return VQ2_ERR_SHAPE;
-  const size_t sm_gu = (size_t)N * H * sizeof(float), sm_dn = (size_t)N * Is * sizeof(float);
-  if (sm_gu > (size_t)SE_SMEM_CAP || sm_dn > (size_t)SE_SMEM_CAP) return VQ2_ERR_SHAPE;
+  if ((size_t)N * H * sizeof(float) > (size_t)SE_SMEM_CAP || (size_t)N * Is * sizeof(float) > (size_t)SE_SMEM_CAP)
+    return VQ2_ERR_SHAPE;
   if (x_dtype < 0 || x_dtype > 2) return VQ2_ERR_DTYPE;
   if ((uintptr_t)w13 % 16 || (uintptr_t)w2 % 16 || (uintptr_t)x % 16) return VQ2_ERR_ALIGN;
-  if (!ws || ws_bytes < vq2_shared_expert_workspace_size(N, Is)) return VQ2_ERR_WORKSPACE;
-  float* inter = (float*)(((uintptr_t)ws + 255) & ~(uintptr_t)255);
+  return VQ2_OK;
+}
+
+// The two kernels on `stream` (inputs checked by se_check). accumulate: 0 write, 1 add, 2 add
+// with fp32 atomics; sms > 0 caps the grids to that many SMs' worth of CTAs.
+inline int se_launch(const void* x, int x_dtype, const void* w13, const void* w2, int N, int H, int Is,
+                     float* out, int accumulate, float* inter, cudaStream_t stream, int sms) {
   // The dynamic shared-memory limit is raised once per device to the cap every call fits in, so
   // calls with different N (other threads, captured graphs) never lower it under one another.
   int dev = 0;
@@ -253,18 +257,98 @@ extern "C" int vq2_shared_expert(const void* x, int x_dtype, const void* w13, co
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cudaLaunchConfig_t cfg = {};
   cfg.blockDim = dim3(SE_THREADS);
-  cfg.stream = (cudaStream_t)stream;
+  cfg.stream = stream;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cfg.gridDim = dim3(se_grid(Is));
-  cfg.dynamicSmemBytes = sm_gu;
+  cfg.gridDim = dim3(se_grid(Is, sms));
+  cfg.dynamicSmemBytes = (size_t)N * H * sizeof(float);
   if (cudaLaunchKernelEx(&cfg, shared_gateup_kernel, x, x_dtype, (const __nv_bfloat16*)w13, N, H, Is, inter) !=
       cudaSuccess)
     return VQ2_ERR_CUDA;
-  cfg.gridDim = dim3(se_grid(H / 2));
-  cfg.dynamicSmemBytes = sm_dn;
+  cfg.gridDim = dim3(se_grid(H / 2, sms));
+  cfg.dynamicSmemBytes = (size_t)N * Is * sizeof(float);
   if (cudaLaunchKernelEx(&cfg, shared_down_kernel, (const float*)inter, (const __nv_bfloat16*)w2, N, H, Is, out,
                          accumulate) != cudaSuccess)
+    return VQ2_ERR_CUDA;
+  return VQ2_OK;
+}
+
+}  // namespace vq2
+
+using namespace vq2;
+
+extern "C" size_t vq2_shared_expert_workspace_size(int N, int Is) {
+  if (N <= 0 || Is <= 0) return 0;
+  return (size_t)N * Is * sizeof(float) + 256;
+}
+
+extern "C" int vq2_shared_expert(const void* x, int x_dtype, const void* w13, const void* w2, int N, int H, int Is,
+                                 float* out, int accumulate, void* ws, size_t ws_bytes, void* stream) {
+  const int rc = se_check(x, x_dtype, w13, w2, N, H, Is, out);
+  if (rc) return rc;
+  if (!ws || ws_bytes < vq2_shared_expert_workspace_size(N, Is)) return VQ2_ERR_WORKSPACE;
+  float* inter = (float*)(((uintptr_t)ws + 255) & ~(uintptr_t)255);
+  return se_launch(x, x_dtype, w13, w2, N, H, Is, out, accumulate ? 1 : 0, inter, (cudaStream_t)stream, 0);
+}
+
+// ------------------------------------------------------------------ routed + shared, co-scheduled
+// The routed decode kernels are issue bound (codebook gathers) and leave HBM bandwidth unused; the
+// shared expert is a pure weight stream. Running the shared expert's kernels on a partition of the
+// SMs while the routed kernels hold the rest overlaps the two: the output is zeroed once, the
+// routed grids run on (SMs - shared_sms) CTAs and add with their fp32 atomics, and the shared
+// kernels run concurrently on a second stream (this library's, one per device, forked from and
+// joined back into the caller's stream with events) on shared_sms SMs' worth of CTAs, adding with
+// fp32 atomics. A host lock per device keeps concurrent callers' fork/join pairs apart.
+#include <mutex>
+
+namespace vq2 {
+struct CoSched {
+  cudaStream_t side = nullptr;
+  cudaEvent_t fork = nullptr, join = nullptr;
+  std::mutex mu;
+};
+static CoSched g_cosched[64];
+}  // namespace vq2
+
+extern "C" size_t vq2_decode_with_shared_workspace_size(int N, int topk, int H, int I, int Is) {
+  const size_t a = (vq2_decode_workspace_size(N, topk, H, I) + 255) & ~(size_t)255;
+  return a + vq2_shared_expert_workspace_size(N, Is);
+}
+
+extern "C" int vq2_decode_with_shared(const vq2_moe_args* a, const void* sw13, const void* sw2, int Is, int shared_sms,
+                                      void* ws, size_t ws_bytes, void* stream) {
+  if (!a) return VQ2_ERR_NULL;
+  int rc = se_check(a->x, a->x_dtype, sw13, sw2, a->N, a->H, Is, a->out);
+  if (rc) return rc;
+  if (!ws || ws_bytes < vq2_decode_with_shared_workspace_size(a->N, a->topk, a->H, a->I, Is)) return VQ2_ERR_WORKSPACE;
+  const size_t wa = (vq2_decode_workspace_size(a->N, a->topk, a->H, a->I) + 255) & ~(size_t)255;
+  float* inter = (float*)((((uintptr_t)ws + wa) + 255) & ~(uintptr_t)255);
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VQ2_ERR_NO_DEVICE;
+  const int nsm = device_sm_count();
+  if (nsm <= 0) return VQ2_ERR_CUDA;
+  if (shared_sms <= 0) shared_sms = VQ2_SHARED_SMS_DEFAULT;
+  if (shared_sms >= nsm) return VQ2_ERR_SHAPE;
+  CoSched& cs = g_cosched[dev];
+  std::lock_guard<std::mutex> lock(cs.mu);
+  if (!cs.side) {
+    if (cudaStreamCreateWithFlags(&cs.side, cudaStreamNonBlocking) != cudaSuccess ||
+        cudaEventCreateWithFlags(&cs.fork, cudaEventDisableTiming) != cudaSuccess ||
+        cudaEventCreateWithFlags(&cs.join, cudaEventDisableTiming) != cudaSuccess)
+      return VQ2_ERR_CUDA;
+  }
+  cudaStream_t s = (cudaStream_t)stream;
+  if (cudaMemsetAsync(a->out, 0, (size_t)a->N * a->H * sizeof(float), s) != cudaSuccess) return VQ2_ERR_CUDA;
+  if (cudaEventRecord(cs.fork, s) != cudaSuccess || cudaStreamWaitEvent(cs.side, cs.fork, 0) != cudaSuccess)
+    return VQ2_ERR_CUDA;
+  // routed first, so its one-CTA-per-SM grids take their SMs before the shared kernels' CTAs land
+  DecEp ep = {};
+  ep.keep_out = 1;
+  rc = decode_launch(a, ws, wa, stream, ep, nsm - shared_sms);
+  if (rc) return rc;
+  rc = se_launch(a->x, a->x_dtype, sw13, sw2, a->N, a->H, Is, a->out, 2, inter, cs.side, shared_sms);
+  if (rc) return rc;
+  if (cudaEventRecord(cs.join, cs.side) != cudaSuccess || cudaStreamWaitEvent(s, cs.join, 0) != cudaSuccess)
     return VQ2_ERR_CUDA;
   return VQ2_OK;
 }

@@ -90,6 +90,9 @@ _SIGS = {
     "vq2_shared_expert": (ctypes.c_int, [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
                                          ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
                                          ctypes.c_size_t, ctypes.c_void_p]),
+    "vq2_decode_with_shared_workspace_size": (ctypes.c_size_t, [ctypes.c_int] * 5),
+    "vq2_decode_with_shared": (ctypes.c_int, [ctypes.POINTER(Vq2MoeArgs), ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int,
+                                              ctypes.c_int, ctypes.c_void_p, ctypes.c_size_t, ctypes.c_void_p]),
     "vq2_device_status": (ctypes.c_int, [ctypes.c_int]),
     "vq2_strerror": (ctypes.c_char_p, [ctypes.c_int]),
     "vq2_version": (ctypes.c_int, []),

@@ -46,3 +46,33 @@ def shared_expert_fused(x: torch.Tensor, w13: torch.Tensor, w2: torch.Tensor, ou
                                        out.data_ptr(), int(acc), ws.data_ptr(), ws.numel(), stream),
                    "vq2_shared_expert")
         return out
+
+
+def moe_with_shared_expert(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn, w13, w2, shared_sms: int = 0,
+                           expert_base: int = 0):
+    """Routed decode (as ``vq2_moe_fused_10b``) plus the shared expert (as ``shared_expert_fused``)
+    for the same tokens in one call -> fp32 [N, H] (N <= 8, N * k within the decode pair limit).
+    The shared expert's kernels run concurrently with the routed ones on ``shared_sms`` SMs (0: the
+    library default) on a second stream of the library, forked and joined with events on the
+    current stream; both add into the output with fp32 atomics."""
+    from .vq2_kernel import _prep
+    if w13.dtype != torch.bfloat16 or w2.dtype != torch.bfloat16:
+        raise ValueError("vq2 shared expert: bf16 weights expected")
+    N, H = x.shape
+    Is = w13.shape[0] // 2
+    if w13.shape != (2 * Is, H) or w2.shape != (H, Is):
+        raise ValueError("vq2 shared expert: w13 [2*Is, H] and w2 [H, Is] expected")
+    if N * topk_ids.shape[1] > _lib.DECODE_MAX_PAIRS:
+        raise ValueError("vq2 routed + shared: N * k above the decode pair limit")
+    with torch.cuda.device(x.device):
+        t = _prep(x, topk_ids, topk_w, Cgu, lgu, hgu, sgu, Cd, ld, hd, sdn)
+        w13, w2 = w13.contiguous(), w2.contiguous()
+        _lib.require_cuda(w13, w2, device=x.get_device())
+        out = torch.empty(N, H, dtype=torch.float32, device=x.device)
+        L = _lib.lib()
+        a = _lib.moe_args(*t, out, expert_base=expert_base)
+        stream = torch.cuda.current_stream(x.device).cuda_stream
+        ws = _lib.workspace(L.vq2_decode_with_shared_workspace_size(N, topk_ids.shape[1], H, a.I, Is), x.device, stream)
+        _lib.check(L.vq2_decode_with_shared(a, w13.data_ptr(), w2.data_ptr(), Is, int(shared_sms), ws.data_ptr(),
+                                            ws.numel(), stream), "vq2_decode_with_shared")
+        return out

@@ -232,6 +232,19 @@ size_t vq2_shared_expert_workspace_size(int N, int Is);
 int vq2_shared_expert(const void* x, int x_dtype, const void* w13, const void* w2, int N, int H, int Is, float* out,
                       int accumulate, void* workspace, size_t ws_bytes, void* stream);
 
+/* Routed decode plus the shared expert in one call: out = routed MoE (as vq2_decode) + the shared
+   expert (as vq2_shared_expert with sw13 / sw2 / Is) for the same x, fp32 [N][H] (N <= 8 for the
+   shared part). The routed kernels run on (SMs - shared_sms) SMs and the shared expert's kernels
+   concurrently on shared_sms SMs (<= 0: VQ2_SHARED_SMS_DEFAULT) on a second stream this library
+   creates per device, forked from and joined into `stream` with events (capturable in a CUDA
+   graph); both add into `out` with fp32 atomics after one zeroing, so the sum order is not fixed.
+   Workspace: vq2_decode_with_shared_workspace_size. No reference counterpart as one call: vLLM
+   runs the shared expert beside the MoE method (reference vq2_vllm/__init__.py:197-198). */
+#define VQ2_SHARED_SMS_DEFAULT 56   /* best of a 12..110 sweep at config 1, batch 1 */
+size_t vq2_decode_with_shared_workspace_size(int N, int topk, int H, int I, int Is);
+int vq2_decode_with_shared(const vq2_moe_args* a, const void* sw13, const void* sw2, int Is, int shared_sms,
+                           void* ws, size_t ws_bytes, void* stream);
+
 /* Error word written by bounded device waits and device-side range checks (0 = none);
    reset = 1 clears it. Synchronises the device. */
 int vq2_device_status(int reset);
