@@ -302,6 +302,40 @@ def ep_moe_p2p_fused(x, topk_ids, topk_w, local: dict, E: int, exch: P2PExchange
     return exch.decode(x, topk_ids, topk_w, local, E)
 
 
+def balanced_placement(load: torch.Tensor, world: int):
+    """Expert placement from per-expert loads (e.g. routed-pair counts of a calibration batch):
+    returns ``(order, virt)``, int64 [E] each. ``order[v]`` is the global expert held in virtual
+    slot v, ranks holding the contiguous virtual slots [r*E/W, (r+1)*E/W) as before, and
+    ``virt[e]`` its inverse. Greedy longest-processing-time: experts by load, heaviest first, each
+    to the rank with the least load that still has room, so every rank holds E/W experts and the
+    per-rank loads are as even as that greedy makes them. Relabel a step's ids with ``virt[ids]``
+    and give rank r the experts ``order[r*E/W:(r+1)*E/W]`` (``local_layer_placed``); the exchange
+    and the kernels are unchanged."""
+    E = load.numel()
+    if E % world:
+        raise ValueError(f"vq2 ep: {E} experts do not split evenly over {world} ranks")
+    per = E // world
+    lsum = [0.0] * world
+    slots = [[] for _ in range(world)]
+    for e in torch.argsort(load.double().cpu(), descending=True, stable=True).tolist():
+        r = min((r for r in range(world) if len(slots[r]) < per), key=lambda r: (lsum[r], r))
+        slots[r].append(e)
+        lsum[r] += float(load[e])
+    order = torch.tensor([e for r in range(world) for e in sorted(slots[r])], dtype=torch.int64)
+    virt = torch.empty_like(order)
+    virt[order] = torch.arange(E, dtype=torch.int64)
+    return order, virt
+
+
+def local_layer_placed(layer: dict, order: torch.Tensor, rank: int, world: int) -> dict:
+    """This rank's experts under a placement (``balanced_placement``): the experts
+    ``order[rank*E/W:(rank+1)*E/W]`` of a full layer dict, in that order."""
+    E = order.numel()
+    per = E // world
+    sel = order[rank * per:(rank + 1) * per]
+    return {k: (v.index_select(0, sel.to(v.device)) if v.dim() == 3 else v) for k, v in layer.items()}
+
+
 def local_layer(layer: dict, rank: int, world: int) -> dict:
     """This rank's slice of a full layer dict (experts [rank*E/W, (rank+1)*E/W))."""
     E = layer["w13_lo"].shape[0]
@@ -449,46 +483,66 @@ def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
         """Config 4: a stack of `nl` seeded layers over `tokens_total` tokens (tokens_total / W per
         rank), Zipf(1.1) top-8 per layer (one expert popularity per layer, shared by the ranks),
         x = x + moe(x) in bf16, NCCL all-to-all dispatch and combine, each rank's experts on the
-        grouped GEMM (fp8). Whole-stack time on the device, max over ranks."""
+        grouped GEMM (fp8). Timed twice: experts placed contiguously, and placed by
+        `balanced_placement` from the per-expert loads of a separate calibration draw of the same
+        popularity (ids relabelled; every rank derives the same placement from the summed
+        counts). Whole-stack time on the device, max over ranks."""
         n = tokens_total // world
         Ls = [synth.make_layer(per, H, I, seed=5000 + 100 * l + rank, device=dev) for l in range(nl)]
         sfns = [cuda_expert_fn(L) for L in Ls]
         x0 = synth.make_tokens(n, H, seed=6000 + rank, device=dev)
         routes = [synth.route_zipf(n, E, K, s=1.1, seed=7000 + l, device=dev, draw_seed=7100 + 100 * l + rank)
                   for l in range(nl)]
-        loads = []
-        for ids, _ in routes:           # pairs per owning rank, summed over the ranks
-            cnt = torch.bincount((ids.long() // per).flatten(), minlength=world).float()
+        placed = []
+        for l in range(nl):             # calibration: the same popularity, another draw
+            cal, _ = synth.route_zipf(n, E, K, s=1.1, seed=7000 + l, device=dev, draw_seed=9100 + 100 * l + rank)
+            cnt = torch.bincount(cal.flatten().long(), minlength=E).double()
             dist.all_reduce(cnt)
-            loads.append((cnt.max() / cnt.mean()).item())
+            _, virt = balanced_placement(cnt, world)
+            placed.append((virt.to(dev)[routes[l][0].long()].to(torch.int32), routes[l][1]))
 
-        def stack_step():
-            x = x0
-            for l in range(nl):
-                x = x + ep_moe(x, *routes[l], sfns[l], E).to(x.dtype)
-            return x
+        def imbalance(rts):             # pairs per owning rank, summed over the ranks
+            out = []
+            for ids, _ in rts:
+                cnt = torch.bincount((ids.long() // per).flatten(), minlength=world).float()
+                dist.all_reduce(cnt)
+                out.append(round((cnt.max() / cnt.mean()).item(), 3))
+            return out
 
-        stack_step()
-        torch.cuda.synchronize()
-        dist.barrier()
-        s, e = torch.cuda.Event(True), torch.cuda.Event(True)
-        s.record()
-        for _ in range(reps):
+        def timed(rts):
+            def stack_step():
+                x = x0
+                for l in range(nl):
+                    x = x + ep_moe(x, *rts[l], sfns[l], E).to(x.dtype)
+                return x
+
             stack_step()
-        e.record()
-        e.synchronize()
-        ms = torch.tensor([s.elapsed_time(e) / reps], device=dev)
-        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
-        ms = ms.item()
+            torch.cuda.synchronize()
+            dist.barrier()
+            s, e = torch.cuda.Event(True), torch.cuda.Event(True)
+            s.record()
+            for _ in range(reps):
+                stack_step()
+            e.record()
+            e.synchronize()
+            ms = torch.tensor([s.elapsed_time(e) / reps], device=dev)
+            dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+            return ms.item()
+
+        ms_c = timed(routes)
+        ms = timed(placed)
         flops = nl * (2.0 * tokens_total * K * H * 2 * I + 2.0 * tokens_total * K * I * H)
         bf16 = peaks_fn()[1] if peaks_fn is not None else 1590.0
         del Ls, sfns
         torch.cuda.empty_cache()
         return {"workload": f"config4: {nl} layers, {tokens_total} tokens ({n} per rank), Zipf(1.1) top-8, fp8, "
-                            f"residual, ep{world} (NCCL all-to-all)",
+                            f"residual, ep{world} (NCCL all-to-all), load-balanced expert placement",
                 "ms_per_stack": ms, "tok_per_s": tokens_total / (ms * 1e-3),
                 "tensor_frac_per_gpu": flops / world / (ms * 1e-3) / 1e12 / (2 * bf16),
-                "expert_load_max_over_mean_per_layer": [round(v, 3) for v in loads], "reps": reps}
+                "expert_load_max_over_mean_per_layer": imbalance(placed),
+                "contiguous_placement": {"ms_per_stack": ms_c, "tok_per_s": tokens_total / (ms_c * 1e-3),
+                                         "expert_load_max_over_mean_per_layer": imbalance(routes)},
+                "reps": reps}
 
     def detail(per_rank, ms):
         """Per-GPU HBM rate on the index bytes of this rank's distinct experts (mean over ranks)
