@@ -45,6 +45,11 @@ __global__ void __launch_bounds__(512) ep_dispatch_kernel(const uint8_t* __restr
                                                           int ids_i64, const float* __restrict__ w, int N, int row_x,
                                                           int k, const uint64_t* __restrict__ peers, int world,
                                                           int rank, unsigned* my_dflag, unsigned* epoch) {
+  // launched with programmatic dependent launch: the decode kernel behind may become resident now
+  // (it waits for this grid); this grid waits for its predecessor (the previous step's combine,
+  // which saw every rank's partials, so every peer has consumed the slots written here) first
+  pdl_launch_dependents();
+  pdl_wait();
   const int C = gridDim.x;
   const int c = blockIdx.x;
   const unsigned ep = *epoch + 1;
@@ -86,6 +91,10 @@ __global__ void __launch_bounds__(512) ep_combine_kernel(const float* __restrict
                                                          const uint64_t* __restrict__ peers, int world, int rank,
                                                          const float* my_comb, unsigned* my_cflag,
                                                          const unsigned* epoch, float* __restrict__ out) {
+  // launched with programmatic dependent launch behind the down kernel: resident early, it waits
+  // for that grid (whose partials it pushes) before reading anything
+  pdl_launch_dependents();
+  pdl_wait();
   const int C = gridDim.x / world;
   const unsigned ep = *epoch;            // this step, advanced by the dispatch kernel
   const int d = blockIdx.x / C, c = blockIdx.x % C;
@@ -163,10 +172,20 @@ extern "C" int vq2_ep_dispatch(const void* x, const void* ids, int ids_dtype, co
   if (((uintptr_t)x & 15) || ((uintptr_t)ids & 15) || ((uintptr_t)w & 15) || (off_dflag & 15) || (off_epoch & 15))
     return VQ2_ERR_ALIGN;
   uint8_t* r = (uint8_t*)my_region;
-  ep_dispatch_kernel<<<ep_slices((size_t)N * row_x), 512, 0, (cudaStream_t)stream>>>(
-      (const uint8_t*)x, ids, ids_dtype == VQ2_ID_I64, w, N, row_x, k, peers, world, rank,
-                                                          (unsigned*)(r + off_dflag), (unsigned*)(r + off_epoch));
-  return cudaGetLastError() == cudaSuccess ? VQ2_OK : VQ2_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(ep_slices((size_t)N * row_x));
+  cfg.blockDim = dim3(512);
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, ep_dispatch_kernel, (const uint8_t*)x, ids, (int)(ids_dtype == VQ2_ID_I64), w, N,
+                            row_x, k, peers, world, rank, (unsigned*)(r + off_dflag), (unsigned*)(r + off_epoch)) ==
+                 cudaSuccess
+             ? VQ2_OK
+             : VQ2_ERR_CUDA;
 }
 
 extern "C" int vq2_ep_combine(const float* part, int N, int H, const uint64_t* peers, int world, int rank,
@@ -177,8 +196,17 @@ extern "C" int vq2_ep_combine(const float* part, int N, int H, const uint64_t* p
   if (((uintptr_t)part & 15) || ((uintptr_t)out & 15) || (off_comb & 15) || (off_cflag & 15) || (off_epoch & 15))
     return VQ2_ERR_ALIGN;
   uint8_t* r = (uint8_t*)my_region;
-  ep_combine_kernel<<<world * ep_slices((size_t)N * H * 4), 512, 0, (cudaStream_t)stream>>>(part, N, H, peers, world, rank, (const float*)(r + off_comb),
-                                                             (unsigned*)(r + off_cflag),
-                                                             (const unsigned*)(r + off_epoch), out);
-  return cudaGetLastError() == cudaSuccess ? VQ2_OK : VQ2_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(world * ep_slices((size_t)N * H * 4));
+  cfg.blockDim = dim3(512);
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, ep_combine_kernel, part, N, H, peers, world, rank, (const float*)(r + off_comb),
+                            (unsigned*)(r + off_cflag), (const unsigned*)(r + off_epoch), out) == cudaSuccess
+             ? VQ2_OK
+             : VQ2_ERR_CUDA;
 }
