@@ -237,7 +237,8 @@ int vq2_shared_expert(const void* x, int x_dtype, const void* w13, const void* w
    shared part). The routed kernels run on (SMs - shared_sms) SMs and the shared expert's kernels
    concurrently on shared_sms SMs (<= 0: VQ2_SHARED_SMS_DEFAULT) on a second stream this library
    creates per device, forked from and joined into `stream` with events (capturable in a CUDA
-   graph); both add into `out` with fp32 atomics after one zeroing, so the sum order is not fixed.
+   graph once the first call on the device, which creates that stream and its events, has run
+   outside capture); both add into `out` with fp32 atomics after one zeroing, so the sum order is not fixed.
    Workspace: vq2_decode_with_shared_workspace_size. No reference counterpart as one call: vLLM
    runs the shared expert beside the MoE method (reference vq2_vllm/__init__.py:197-198). */
 #define VQ2_SHARED_SMS_DEFAULT 56   /* best of a 12..110 sweep at config 1, batch 1 */
