@@ -78,3 +78,36 @@ def test_shared_expert_rejects_bad_arguments_without_a_gpu():
     assert L.vq2_shared_expert(fake, 0, fake + 2, fake, 1, 256, 256, fake, 0, fake, 1 << 20, None) == 3  # alignment
     assert L.vq2_shared_expert(fake, 0, fake, fake, 1, 256, 256, fake, 0, None, 0, None) == 5           # workspace
     assert L.vq2_shared_expert(None, 0, fake, fake, 1, 256, 256, fake, 0, fake, 1 << 20, None) == 1     # null
+
+
+def test_fused_ep_and_coscheduled_entries_reject_bad_arguments_without_a_gpu():
+    """vq2_ep_decode and vq2_decode_with_shared return their error codes before any CUDA call."""
+    import ctypes
+    from vq2_vllm import _lib
+    L = _lib.lib()
+    fake = 1 << 20
+    a = _lib.Vq2MoeArgs()
+    a.N, a.H, a.I, a.E, a.topk, a.x_dtype, a.ids_dtype = 1, 4096, 2048, 32, 8, 0, 0
+    a.x = a.topk_ids = a.topk_w = a.out = fake
+    a.w13_cb = a.w13_lo = a.w13_hi = a.w13_sc = a.w2_cb = a.w2_lo = a.w2_hi = a.w2_sc = fake
+    lay = _lib.Vq2EpLayout(0, 256, 512, 768, 1024, 1280, 1536, 1552)
+    ref, lref = ctypes.byref(a), ctypes.byref(lay)
+    assert L.vq2_ep_decode(None, fake, 2, 0, fake, lref, fake, 1 << 20, None) == 1            # null args
+    assert L.vq2_ep_decode(ref, fake, 0, 0, fake, lref, fake, 1 << 20, None) == 2             # world 0
+    assert L.vq2_ep_decode(ref, fake, 2, 2, fake, lref, fake, 1 << 20, None) == 2             # rank >= world
+    a.N = 2
+    assert L.vq2_ep_decode(ref, fake, 64, 0, fake, lref, fake, 1 << 20, None) == 6            # 64*2*8 > 512 pairs
+    a.N = 1
+    bad = _lib.Vq2EpLayout(0, 256, 512, 768, 1024, 1280, 1536, 1544)
+    assert L.vq2_ep_decode(ref, fake, 2, 0, fake, ctypes.byref(bad), fake, 1 << 20, None) == 3  # offset % 16
+    a.ids_dtype = 5
+    assert L.vq2_ep_decode(ref, fake, 2, 0, fake, lref, fake, 1 << 20, None) == 4             # dtype
+    a.ids_dtype = 0
+    assert L.vq2_decode_with_shared(None, fake, fake, 2048, 0, fake, 1 << 30, None) == 1     # null args
+    a.N = 9
+    assert L.vq2_decode_with_shared(ref, fake, fake, 2048, 0, fake, 1 << 30, None) == 2      # shared part N > 8
+    a.N = 1
+    assert L.vq2_decode_with_shared(ref, fake, fake, 2048, 0, None, 0, None) == 5            # workspace
+    assert L.vq2_decode_with_shared(ref, fake + 2, fake, 2048, 0, fake, 1 << 30, None) == 3  # alignment
+    assert L.vq2_decode_with_shared_workspace_size(1, 8, 4096, 2048, 2048) >= \
+        L.vq2_decode_workspace_size(1, 8, 4096, 2048) + L.vq2_shared_expert_workspace_size(1, 2048)
