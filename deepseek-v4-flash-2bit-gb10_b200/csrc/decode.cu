@@ -296,23 +296,20 @@ __device__ __forceinline__ void multi_dot(const uint4* lo, const uint32_t* hw, c
     for (int t = 0; t < NT; ++t) { a0[r][t] = __float2half2_rn(0.f); a1[r][t] = a0[r][t]; }
 #pragma unroll
   for (int q = 0; q < 4; ++q) {
-    // Each id comes out of one byte permute: its low byte from the lo word, its two high bits from
-    // a word holding the high-bit pairs of ids 0/2 (or 1/3) in bytes whose neighbours are zero.
+    // each id from one byte permute (ids_hi_pairs / id_of)
     uint32_t Lw[R], h02[R], h13[R];
 #pragma unroll
     for (int r = 0; r < R; ++r) {
       Lw[r] = q == 0 ? lo[r].x : q == 1 ? lo[r].y : q == 2 ? lo[r].z : lo[r].w;
-      const uint32_t hb = __byte_perm(hw[r], 0u, 0x4440 + q);
-      h02[r] = (hb * 0x1001u) & 0x00030003u;    // h0 -> byte 0, h2 -> byte 2
-      h13[r] = (hb * 0x40040u) & 0x03000300u;   // h1 -> byte 1, h3 -> byte 3
+      ids_hi_pairs(__byte_perm(hw[r], 0u, 0x4440 + q), h02[r], h13[r]);
     }
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
       const int s = 4 * q + j;
 #pragma unroll
       for (int r = 0; r < R; ++r) {
-        const uint32_t id = __byte_perm(Lw[r], (j & 1) ? h13[r] : h02[r],
-                                        j == 0 ? 0x5540 : j == 1 ? 0x4451 : j == 2 ? 0x5562 : 0x4473);
+        const uint32_t id = j == 0 ? id_of<0>(Lw[r], h02[r], h13[r]) : j == 1 ? id_of<1>(Lw[r], h02[r], h13[r])
+                          : j == 2 ? id_of<2>(Lw[r], h02[r], h13[r]) : id_of<3>(Lw[r], h02[r], h13[r]);
         const uint2 c = lds64(cbl + (id << CB_SHIFT));
         const __half2 c01 = *(const __half2*)&c.x, c23 = *(const __half2*)&c.y;
 #pragma unroll

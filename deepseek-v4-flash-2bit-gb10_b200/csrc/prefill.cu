@@ -164,11 +164,12 @@ __device__ __forceinline__ void decode8_fp8_f32cb(uint32_t cbl, uint2 lo, uint32
 // C[id] * sc in fp16.
 __device__ __forceinline__ void decode4_f16(uint32_t cbl, uint32_t lo, uint32_t hw, unsigned short sb, uint32_t* v) {
   const __half2 s2 = __half2half2(__ushort_as_half(sb));
-  uint32_t ids[2];
-  unpack_ids4(lo, hw & 0xFFu, ids[0], ids[1]);
+  uint32_t h02, h13;
+  ids_hi_pairs(hw & 0xFFu, h02, h13);
 #pragma unroll
   for (int j = 0; j < 4; ++j) {
-    const uint32_t id = (j & 2) ? (ids[j & 1] >> 16) : (ids[j & 1] & 0xFFFFu);
+    const uint32_t id = j == 0 ? id_of<0>(lo, h02, h13) : j == 1 ? id_of<1>(lo, h02, h13)
+                      : j == 2 ? id_of<2>(lo, h02, h13) : id_of<3>(lo, h02, h13);
     const uint2 c = lds64(cbl + (id << 7));
     const __half2 a0 = __hmul2(*(const __half2*)&c.x, s2), a1 = __hmul2(*(const __half2*)&c.y, s2);
     v[2 * j] = *(const uint32_t*)&a0;

@@ -210,6 +210,18 @@ __device__ __forceinline__ void unpack_ids4(uint32_t lo_word, uint32_t hb, uint3
   ids13 = e13 | ((hb * 0x00040040u) & 0x03000300u);         // hb bits 2-3 -> 8-9, bits 6-7 -> 24-25
 }
 
+// The same four ids, each from one byte permute: ids_hi_pairs() spreads the hi byte (8 bits, two
+// per id) into two words whose other bytes are zero — h02 = [h0, 0, h2, 0], h13 = [0, h1, 0, h3] —
+// and id_of<j>() puts id j's low byte (from the lo word) and its high bits side by side.
+__device__ __forceinline__ void ids_hi_pairs(uint32_t hb, uint32_t& h02, uint32_t& h13) {
+  h02 = (hb * 0x1001u) & 0x00030003u;    // hb bits 0-1 -> byte 0, bits 4-5 -> byte 2
+  h13 = (hb * 0x40040u) & 0x03000300u;   // hb bits 2-3 -> byte 1, bits 6-7 -> byte 3
+}
+template <int J>
+__device__ __forceinline__ uint32_t id_of(uint32_t lo_word, uint32_t h02, uint32_t h13) {
+  return __byte_perm(lo_word, (J & 1) ? h13 : h02, J == 0 ? 0x5540 : J == 1 ? 0x4451 : J == 2 ? 0x5562 : 0x4473);
+}
+
 // Streaming-multiprocessor count of the current device, looked up once per device (grids of the
 // grid-stride kernels are sized from it). Returns 0 if the query fails.
 inline int device_sm_count() {
@@ -219,13 +231,6 @@ inline int device_sm_count() {
   if (!counts[dev] && cudaDeviceGetAttribute(&counts[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     counts[dev] = 0;
   return counts[dev];
-}
-
-// Like unpack_ids4, but the ids come out multiplied by 64 (a byte offset into a table of 64-byte
-// entries): o02 = 64*id0 | 64*id2 << 16, o13 = 64*id1 | 64*id3 << 16 (64 * 1023 fits 16 bits).
-__device__ __forceinline__ void unpack_off4_x64(uint32_t lo_word, uint32_t hb, uint32_t& o02, uint32_t& o13) {
-  o02 = (__byte_perm(lo_word, 0u, 0x4240) << 6) | ((hb * 0x04004000u) & 0xC000C000u);   // hb bits 0-1 -> 14-15, 4-5 -> 30-31
-  o13 = (__byte_perm(lo_word, 0u, 0x4341) << 6) | ((hb * 0x01001000u) & 0xC000C000u);   // hb bits 2-3 -> 14-15, 6-7 -> 30-31
 }
 
 // Packed fp32 multiply of two pairs (Blackwell mul.rn.f32x2: each half rounded on its own).
