@@ -183,9 +183,28 @@ int launch_align_ex(const void* ids, int dt, long N, int k, int E, int BM, int b
   int threads = ALIGN_THREADS;
   while ((size_t)(threads / 32) * E * sizeof(int) > 96 * 1024 && threads > 128) threads /= 2;
   const size_t wc = (size_t)(threads / 32) * E * sizeof(int);
-  if (cudaFuncSetAttribute(align_single_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wc) != cudaSuccess ||
-      cudaFuncSetAttribute(align_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)wc) != cudaSuccess)
-    return VQ2_ERR_CUDA;
+  // The kernels' dynamic shared-memory limit is raised once per device, to what the device's
+  // opt-in maximum leaves beside their static arrays, not per call to this call's size: a per-call
+  // value could be lowered by a concurrent call with a smaller E between another call's set and
+  // its launch, or under a captured graph.
+  static int limit_set[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return VQ2_ERR_CUDA;
+  if (!limit_set[dev]) {
+    int optin = 0;
+    cudaFuncAttributes fs, fp;
+    if (cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess ||
+        cudaFuncGetAttributes(&fs, align_single_kernel) != cudaSuccess ||
+        cudaFuncGetAttributes(&fp, align_place_kernel) != cudaSuccess)
+      return VQ2_ERR_CUDA;
+    const int lim = optin - (int)max(fs.sharedSizeBytes, fp.sharedSizeBytes);
+    if (lim <= 0 ||
+        cudaFuncSetAttribute(align_single_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, lim) != cudaSuccess ||
+        cudaFuncSetAttribute(align_place_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, lim) != cudaSuccess)
+      return VQ2_ERR_CUDA;
+    limit_set[dev] = lim;
+  }
+  if (wc > (size_t)limit_set[dev]) return VQ2_ERR_SHAPE;
   if (a.nchunks <= 1) {
     align_single_kernel<<<1, threads, wc, stream>>>(a);
   } else {
