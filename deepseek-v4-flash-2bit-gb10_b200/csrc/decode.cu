@@ -391,8 +391,11 @@ __device__ __forceinline__ void stage_rotate(int ng, DecodeShared* sh, const flo
   const float climit = 1024.f / sh->cmax;
 #pragma unroll
   for (int i = 0; i < GPW; ++i) {
+    // straight-line over the warp's groups (a group past ng rotates zeros and stores nothing), so
+    // the groups' shuffle chains interleave
     const int g = warp + i * DEC_NW;
-    if (g < ng) {
+    const bool gok = g < ng;
+    {
       float a = va[i], b = vb[i];
       const float t = a + b;
       b = a - b;
@@ -415,12 +418,12 @@ __device__ __forceinline__ void stage_rotate(int ng, DecodeShared* sh, const flo
       }
       const float ea = a * sc, eb = b * sc;
       const float na = __shfl_down_sync(0xffffffffu, ea, 1), nb = __shfl_down_sync(0xffffffffu, eb, 1);
-      if (!(lane & 1)) {                          // element pairs (2j, 2j+1) -> half2 j
+      if (gok && !(lane & 1)) {                   // element pairs (2j, 2j+1) -> half2 j
         __half2 h0 = __floats2half2_rn(ea, na), h1 = __floats2half2_rn(eb, nb);
         sh->xs[g][lane >> 1] = *(uint32_t*)&h0;
         sh->xs[g][16 + (lane >> 1)] = *(uint32_t*)&h1;
       }
-      if (lane == 0) sh->ginv[g] = inv * 0.125f;
+      if (gok && lane == 0) sh->ginv[g] = inv * 0.125f;
     }
   }
   consumer_sync();
