@@ -618,15 +618,25 @@ __device__ __forceinline__ void gateup_pre(const vq2_moe_args& a, const DecSmem&
   const ChunkIter it0((long)sh->nunits * a.I, a.I, DEC_SA);
   if (it0.left > 0) {
     pre.m = sh->unit_m[it0.u][0];
-    const size_t xrow = (size_t)(pre.m / a.topk) * a.H;
-    const void* xp = a.x;
-    const int xdt = a.x_dtype;
-    stage_load([&](int i) { return load_act(xp, xdt, xrow + i); }, a.H / 64, pre.va, pre.vb);
+    if (a.N != 1) {   // (one token: its row was loaded before the plan, gateup_load_single)
+      const size_t xrow = (size_t)(pre.m / a.topk) * a.H;
+      const void* xp = a.x;
+      const int xdt = a.x_dtype;
+      stage_load([&](int i) { return load_act(xp, xdt, xrow + i); }, a.H / 64, pre.va, pre.vb);
+    }
   }
   if (!zero_out) return;
   const long tot = (long)a.N * a.H;
   for (long i = (long)blockIdx.x * DEC_NW * 32 + threadIdx.x; i < tot; i += (long)gridDim.x * DEC_NW * 32)
     a.out[i] = 0.f;
+}
+
+// Consumers, one token (N == 1): its row is the first unit's activation whatever the plan says, so
+// it is loaded before the plan is built (the two loads' latencies overlap).
+__device__ __forceinline__ void gateup_load_single(const vq2_moe_args& a, GateupPre& pre) {
+  const void* xp = a.x;
+  const int xdt = a.x_dtype;
+  stage_load([&](int i) { return load_act(xp, xdt, (size_t)i); }, a.H / 64, pre.va, pre.vb);
 }
 
 // Consumers: gate/up K-slice partials of this CTA's rows into `part`. KH = K-slices of the
@@ -794,6 +804,8 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part, DecEp ep) {
   else pdl_wait();
   // dependents (the down kernel) may launch now: everything this grid waited for is complete
   pdl_launch_dependents();
+  GateupPre pre;
+  if (a.N == 1 && threadIdx.x >> 5 < DEC_NW) gateup_load_single(a, pre);
   build_plan(a.topk_ids, a.ids_dtype, a.topk_w, a.N * a.topk, a.E, a.expert_base, d.sh);
   int c = 0;
   if (threadIdx.x >> 5 == DEC_NW) {   // producer warp
@@ -803,7 +815,6 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part, DecEp ep) {
     }
     return;
   }
-  GateupPre pre;
   gateup_pre(a, d, pre, ep.world == 0 && !ep.keep_out);
   fill_codebook(d.cbs, d.sh);         // overlaps the activation loads of gateup_pre
   gateup_consume<KH>(a, d, part, pre, c);
