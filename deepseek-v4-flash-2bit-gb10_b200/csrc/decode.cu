@@ -790,12 +790,13 @@ __global__ void __launch_bounds__(DEC_THREADS, 1)
 decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part, DecEp ep) {
   extern __shared__ __align__(128) uint8_t smem[];
   const DecSmem d = dec_smem(smem);
-  // Launched with programmatic dependent launch: the CTA becomes resident and issues the
-  // codebook copy (a constant weight) while the previous kernel drains. Everything after
-  // pdl_wait() reads the call's inputs or writes the workspace and output, which the previous
-  // kernel may still be using. (Replicating the codebook before the wait was measured slower:
-  // it then no longer hides the activation loads below.)
+  // Launched with programmatic dependent launch: the CTA becomes resident, copies the codebook (a
+  // constant weight) and replicates it in shared memory while the previous kernel drains.
+  // Everything after pdl_wait() reads the call's inputs or writes the workspace and output, which
+  // the previous kernel may still be using.
   dec_init(a.w13_cb, d);
+  __syncthreads();                              // the barriers are initialised
+  if (threadIdx.x >> 5 < DEC_NW) fill_codebook(d.cbs, d.sh);
   // expert parallelism: every rank's rows, ids and weights must have arrived (the plan reads them;
   // their flags order them, and the push kernel ahead starts only after the previous step's
   // finish kernel, which waited for every rank's down kernel, so no grid-dependency wait is
@@ -816,7 +817,6 @@ decode_gateup_kernel(vq2_moe_args a, float* __restrict__ part, DecEp ep) {
     return;
   }
   gateup_pre(a, d, pre, ep.world == 0 && !ep.keep_out);
-  fill_codebook(d.cbs, d.sh);         // overlaps the activation loads of gateup_pre
   gateup_consume<KH>(a, d, part, pre, c);
 }
 
@@ -827,7 +827,7 @@ decode_down_kernel(vq2_moe_args a, const float* __restrict__ part, int khA, DecE
   extern __shared__ __align__(128) uint8_t smem[];
   const DecSmem d = dec_smem(smem);
   // the next call's gate/up kernel may launch now: before its own grid-dependency wait it only
-  // initialises barriers and copies its codebook into its shared memory
+  // initialises barriers, copies its codebook and replicates it in its shared memory
   pdl_launch_dependents();
   // expert parallelism: the gathered ids the plan reads were written by the peers (their arrival
   // flags are set by now; the acquire makes the data visible to this CTA)
