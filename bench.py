@@ -107,7 +107,7 @@ def cpu_model():
 # DRAM bytes (read + write) per distinct expert of one decode layer call, from the ncu capture in
 # profiles/decode_config1_b1.txt (69.97 MB over 8 distinct experts, both kernels), so the roofline
 # line scales it to its own run's distinct-expert count.
-NCU_DECODE_BYTES_PER_EXPERT = 69.685e6 / 8
+NCU_DECODE_BYTES_PER_EXPERT = 70.03e6 / 8
 
 
 def make_routing(x, seed):
