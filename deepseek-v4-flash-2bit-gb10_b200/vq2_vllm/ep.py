@@ -445,36 +445,43 @@ def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
         for i in range(warmup):
             step(i)
         torch.cuda.synchronize()
+        block = 1                              # steps per launch unit
         if gather:
-            # the gather-mode step has no host read: replay it from CUDA graphs, one per input set
+            # the gather-mode step has no host read: the timed steps are captured as one CUDA
+            # graph of consecutive steps (input sets and layers in turn, as a model's decode graph
+            # holds its layers), so the kernels keep their programmatic-launch overlap across step
+            # boundaries; exactly `steps` steps per replay (up to 64, else one graph per step)
             try:
-                gs = []
+                block = steps if steps <= 64 else 1
                 torch.cuda.synchronize()
-                for j in range(8):
-                    g = torch.cuda.CUDAGraph()
-                    with torch.cuda.graph(g):
+                gk = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(gk):
+                    for j in range(block):
                         step(j)
-                    gs.append(g)
+                torch.cuda.synchronize()
+                gk.replay()                    # untimed: the graph's first launch
                 torch.cuda.synchronize()
                 dist.barrier()
-                step = lambda i: gs[i % 8].replay()
+                step = lambda i: gk.replay()
                 if not collective_only:
-                    graphs_used[per_rank] = True
+                    graphs_used[per_rank] = f"one graph of {block} steps"
             except Exception as ex:            # fall back to eager launches
+                block = 1
                 if not collective_only:
                     graphs_used[per_rank] = f"eager ({type(ex).__name__})"
                 torch.cuda.synchronize()
+        nunits = steps // block
         torch.cuda.synchronize()
         dist.barrier()
         torch.cuda.synchronize()
         s, e = torch.cuda.Event(True), torch.cuda.Event(True)
         torch.cuda._sleep(5_000_000)          # every rank queues its steps ahead of its GPU, so the
         s.record()                            # timed region sees device time, not launch gaps
-        for i in range(steps):
+        for i in range(nunits):
             step(i)
         e.record()
         e.synchronize()
-        ms = torch.tensor([s.elapsed_time(e) / steps], device=dev)
+        ms = torch.tensor([s.elapsed_time(e) / (nunits * block)], device=dev)
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         dist.barrier()
         return ms.item()
