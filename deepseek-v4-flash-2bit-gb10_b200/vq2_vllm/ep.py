@@ -450,21 +450,28 @@ def bench_ep(args, rank, world, metric, clocks_cls=None, peaks_fn=None):
             # the gather-mode step has no host read: the timed steps are captured as one CUDA
             # graph of consecutive steps (input sets and layers in turn, as a model's decode graph
             # holds its layers), so the kernels keep their programmatic-launch overlap across step
-            # boundaries; exactly `steps` steps per replay (up to 64, else one graph per step)
+            # boundaries. A graph holds `steps` steps (up to 64) or the largest divisor of `steps`
+            # in [8, 64], replayed steps / block times; without one, eight one-step graphs (one per
+            # input set and layer) replayed in turn. Exactly `steps` steps are timed.
             try:
-                block = steps if steps <= 64 else 1
+                block = steps if steps <= 64 else max([b for b in range(8, 65) if steps % b == 0], default=1)
                 torch.cuda.synchronize()
-                gk = torch.cuda.CUDAGraph()
-                with torch.cuda.graph(gk):
-                    for j in range(block):
-                        step(j)
+                gks = []
+                for gi in range(1 if block > 1 else 8):
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g):
+                        for j in range(block):
+                            step(gi + j)
+                    gks.append(g)
                 torch.cuda.synchronize()
-                gk.replay()                    # untimed: the graph's first launch
+                for g in gks:
+                    g.replay()                 # untimed: each graph's first launch
                 torch.cuda.synchronize()
                 dist.barrier()
-                step = lambda i: gk.replay()
+                step = lambda i: gks[i % len(gks)].replay()
                 if not collective_only:
-                    graphs_used[per_rank] = f"one graph of {block} steps"
+                    graphs_used[per_rank] = (f"one graph of {block} steps" if block > 1
+                                             else "one graph per step, 8 cycled")
             except Exception as ex:            # fall back to eager launches
                 block = 1
                 if not collective_only:
