@@ -700,6 +700,7 @@ __global__ void __launch_bounds__(256) had_quant_rows_kernel(const void* __restr
                                                              uint8_t* __restrict__ out, float* __restrict__ inv,
                                                              const int32_t* __restrict__ pslot, int k) {
   __shared__ float red[33];
+  __shared__ __align__(16) uint8_t qrow[4096 * 2];   // one quantised row (cols <= 4096, up to 2 bytes each)
   const long row = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int ng = cols / 64;
@@ -746,6 +747,22 @@ __global__ void __launch_bounds__(256) had_quant_rows_kernel(const void* __restr
     }
   }
   const float is = 1.0f / s;
+  // the quantised row once into shared memory, then 16-byte stores of it to every destination
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int g = warp + 8 * i;
+    if (g < ng) {
+      if (PREC == VQ2_PREC_FP8) {
+        qrow[g * 64 + lane] = (uint8_t)__nv_cvt_float_to_fp8(va[i] * s, __NV_SATFINITE, __NV_E4M3);
+        qrow[g * 64 + 32 + lane] = (uint8_t)__nv_cvt_float_to_fp8(vb[i] * s, __NV_SATFINITE, __NV_E4M3);
+      } else {
+        ((__half*)qrow)[g * 64 + lane] = __float2half_rn(va[i] * s);
+        ((__half*)qrow)[g * 64 + 32 + lane] = __float2half_rn(vb[i] * s);
+      }
+    }
+  }
+  __syncthreads();
+  const int n16 = cols * elem / 16;             // cols is a multiple of 64: whole 16-byte words
   const int ndst = pslot ? k : 1;
   for (int jd = 0; jd < ndst; ++jd) {
     long dst = row;
@@ -753,21 +770,9 @@ __global__ void __launch_bounds__(256) had_quant_rows_kernel(const void* __restr
       dst = pslot[row * k + jd];
       if (dst < 0) continue;                    // pair owned by another device
     }
-    uint8_t* orow_d = out + dst * (size_t)cols * elem;
+    uint4* orow_d = (uint4*)(out + dst * (size_t)cols * elem);
     if (threadIdx.x == 0) inv[dst] = is;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const int g = warp + 8 * i;
-      if (g < ng) {
-        if (PREC == VQ2_PREC_FP8) {
-          orow_d[g * 64 + lane] = (uint8_t)__nv_cvt_float_to_fp8(va[i] * s, __NV_SATFINITE, __NV_E4M3);
-          orow_d[g * 64 + 32 + lane] = (uint8_t)__nv_cvt_float_to_fp8(vb[i] * s, __NV_SATFINITE, __NV_E4M3);
-        } else {
-          ((__half*)orow_d)[g * 64 + lane] = __float2half_rn(va[i] * s);
-          ((__half*)orow_d)[g * 64 + 32 + lane] = __float2half_rn(vb[i] * s);
-        }
-      }
-    }
+    for (int c = threadIdx.x; c < n16; c += blockDim.x) orow_d[c] = ((const uint4*)qrow)[c];
   }
 }
 
